@@ -1,0 +1,140 @@
+/*
+ * ska_b200.h -- C ABI of the B200 (sm_100a) Spectral Koopman Attention core.
+ *
+ * The "SKA core" is the part of the reference SKAModule.forward between the
+ * key/query/value projections and the eta/out_proj epilogue:
+ *
+ *     (z, zq, v, ssn_gamma) -> y_hat            forward
+ *     (dy_hat, ...)         -> dz, dzq, dv, dgamma   backward
+ *
+ * Reference interface replaced (paths relative to the upstream project root,
+ * KLF = koopman-lm-fast):
+ *   - KLF/koopman_lm/ska.py:432-457   fp32 upcast, max-key-norm scaling, chunk
+ *                                      statistics, Cholesky, post-Cholesky chain
+ *   - KLF/koopman_lm/ska.py:73-151    _compute_chunk_stats_and_cholesky
+ *   - KLF/koopman_lm/ska.py:158-187   _post_cholesky_pytorch
+ *   - KLF/koopman_lm/ska.py:263-330   _post_cholesky_triton (+ its kernel 196-260)
+ *   - KLF/koopman_lm/adaptive_chunking.py:171-256  compute_chunk_stats_decay
+ *   - the PyTorch autograd backward of all of the above (the reference has no
+ *     hand-written backward).
+ *
+ * Conventions
+ *   - Every tensor is [B, T, H, D] with the last (feature) dimension
+ *     contiguous; the three other strides are given in ELEMENTS and may be
+ *     arbitrary (e.g. column slices of one fused projection output).
+ *   - io_dtype selects the element type of z, zq, v, y, dy, dz, dzq, dv:
+ *     SKA_DTYPE_F32 or SKA_DTYPE_BF16.  All arithmetic is fp32 (the reference
+ *     upcasts with .float(), ska.py:436-438).
+ *   - gamma / dgamma are device pointers to one fp32 scalar; dgamma is
+ *     OVERWRITTEN (not accumulated).
+ *   - The caller owns all memory.  ska_fwd writes a "saved" buffer that
+ *     ska_bwd reads; ska_bwd also needs a scratch buffer.  Their sizes come
+ *     from ska_workspace_size.  The library never allocates, never frees and
+ *     never synchronises the host; work is enqueued on `stream`
+ *     (a cudaStream_t, NULL = legacy default stream).
+ *   - Return value: 0 on success, a negative SKA_ERR_* code otherwise (no
+ *     work is enqueued on error).  A Cholesky failure is not an error: as in
+ *     the reference (ska.py:140-145), a slice whose factorisation fails is
+ *     refactored with 1e-4 added to the diagonal.
+ */
+#ifndef SKA_B200_H
+#define SKA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SKA_ABI_VERSION 1
+
+enum {
+  SKA_DTYPE_F32 = 0,
+  SKA_DTYPE_BF16 = 1,
+};
+
+enum {
+  SKA_STRATEGY_STANDARD = 0, /* ska.py:114-133                       */
+  SKA_STRATEGY_DECAY = 1,    /* adaptive_chunking.py:213-238         */
+};
+
+enum {
+  SKA_OK = 0,
+  SKA_ERR_NULL = -1,        /* a required pointer is NULL                          */
+  SKA_ERR_SHAPE = -2,       /* B<0, T<1, H<1, r<1, P<1, chunk<1, power_K<0 ...      */
+  SKA_ERR_UNSUPPORTED = -3, /* r > 64, P > 128, chunk > 256, power_K > 8            */
+  SKA_ERR_DTYPE = -4,       /* unknown io_dtype                                     */
+  SKA_ERR_WORKSPACE = -5,   /* saved / scratch buffer too small                    */
+  SKA_ERR_ALIGN = -6,       /* misaligned pointer or stride                        */
+  SKA_ERR_LAUNCH = -7,      /* a kernel launch failed (cudaGetLastError)           */
+  SKA_ERR_STRATEGY = -8,    /* unknown strategy, or decay_alpha not finite         */
+};
+
+/* Static problem description (constructor arguments of the reference
+ * SKAModule, ska.py:368-371, plus the activation shape). */
+typedef struct SkaShape {
+  int64_t B;          /* batch                                              */
+  int64_t T;          /* sequence length (any T >= 1; the tail is padded)   */
+  int64_t H;          /* heads                                              */
+  int64_t r;          /* Koopman rank (key/query dim per head), 1..64       */
+  int64_t P;          /* value dim per head, 1..128                         */
+  int64_t chunk_size; /* CS, 1..256                                         */
+  int32_t power_K;    /* filter power, 0..8                                 */
+  int32_t strategy;   /* SKA_STRATEGY_*                                     */
+  float ridge_eps;    /* ridge added to the Gram diagonal                   */
+  float decay_alpha;  /* decay strategy only                                */
+} SkaShape;
+
+/* One [B, T, H, D] tensor: data pointer + element strides (feature stride 1). */
+typedef struct SkaTensor {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_t;
+  int64_t stride_h;
+} SkaTensor;
+
+/* ABI version (SKA_ABI_VERSION of the built library). */
+int ska_abi_version(void);
+
+/* Static string for a return code. */
+const char* ska_status_string(int code);
+
+/* Bytes needed for the forward's saved buffer (read by ska_bwd) and for the
+ * backward's scratch buffer.  Either output pointer may be NULL. */
+int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scratch_bytes);
+
+/* Forward.  Replaces ska.py:436-457 between the projections and eta:
+ *   y = SKA_core(z, zq, v; ssn_gamma)   (y in io_dtype, [B,T,H,P]).
+ * `saved` must hold ska_workspace_size(...).saved_bytes; its contents are
+ * consumed by ska_bwd for the same inputs. */
+int ska_fwd(const SkaShape* shape, int io_dtype,
+            const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+            const float* gamma, const SkaTensor* y,
+            void* saved, size_t saved_bytes, void* stream);
+
+/* Backward of ska_fwd (what PyTorch autograd computes for the reference's
+ * PyTorch backend): given dy, writes dz, dzq, dv (io_dtype) and *dgamma (fp32,
+ * overwritten).  z, zq, v, gamma and `saved` must be those of the forward. */
+int ska_bwd(const SkaShape* shape, int io_dtype,
+            const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+            const float* gamma, const SkaTensor* dy,
+            const void* saved, size_t saved_bytes,
+            void* scratch, size_t scratch_bytes,
+            const SkaTensor* dz, const SkaTensor* dzq, const SkaTensor* dv,
+            float* dgamma, void* stream);
+
+/* Profiling hook (process-wide, not thread-safe; no counterpart in the
+ * reference, which has no per-kernel timing).  With `events` non-NULL and
+ * count >= SKA_PROFILE_EVENTS, every later ska_fwd records events[0] on its
+ * stream before its first kernel and events[i] after its i-th kernel
+ * (i = 1..3); ska_bwd does the same with events[4..7].  The handles are
+ * cudaEvent_t values created by the caller.  NULL disables recording. */
+#define SKA_PROFILE_EVENTS 8
+int ska_set_profile_events(void* const* events, int count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SKA_B200_H */

@@ -1,0 +1,205 @@
+// ska_capi.cu -- extern "C" entry points of libska_b200.so (declared in
+// include/ska_b200.h): argument validation, workspace layout, dispatch.
+#include "../../include/ska_b200.h"
+#include "ska_common.cuh"
+
+#include <cmath>
+
+namespace ska {
+template <typename T>
+cudaError_t launch_fwd(const Dims&, const In&, const In&, const In&, const float*, const Out&,
+                       const SavedLayout&, char*, cudaStream_t);
+template <typename T>
+cudaError_t launch_bwd(const Dims&, const In&, const In&, const In&, const float*, const In&,
+                       const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&, const Out&,
+                       const Out&, float*, cudaStream_t);
+size_t smem_fwd_stats(const Dims&);
+size_t smem_fwd_chunk(const Dims&);
+size_t smem_bwd_chunk(const Dims&);
+size_t smem_bwd_tok(const Dims&);
+}  // namespace ska
+
+namespace {
+
+using ska::Dims;
+
+int make_dims(const SkaShape* s, Dims* d) {
+  if (!s) return SKA_ERR_NULL;
+  if (s->B < 0 || s->T < 1 || s->H < 1 || s->r < 1 || s->P < 1 || s->chunk_size < 1 || s->power_K < 0)
+    return SKA_ERR_SHAPE;
+  if (s->r > ska::kMaxRank || s->P > ska::kMaxP || s->chunk_size > ska::kMaxChunk ||
+      s->power_K > ska::kMaxPowerK)
+    return SKA_ERR_UNSUPPORTED;
+  const long long C = (s->T + s->chunk_size - 1) / s->chunk_size;
+  // grid limits: (C, H, B) and (SW/256, B*H)
+  if (s->H > 65535 || s->B > 65535 || s->B * s->H > 65535 || C > 0x7fffffffLL || s->T > 0x7fffffffLL)
+    return SKA_ERR_UNSUPPORTED;
+  if (s->strategy != SKA_STRATEGY_STANDARD && s->strategy != SKA_STRATEGY_DECAY) return SKA_ERR_STRATEGY;
+  if (s->strategy == SKA_STRATEGY_DECAY && !std::isfinite(s->decay_alpha)) return SKA_ERR_STRATEGY;
+  d->B = (int)s->B;
+  d->T = (int)s->T;
+  d->H = (int)s->H;
+  d->r = (int)s->r;
+  d->P = (int)s->P;
+  d->CS = (int)s->chunk_size;
+  d->C = (int)C;
+  d->K = s->power_K;
+  d->decay = s->strategy == SKA_STRATEGY_DECAY ? 1 : 0;
+  d->ridge = s->ridge_eps;
+  d->alpha = d->decay ? s->decay_alpha : 1.f;
+  d->SW = 2 * d->r * d->r + d->P * d->r;
+  // every kernel's shared-memory tile set must fit one sm_100a CTA (227 KB opt-in)
+  const size_t kMaxSmem = 232448;
+  if (ska::smem_fwd_stats(*d) > kMaxSmem || ska::smem_fwd_chunk(*d) > kMaxSmem ||
+      ska::smem_bwd_chunk(*d) > kMaxSmem || ska::smem_bwd_tok(*d) > kMaxSmem)
+    return SKA_ERR_UNSUPPORTED;
+  return SKA_OK;
+}
+
+int elem_size(int dtype) {
+  switch (dtype) {
+    case SKA_DTYPE_F32: return 4;
+    case SKA_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+int check_tensor(const SkaTensor* t, int esize, bool needed, ska::In* out) {
+  if (!t) return SKA_ERR_NULL;
+  if (needed && !t->data) return SKA_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(t->data) % (uintptr_t)esize) return SKA_ERR_ALIGN;
+  out->p = t->data;
+  out->sb = t->stride_b;
+  out->st = t->stride_t;
+  out->sh = t->stride_h;
+  return SKA_OK;
+}
+
+int check_out(const SkaTensor* t, int esize, bool needed, ska::Out* out) {
+  ska::In tmp{};
+  const int rc = check_tensor(t, esize, needed, &tmp);
+  if (rc) return rc;
+  out->p = t->data;
+  out->sb = t->stride_b;
+  out->st = t->stride_t;
+  out->sh = t->stride_h;
+  return SKA_OK;
+}
+
+}  // namespace
+
+namespace ska {
+ProfileEvents* profile_events() {
+  static ProfileEvents p{};
+  return &p;
+}
+}  // namespace ska
+
+extern "C" {
+
+int ska_abi_version(void) { return SKA_ABI_VERSION; }
+
+int ska_set_profile_events(void* const* events, int count) {
+  ska::ProfileEvents* p = ska::profile_events();
+  if (!events) {
+    p->on = false;
+    return SKA_OK;
+  }
+  if (count < SKA_PROFILE_EVENTS) return SKA_ERR_SHAPE;
+  for (int i = 0; i < SKA_PROFILE_EVENTS; ++i) {
+    if (!events[i]) return SKA_ERR_NULL;
+    p->ev[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  p->on = true;
+  return SKA_OK;
+}
+
+const char* ska_status_string(int code) {
+  switch (code) {
+    case SKA_OK: return "ok";
+    case SKA_ERR_NULL: return "a required pointer is NULL";
+    case SKA_ERR_SHAPE: return "invalid shape (need B>=0, T>=1, H>=1, r>=1, P>=1, chunk_size>=1, power_K>=0)";
+    case SKA_ERR_UNSUPPORTED: return "unsupported size (r<=64, P<=128, chunk_size<=256, power_K<=8, B*H<=65535)";
+    case SKA_ERR_DTYPE: return "unknown io dtype";
+    case SKA_ERR_WORKSPACE: return "saved or scratch buffer too small";
+    case SKA_ERR_ALIGN: return "misaligned pointer";
+    case SKA_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case SKA_ERR_STRATEGY: return "unknown chunk strategy or non-finite decay_alpha";
+    default: return "unknown status";
+  }
+}
+
+int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scratch_bytes) {
+  Dims d{};
+  const int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (saved_bytes) *saved_bytes = ska::saved_layout(d.B, d.H, d.C, d.SW).total;
+  if (scratch_bytes) *scratch_bytes = ska::scratch_layout(d.B, d.H, d.C, d.SW).total;
+  return SKA_OK;
+}
+
+int ska_fwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+            const float* gamma, const SkaTensor* y, void* saved, size_t saved_bytes, void* stream) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  const int es = elem_size(io_dtype);
+  if (!es) return SKA_ERR_DTYPE;
+  const bool work = d.B > 0;
+  ska::In iz{}, izq{}, iv{};
+  ska::Out oy{};
+  if ((rc = check_tensor(z, es, work, &iz)) || (rc = check_tensor(zq, es, work, &izq)) ||
+      (rc = check_tensor(v, es, work, &iv)) || (rc = check_out(y, es, work, &oy)))
+    return rc;
+  if (!work) return SKA_OK;
+  if (!gamma || !saved) return SKA_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
+  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW);
+  if (saved_bytes < L.total) return SKA_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (io_dtype == SKA_DTYPE_F32)
+    e = ska::launch_fwd<float>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st);
+  else
+    e = ska::launch_fwd<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st);
+  return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
+}
+
+int ska_bwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+            const float* gamma, const SkaTensor* dy, const void* saved, size_t saved_bytes, void* scratch,
+            size_t scratch_bytes, const SkaTensor* dz, const SkaTensor* dzq, const SkaTensor* dv, float* dgamma,
+            void* stream) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  const int es = elem_size(io_dtype);
+  if (!es) return SKA_ERR_DTYPE;
+  const bool work = d.B > 0;
+  ska::In iz{}, izq{}, iv{}, idy{};
+  ska::Out odz{}, odzq{}, odv{};
+  if ((rc = check_tensor(z, es, work, &iz)) || (rc = check_tensor(zq, es, work, &izq)) ||
+      (rc = check_tensor(v, es, work, &iv)) || (rc = check_tensor(dy, es, work, &idy)) ||
+      (rc = check_out(dz, es, work, &odz)) || (rc = check_out(dzq, es, work, &odzq)) ||
+      (rc = check_out(dv, es, work, &odv)))
+    return rc;
+  if (!dgamma) return SKA_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!work) {
+    return cudaMemsetAsync(dgamma, 0, sizeof(float), st) == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
+  }
+  if (!gamma || !saved || !scratch) return SKA_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(saved) % 256 || reinterpret_cast<uintptr_t>(scratch) % 256) return SKA_ERR_ALIGN;
+  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW);
+  const ska::ScratchLayout S = ska::scratch_layout(d.B, d.H, d.C, d.SW);
+  if (saved_bytes < L.total || scratch_bytes < S.total) return SKA_ERR_WORKSPACE;
+  cudaError_t e;
+  if (io_dtype == SKA_DTYPE_F32)
+    e = ska::launch_bwd<float>(d, iz, izq, iv, gamma, idy, L, static_cast<const char*>(saved), S,
+                               static_cast<char*>(scratch), odz, odzq, odv, dgamma, st);
+  else
+    e = ska::launch_bwd<__nv_bfloat16>(d, iz, izq, iv, gamma, idy, L, static_cast<const char*>(saved), S,
+                                       static_cast<char*>(scratch), odz, odzq, odv, dgamma, st);
+  return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
+}
+
+}  // extern "C"

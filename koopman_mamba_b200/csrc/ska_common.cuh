@@ -1,0 +1,159 @@
+// ska_common.cuh -- shared definitions of the SKA core kernels (sm_100a).
+//
+// Data model (one (batch b, head h) "series" of T tokens, split into
+// C = ceil(T / CS) chunks of CS tokens; the tail chunk is zero padded as in
+// KLF/koopman_lm/ska.py:87-94):
+//
+//   raw chunk statistics of chunk c (unnormalised keys z, values v):
+//     G'_c = sum_{t in c} z_t z_t^T                          r x r
+//     M'_c = sum_{t in c} z_{t+1} z_t^T                      r x r
+//            (the transition that leaves chunk c is owned by chunk c, which
+//             folds the reference's boundary term ska.py:108-111,125-129
+//             into the ordinary exclusive scan)
+//     C'_c = sum_{t in c} v_t z_t^T                          P x r
+//   exclusive (decayed) scan over chunks:  X_excl[c] = a * X_excl[c-1] + X'[c-1]
+//   (a = 1 for the standard strategy, ska.py:114-133; a = decay_alpha for the
+//    decay strategy, adaptive_chunking.py:225-238).
+//
+//   The shared key norm m = max_t ||z_t|| (ska.py:441) enters only as scalars:
+//   Gn = G_excl / m^2 + ridge I,  Mn = M_excl / m^2,  Cn = C_excl / m,
+//   Qn = zq / m.  Raw statistics are therefore computed once and scaled.
+//
+//   Per chunk operator (L = chol(Gn), Li = L^{-1}, S = Li^T Li = Gn^{-1}):
+//     A0 = Mn S,  A = clamp(gamma,1,1.5) / max(sigma(A0),1) * A0
+//     W  = Cn Li^T A^K Li                                    P x r
+//     y_t = W qn_t  for t in chunk c
+//   which equals B_v L A^K L^{-1} qn of ska.py:165-181.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace ska {
+
+constexpr int kMaxRank = 64;
+constexpr int kMaxP = 128;
+constexpr int kMaxChunk = 256;
+constexpr int kMaxPowerK = 8;
+constexpr int kThreads = 256;
+constexpr int kPowerIters = 6;        // ska.py:41 (n_iters=6)
+constexpr float kJitter = 1e-4f;      // ska.py:142
+constexpr float kNormClamp = 1e-6f;   // ska.py:441
+constexpr float kPowerEps = 1e-8f;    // ska.py:53,55
+
+struct Dims {
+  int B, T, H, r, P, CS, C, K;
+  int decay;        // 0: standard, 1: decay
+  float ridge;
+  float alpha;      // 1 for standard
+  int SW;           // floats per statistics record: 2 r r + P r
+};
+
+struct In {
+  const void* p;
+  long long sb, st, sh;
+};
+struct Out {
+  void* p;
+  long long sb, st, sh;
+};
+
+template <typename T>
+__device__ __forceinline__ float load_elem(const T* p);
+template <>
+__device__ __forceinline__ float load_elem<float>(const float* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ float load_elem<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_elem(T* p, float v);
+template <>
+__device__ __forceinline__ void store_elem<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_tok(const In& x, int b, int t, int h, int j) {
+  const T* base = static_cast<const T*>(x.p);
+  return load_elem<T>(base + (long long)b * x.sb + (long long)t * x.st + (long long)h * x.sh + j);
+}
+template <typename T>
+__device__ __forceinline__ void st_tok(const Out& x, int b, int t, int h, int j, float v) {
+  T* base = static_cast<T*>(x.p);
+  store_elem<T>(base + (long long)b * x.sb + (long long)t * x.st + (long long)h * x.sh + j, v);
+}
+
+// ---- saved (forward -> backward) and scratch layouts -----------------------
+
+__host__ __device__ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct SavedLayout {
+  size_t stats;     // float [B][H][C][SW]  exclusive-scanned raw statistics
+  size_t cmax;      // u64   [B][H][C]      packed (norm bits, ~t) chunk maxima
+  size_t invs;      // float [B][H][C]      1 / max(sigma, 1)
+  size_t flags;     // int   [B][H][C]      bit0: jittered, bit1: jitter failed too
+  size_t total;
+};
+
+struct ScratchLayout {
+  size_t dstats;    // float [B][H][C][SW]  gradients of the raw statistics
+  size_t dmpart;    // float [B][H][C]      per-chunk partial d(max norm)
+  size_t dgpart;    // float [B][H][C]      per-chunk partial d(gamma)
+  size_t dm;        // float [B][H]
+  size_t total;
+};
+
+__host__ __device__ inline SavedLayout saved_layout(long long B, long long H, long long C, long long SW) {
+  SavedLayout L{};
+  const size_t n = (size_t)B * H * C;
+  size_t off = 0;
+  L.stats = off; off = align256(off + n * SW * sizeof(float));
+  L.cmax = off;  off = align256(off + n * sizeof(unsigned long long));
+  L.invs = off;  off = align256(off + n * sizeof(float));
+  L.flags = off; off = align256(off + n * sizeof(int));
+  L.total = off;
+  return L;
+}
+
+__host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H, long long C, long long SW) {
+  ScratchLayout L{};
+  const size_t n = (size_t)B * H * C;
+  size_t off = 0;
+  L.dstats = off; off = align256(off + n * SW * sizeof(float));
+  L.dmpart = off; off = align256(off + n * sizeof(float));
+  L.dgpart = off; off = align256(off + n * sizeof(float));
+  L.dm = off;     off = align256(off + (size_t)B * H * sizeof(float));
+  L.total = off;
+  return L;
+}
+
+// Packed arg-max key: larger norm wins, ties go to the smaller token index
+// (the first maximum, as torch.max(dim) / numpy.argmax return on the CPU).
+__device__ __forceinline__ unsigned long long pack_max(float norm, int t) {
+  return ((unsigned long long)__float_as_uint(norm) << 32) |
+         (unsigned long long)(0xFFFFFFFFu - (unsigned)t);
+}
+__device__ __forceinline__ float unpack_norm(unsigned long long k) {
+  return __uint_as_float((unsigned)(k >> 32));
+}
+__device__ __forceinline__ int unpack_t(unsigned long long k) {
+  return (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull));
+}
+
+// Caller-provided timing events (ska_set_profile_events); nullptr = off.
+struct ProfileEvents {
+  cudaEvent_t ev[8];
+  bool on;
+};
+ProfileEvents* profile_events();
+inline void prof_record(int i, cudaStream_t st) {
+  ProfileEvents* p = profile_events();
+  if (p->on) cudaEventRecord(p->ev[i], st);
+}
+
+}  // namespace ska

@@ -1,0 +1,930 @@
+// ska_exact.cu -- fp32 CUDA-core SKA core kernels for sm_100a.
+//
+// Six kernels, one CTA per (chunk, head, batch) unless noted:
+//   forward : k_fwd_stats  raw per-chunk statistics G', M', C' + chunk key-norm max
+//             k_scan_fwd   exclusive (decayed) scan over chunks, per (b,h) element
+//             k_fwd_chunk  Cholesky (+jitter) / inverse / spectral norm / operator W,
+//                          readout y = W qn
+//   backward: k_bwd_chunk  recompute the chunk operator, dW and dzq from dy, then the
+//                          reverse chain rule down to d(raw statistics), d(max norm)
+//                          partial and d(gamma) partial
+//             k_scan_bwd   reverse exclusive (decayed) suffix scan; d(max norm) and
+//                          d(gamma) reductions
+//             k_bwd_tok    per-token dz, dv from the scanned statistic gradients, plus
+//                          the arg-max key's share of d(max norm)
+//
+// Every small matrix lives in shared memory with an odd leading dimension so that
+// row- and column-wise accesses are bank-conflict free.  All arithmetic is fp32.
+#include "ska_common.cuh"
+
+namespace ska {
+
+// ----------------------------------------------------------------------------
+// helpers
+// ----------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long y = __shfl_xor_sync(0xffffffffu, x, o);
+    x = y > x ? y : x;
+  }
+  return x;
+}
+
+// Block-wide sum; every thread receives the total.  `red` holds >= 32 floats.
+__device__ float block_sum(float x, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  x = warp_sum(x);
+  __syncthreads();
+  if (lane == 0) red[w] = x;
+  __syncthreads();
+  float s = lane < nw ? red[lane] : 0.f;
+  return warp_sum(s);
+}
+
+__device__ unsigned long long block_max_u64(unsigned long long x, unsigned long long* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  x = warp_max_u64(x);
+  __syncthreads();
+  if (lane == 0) red[w] = x;
+  __syncthreads();
+  unsigned long long s = lane < nw ? red[lane] : 0ull;
+  return warp_max_u64(s);
+}
+
+// C[M x N] = alpha * op(A) op(B)  (+ C when acc), all operands in shared memory.
+//   op(A)(i,k) = TA ? A[k*lda + i] : A[i*lda + k]
+//   op(B)(k,j) = TB ? B[j*ldb + k] : B[k*ldb + j]
+// C must not alias A or B.  Threads tid..nthr-1 of the caller's group share the work;
+// the caller synchronises.
+template <bool TA, bool TB>
+__device__ void smm(float* __restrict__ Cm, int ldc, const float* __restrict__ A, int lda,
+                    const float* __restrict__ Bm, int ldb, int M, int N, int K, float alpha,
+                    bool acc, int tid, int nthr) {
+  constexpr int TM = 2, TN = 2;
+  const int tm = (M + TM - 1) / TM, tn = (N + TN - 1) / TN;
+  for (int t = tid; t < tm * tn; t += nthr) {
+    const int i0 = (t / tn) * TM, j0 = (t % tn) * TN;
+    int ii[TM], jj[TN];
+#pragma unroll
+    for (int u = 0; u < TM; ++u) ii[u] = min(i0 + u, M - 1);
+#pragma unroll
+    for (int v = 0; v < TN; ++v) jj[v] = min(j0 + v, N - 1);
+    float c[TM][TN];
+#pragma unroll
+    for (int u = 0; u < TM; ++u)
+#pragma unroll
+      for (int v = 0; v < TN; ++v) c[u][v] = 0.f;
+    for (int k = 0; k < K; ++k) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int u = 0; u < TM; ++u) a[u] = TA ? A[k * lda + ii[u]] : A[ii[u] * lda + k];
+#pragma unroll
+      for (int v = 0; v < TN; ++v) b[v] = TB ? Bm[jj[v] * ldb + k] : Bm[k * ldb + jj[v]];
+#pragma unroll
+      for (int u = 0; u < TM; ++u)
+#pragma unroll
+        for (int v = 0; v < TN; ++v) c[u][v] = fmaf(a[u], b[v], c[u][v]);
+    }
+#pragma unroll
+    for (int u = 0; u < TM; ++u)
+#pragma unroll
+      for (int v = 0; v < TN; ++v)
+        if (i0 + u < M && j0 + v < N) {
+          float* p = &Cm[(i0 + u) * ldc + j0 + v];
+          *p = acc ? *p + alpha * c[u][v] : alpha * c[u][v];
+        }
+  }
+}
+
+// Lower Cholesky in place (right-looking, one barrier per column).  Reads the lower
+// triangle; on return the lower triangle holds L and the strict upper triangle is
+// zero.  Returns true (uniformly) when a pivot is not positive, as LAPACK potrf's
+// info > 0 (ska.py:140).
+__device__ bool cta_cholesky(float* G, int n, int ld) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  float dprev = 0.f;
+  for (int j = 0; j < n; ++j) {
+    __syncthreads();
+    const float d = G[j * ld + j];
+    if (!(d > 0.f)) {
+      __syncthreads();
+      return true;
+    }
+    if (j > 0) {  // finish column j-1: L[i][j-1] = G[i][j-1] / sqrt(d_{j-1})
+      const float sp = sqrtf(dprev);
+      for (int i = j - 1 + tid; i < n; i += nthr)
+        G[i * ld + j - 1] = (i == j - 1) ? sp : G[i * ld + j - 1] / sp;
+    }
+    const int m = n - j - 1;  // trailing update with the unscaled column j
+    for (int idx = tid; idx < m * m; idx += nthr) {
+      const int i = j + 1 + idx / m, k = j + 1 + idx % m;
+      if (k <= i) G[i * ld + k] -= G[i * ld + j] * G[k * ld + j] / d;
+    }
+    dprev = d;
+  }
+  __syncthreads();
+  if (tid == 0) G[(n - 1) * ld + n - 1] = sqrtf(dprev);
+  for (int idx = tid; idx < n * n; idx += nthr) {
+    const int i = idx / n, k = idx % n;
+    if (k > i) G[i * ld + k] = 0.f;
+  }
+  __syncthreads();
+  return false;
+}
+
+// X = L^{-1} for lower-triangular L (forward elimination, one barrier per row).
+__device__ void cta_tri_inv(float* X, const float* L, int n, int ld) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  for (int idx = tid; idx < n * n; idx += nthr) {
+    const int i = idx / n, c = idx % n;
+    X[i * ld + c] = (i == c) ? 1.f : 0.f;
+  }
+  for (int j = 0; j < n; ++j) {
+    __syncthreads();
+    const float ljj = L[j * ld + j];
+    if (j > 0) {  // finish row j-1
+      const float lp = L[(j - 1) * ld + j - 1];
+      for (int c = tid; c <= j - 1; c += nthr) X[(j - 1) * ld + c] /= lp;
+    }
+    const int m = n - j - 1, w = j + 1;
+    for (int idx = tid; idx < m * w; idx += nthr) {
+      const int i = j + 1 + idx / w, c = idx % w;
+      X[i * ld + c] -= L[i * ld + j] * X[j * ld + c] / ljj;
+    }
+  }
+  __syncthreads();
+  for (int c = tid; c < n; c += nthr) X[(n - 1) * ld + c] /= L[(n - 1) * ld + n - 1];
+  __syncthreads();
+}
+
+// sigma_max estimate of ska.py:41-58 (6 power iterations from v = 1/sqrt(r)),
+// computed by one full warp; r <= 64 (two rows per lane).
+__device__ float warp_power_sigma(const float* A, int r, int ld) {
+  const int lane = threadIdx.x & 31;
+  const float v_init = 1.f / sqrtf((float)r);
+  float v0 = lane < r ? v_init : 0.f, v1 = lane + 32 < r ? v_init : 0.f;
+  float a0 = 0.f, a1 = 0.f;
+  for (int it = 0; it <= kPowerIters; ++it) {
+    a0 = 0.f;
+    a1 = 0.f;
+    for (int j = 0; j < r; ++j) {
+      const float vj = __shfl_sync(0xffffffffu, j < 32 ? v0 : v1, j & 31);
+      if (lane < r) a0 = fmaf(A[lane * ld + j], vj, a0);
+      if (lane + 32 < r) a1 = fmaf(A[(lane + 32) * ld + j], vj, a1);
+    }
+    if (it == kPowerIters) break;  // final A v for sigma
+    const float na = fmaxf(sqrtf(warp_sum(a0 * a0 + a1 * a1)), kPowerEps);
+    const float u0 = a0 / na, u1 = a1 / na;
+    float b0 = 0.f, b1 = 0.f;
+    for (int i = 0; i < r; ++i) {
+      const float ui = __shfl_sync(0xffffffffu, i < 32 ? u0 : u1, i & 31);
+      if (lane < r) b0 = fmaf(A[i * ld + lane], ui, b0);
+      if (lane + 32 < r) b1 = fmaf(A[i * ld + lane + 32], ui, b1);
+    }
+    const float nb = fmaxf(sqrtf(warp_sum(b0 * b0 + b1 * b1)), kPowerEps);
+    v0 = b0 / nb;
+    v1 = b1 / nb;
+  }
+  return sqrtf(warp_sum(a0 * a0 + a1 * a1));
+}
+
+struct SeriesMax {
+  float m;       // clamp(max_t ||z_t||, 1e-6)
+  float raw;     // max_t ||z_t||
+  int tstar;     // first arg-max token
+};
+
+__device__ SeriesMax series_max(const unsigned long long* cmax_bh, int C, unsigned long long* red) {
+  unsigned long long k = 0ull;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const unsigned long long x = cmax_bh[c];
+    k = x > k ? x : k;
+  }
+  k = block_max_u64(k, red);
+  SeriesMax s;
+  s.raw = unpack_norm(k);
+  s.tstar = unpack_t(k);
+  s.m = fmaxf(s.raw, kNormClamp);
+  return s;
+}
+
+__host__ __device__ __forceinline__ int odd_ld(int n) { return n | 1; }
+
+// ----------------------------------------------------------------------------
+// forward: raw chunk statistics
+// ----------------------------------------------------------------------------
+constexpr int kStatTok = 64;      // tokens staged per tile
+constexpr int kStatTiles = 4;     // 4x4 output tiles per thread (covers (2r+P) x r <= 256 x 64)
+
+template <typename IO>
+__global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, float* __restrict__ stats,
+                                                        unsigned long long* __restrict__ cmax) {
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+  const int ldz = odd_ld(r), ldv = odd_ld(P);
+  extern __shared__ float sm[];
+  float* Zs = sm;                          // (kStatTok + 1) x ldz
+  float* Vs = Zs + (kStatTok + 1) * ldz;   // kStatTok x ldv
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(Vs + kStatTok * ldv + 1) ;
+  red = reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(red) + 7) & ~uintptr_t(7));
+
+  const int rows = 2 * r + P;              // stacked left operand [Z ; Z+ ; V]
+  const int tr = (rows + 3) / 4, tc = (r + 3) / 4, ntiles = tr * tc;
+  float acc[kStatTiles][4][4];
+#pragma unroll
+  for (int q = 0; q < kStatTiles; ++q)
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int w = 0; w < 4; ++w) acc[q][u][w] = 0.f;
+
+  unsigned long long key = 0ull;
+  const int tchunk = c * CS;
+  for (int k0 = 0; k0 < CS; k0 += kStatTok) {
+    const int nk = min(kStatTok, CS - k0);
+    __syncthreads();
+    // z rows k0 .. k0+nk (one extra: the next token, which may sit in the next chunk)
+    for (int idx = tid; idx < (nk + 1) * r; idx += blockDim.x) {
+      const int k = idx / r, j = idx % r, t = tchunk + k0 + k;
+      // the extra row belongs to this chunk's transitions only when it exists in [0, T)
+      Zs[k * ldz + j] = (t < T) ? ld_tok<IO>(z, b, t, h, j) : 0.f;
+    }
+    for (int idx = tid; idx < nk * P; idx += blockDim.x) {
+      const int k = idx / P, j = idx % P, t = tchunk + k0 + k;
+      Vs[k * ldv + j] = (t < T) ? ld_tok<IO>(v, b, t, h, j) : 0.f;
+    }
+    __syncthreads();
+    // key-norm maxima over the real tokens of this tile
+    for (int k = warp; k < nk; k += nwarp) {
+      const int t = tchunk + k0 + k;
+      if (t >= T) break;
+      float s = 0.f;
+      for (int j = lane; j < r; j += 32) s = fmaf(Zs[k * ldz + j], Zs[k * ldz + j], s);
+      s = warp_sum(s);
+      const unsigned long long kk = pack_max(sqrtf(s), t);
+      key = kk > key ? kk : key;
+    }
+    // statistics: rows [0,r) = z_t, [r,2r) = z_{t+1}, [2r,2r+P) = v_t ; cols = z_t
+#pragma unroll
+    for (int q = 0; q < kStatTiles; ++q) {
+      const int tile = tid + q * blockDim.x;
+      if (tile >= ntiles) break;
+      const int i0 = (tile / tc) * 4, j0 = (tile % tc) * 4;
+      const float* ap[4];
+      int as[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int row = min(i0 + u, rows - 1);
+        if (row < r) { ap[u] = Zs + row; as[u] = ldz; }
+        else if (row < 2 * r) { ap[u] = Zs + ldz + (row - r); as[u] = ldz; }
+        else { ap[u] = Vs + (row - 2 * r); as[u] = ldv; }
+      }
+      int jj[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) jj[w] = min(j0 + w, r - 1);
+      for (int k = 0; k < nk; ++k) {
+        float a[4], bb[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = ap[u][k * as[u]];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) bb[w] = Zs[k * ldz + jj[w]];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int w = 0; w < 4; ++w) acc[q][u][w] = fmaf(a[u], bb[w], acc[q][u][w]);
+      }
+    }
+  }
+  // record = [G ; M ; C] as a (2r+P) x r row-major matrix
+  const size_t bhc = ((size_t)b * d.H + h) * d.C + c;
+  float* rec = stats + bhc * d.SW;
+#pragma unroll
+  for (int q = 0; q < kStatTiles; ++q) {
+    const int tile = tid + q * blockDim.x;
+    if (tile >= ntiles) break;
+    const int i0 = (tile / tc) * 4, j0 = (tile % tc) * 4;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+        if (i0 + u < rows && j0 + w < r) rec[(i0 + u) * r + j0 + w] = acc[q][u][w];
+  }
+  key = block_max_u64(key, red);
+  if (tid == 0) cmax[bhc] = key;
+}
+
+// ----------------------------------------------------------------------------
+// exclusive scan over chunks (forward) and exclusive suffix scan (backward)
+// ----------------------------------------------------------------------------
+constexpr int kScanBatch = 8;
+
+__global__ void __launch_bounds__(kThreads) k_scan_fwd(Dims d, float* __restrict__ stats) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= d.SW) return;
+  float* base = stats + (size_t)blockIdx.y * d.C * d.SW + e;
+  const size_t s = d.SW;
+  float acc = 0.f;
+  for (int c0 = 0; c0 < d.C; c0 += kScanBatch) {
+    float x[kScanBatch];
+#pragma unroll
+    for (int q = 0; q < kScanBatch; ++q) x[q] = (c0 + q < d.C) ? base[(c0 + q) * s] : 0.f;
+#pragma unroll
+    for (int q = 0; q < kScanBatch; ++q) {
+      if (c0 + q < d.C) {
+        base[(c0 + q) * s] = acc;
+        acc = d.decay ? fmaf(d.alpha, acc, x[q]) : acc + x[q];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict__ dstats,
+                                                       const float* __restrict__ dmpart,
+                                                       const float* __restrict__ dgpart,
+                                                       float* __restrict__ dm, float* __restrict__ dgamma) {
+  __shared__ float red[32];
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int bh = blockIdx.y;
+  if (e < d.SW) {
+    float* base = dstats + (size_t)bh * d.C * d.SW + e;
+    const size_t s = d.SW;
+    float acc = 0.f;
+    for (int c1 = d.C; c1 > 0; c1 -= kScanBatch) {  // chunks c1-1 down to c1-kScanBatch
+      float x[kScanBatch];
+#pragma unroll
+      for (int q = 0; q < kScanBatch; ++q) {
+        const int c = c1 - 1 - q;
+        x[q] = (c >= 0) ? base[c * s] : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < kScanBatch; ++q) {
+        const int c = c1 - 1 - q;
+        if (c >= 0) {
+          base[c * s] = acc;
+          acc = d.decay ? fmaf(d.alpha, acc, x[q]) : acc + x[q];
+        }
+      }
+    }
+  }
+  if (blockIdx.x == 0) {
+    float s = 0.f;
+    for (int c = threadIdx.x; c < d.C; c += blockDim.x) s += dmpart[(size_t)bh * d.C + c];
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) dm[bh] = s;
+    if (bh == 0) {
+      const size_t n = (size_t)d.B * d.H * d.C;
+      float g = 0.f;
+      for (size_t i = threadIdx.x; i < n; i += blockDim.x) g += dgpart[i];
+      g = block_sum(g, red);
+      if (threadIdx.x == 0) *dgamma = g;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// per-chunk operator (shared by forward and backward)
+// ----------------------------------------------------------------------------
+
+// Loads Gn (+ jitter when `jitter`), factors it into `Lb`, returns the failure flag.
+__device__ bool load_and_factor(const float* rec, int r, int ld, float m2, float ridge, bool jitter,
+                                float* Lb) {
+  for (int idx = threadIdx.x; idx < r * r; idx += blockDim.x) {
+    const int i = idx / r, j = idx % r;
+    // ska.py:119,138: G_excl + ridge I, then symmetrise
+    float g = 0.5f * (rec[i * r + j] / m2 + rec[j * r + i] / m2);
+    if (i == j) g += ridge + (jitter ? kJitter : 0.f);
+    Lb[i * ld + j] = g;
+  }
+  return cta_cholesky(Lb, r, ld);
+}
+
+// A^K into a buffer chosen among {b_even, b_odd}; returns the pointer holding it
+// (may be A itself for K == 1).
+__device__ float* matrix_power(float* A, float* b_even, float* b_odd, int r, int ld, int K) {
+  if (K == 0) {
+    for (int idx = threadIdx.x; idx < r * r; idx += blockDim.x) {
+      const int i = idx / r, j = idx % r;
+      b_even[i * ld + j] = (i == j) ? 1.f : 0.f;
+    }
+    __syncthreads();
+    return b_even;
+  }
+  float* cur = A;
+  for (int s = 1; s < K; ++s) {
+    float* out = (s & 1) ? b_even : b_odd;
+    smm<false, false>(out, ld, cur, ld, A, ld, r, r, r, 1.f, false, threadIdx.x, blockDim.x);
+    __syncthreads();
+    cur = out;
+  }
+  return cur;
+}
+
+// ----------------------------------------------------------------------------
+// forward: chunk operator + readout
+// ----------------------------------------------------------------------------
+constexpr int kReadTok = 64;
+
+template <typename IO>
+__global__ void __launch_bounds__(kThreads) k_fwd_chunk(Dims d, In zq, const float* __restrict__ gamma_p, Out y,
+                                                        const float* __restrict__ stats,
+                                                        const unsigned long long* __restrict__ cmax,
+                                                        float* __restrict__ invs_out, int* __restrict__ flags_out) {
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T, tid = threadIdx.x, nthr = blockDim.x;
+  const int ld = odd_ld(r), MX = max(r, P), bs = MX * ld;
+  extern __shared__ float sm[];
+  float* red = sm;                                  // 64 floats (32 u64), 256-byte aligned
+  float* B0 = sm + 64;
+  float* B1 = B0 + bs;
+  float* B2 = B1 + bs;
+  float* B3 = B2 + bs;
+  float* P0 = B3 + bs;
+  float* P1 = P0 + bs;
+  float* Qs = P1 + bs;                              // kReadTok x ld
+  __shared__ float s_sigma;
+
+  const size_t bh = (size_t)b * d.H + h;
+  const size_t bhc = bh * d.C + c;
+  const float* rec = stats + bhc * d.SW;
+  const SeriesMax sx = series_max(cmax + bh * d.C, d.C, reinterpret_cast<unsigned long long*>(red));
+  const float m = sx.m, m2 = m * m;
+
+  // Mn -> B2, Cn -> P0
+  for (int idx = tid; idx < r * r; idx += nthr) B2[(idx / r) * ld + idx % r] = rec[r * r + idx] / m2;
+  for (int idx = tid; idx < P * r; idx += nthr) P0[(idx / r) * ld + idx % r] = rec[2 * r * r + idx] / m;
+  // L -> B0 (jitter retry on failure, ska.py:140-145)
+  int flag = 0;
+  if (load_and_factor(rec, r, ld, m2, d.ridge, false, B0)) {
+    flag = 1;
+    if (load_and_factor(rec, r, ld, m2, d.ridge, true, B0)) flag |= 2;
+  }
+  cta_tri_inv(B1, B0, r, ld);                                               // Li
+  smm<true, false>(B0, ld, B1, ld, B1, ld, r, r, r, 1.f, false, tid, nthr);  // S = Li^T Li
+  __syncthreads();
+  smm<false, false>(B3, ld, B2, ld, B0, ld, r, r, r, 1.f, false, tid, nthr); // A0 = Mn S
+  __syncthreads();
+  if (tid < 32) {
+    const float sg = warp_power_sigma(B3, r, ld);
+    if (tid == 0) s_sigma = sg;
+  } else {
+    smm<false, true>(P1, ld, P0, ld, B1, ld, P, r, r, 1.f, false, tid - 32, nthr - 32);  // X1 = Cn Li^T
+  }
+  __syncthreads();
+  const float invs = 1.f / fmaxf(s_sigma, 1.f);
+  const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
+  const float kk = gs * invs;
+  for (int idx = tid; idx < r * r; idx += nthr) B3[(idx / r) * ld + idx % r] *= kk;   // A
+  __syncthreads();
+  float* AK = matrix_power(B3, B0, B2, r, ld, d.K);
+  smm<false, false>(P0, ld, P1, ld, AK, ld, P, r, r, 1.f, false, tid, nthr);          // X2 = X1 A^K
+  __syncthreads();
+  smm<false, false>(P1, ld, P0, ld, B1, ld, P, r, r, 1.f / m, false, tid, nthr);      // W / m
+  if (tid == 0) {
+    invs_out[bhc] = invs;
+    flags_out[bhc] = flag;
+  }
+  // readout y_t = (W/m) zq_t
+  const int tchunk = c * CS;
+  for (int k0 = 0; k0 < CS; k0 += kReadTok) {
+    const int nk = min(kReadTok, CS - k0);
+    __syncthreads();
+    for (int idx = tid; idx < nk * r; idx += nthr) {
+      const int k = idx / r, j = idx % r, t = tchunk + k0 + k;
+      Qs[k * ld + j] = (t < T) ? ld_tok<IO>(zq, b, t, h, j) : 0.f;
+    }
+    __syncthreads();
+    for (int o = tid; o < nk * P; o += nthr) {
+      const int k = o / P, p = o % P, t = tchunk + k0 + k;
+      if (t >= T) continue;
+      float a = 0.f;
+      for (int j = 0; j < r; ++j) a = fmaf(P1[p * ld + j], Qs[k * ld + j], a);
+      st_tok<IO>(y, b, t, h, p, a);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// backward: chunk operator gradients
+// ----------------------------------------------------------------------------
+constexpr int kBwdTok = 32;
+
+template <typename IO>
+__global__ void __launch_bounds__(kThreads) k_bwd_chunk(Dims d, In zq, In dy, const float* __restrict__ gamma_p,
+                                                        Out dzq, const float* __restrict__ stats,
+                                                        const unsigned long long* __restrict__ cmax,
+                                                        const float* __restrict__ invs_in,
+                                                        const int* __restrict__ flags_in,
+                                                        float* __restrict__ dstats, float* __restrict__ dmpart,
+                                                        float* __restrict__ dgpart) {
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T, tid = threadIdx.x, nthr = blockDim.x;
+  const int ld = odd_ld(r), ldp = odd_ld(P), MX = max(r, P), bs = MX * ld;
+  extern __shared__ float sm[];
+  float* red = sm;                          // 64 floats (32 u64)
+  float* Bf[9];
+  for (int i = 0; i < 9; ++i) Bf[i] = sm + 64 + i * bs;
+  float* DYs = sm + 64 + 9 * bs;            // kBwdTok x ldp
+  float* Qs = DYs + kBwdTok * ldp;          // kBwdTok x ld
+
+  const size_t bh = (size_t)b * d.H + h;
+  const size_t bhc = bh * d.C + c;
+  const float* rec = stats + bhc * d.SW;
+  const SeriesMax sx = series_max(cmax + bh * d.C, d.C, reinterpret_cast<unsigned long long*>(red));
+  const float m = sx.m, m2 = m * m, im = 1.f / m;
+  const int flag = flags_in[bhc];
+  const float invs = invs_in[bhc];
+  const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
+  const bool gpass = (*gamma_p >= 1.f) && (*gamma_p <= 1.5f);   // clamp passes grads inclusively
+  const float kk = gs * invs;
+
+  // ---- recompute the forward operator (same arithmetic as k_fwd_chunk) ----
+  float *bL = Bf[0], *bLi = Bf[1], *bM = Bf[2], *bA = Bf[3];
+  float *p0 = Bf[5], *p1 = Bf[6], *p2 = Bf[7], *p3 = Bf[8];
+  for (int idx = tid; idx < r * r; idx += nthr) bM[(idx / r) * ld + idx % r] = rec[r * r + idx] / m2;
+  for (int idx = tid; idx < P * r; idx += nthr) p0[(idx / r) * ld + idx % r] = rec[2 * r * r + idx] / m;
+  load_and_factor(rec, r, ld, m2, d.ridge, (flag & 1) != 0, bL);
+  cta_tri_inv(bLi, bL, r, ld);
+  smm<true, false>(bL, ld, bLi, ld, bLi, ld, r, r, r, 1.f, false, tid, nthr);  // S (in bL)
+  __syncthreads();
+  smm<false, false>(bA, ld, bM, ld, bL, ld, r, r, r, 1.f, false, tid, nthr);   // A0
+  __syncthreads();
+  for (int idx = tid; idx < r * r; idx += nthr) bA[(idx / r) * ld + idx % r] *= kk;  // A
+  smm<false, true>(p1, ld, p0, ld, bLi, ld, P, r, r, 1.f, false, tid, nthr);   // X1 = Cn Li^T
+  __syncthreads();
+  // A^K uses bL (S, dead) / bM (Mn, dead) as ping-pong buffers
+  float* AK = matrix_power(bA, bL, bM, r, ld, d.K);
+  smm<false, false>(p2, ld, p1, ld, AK, ld, P, r, r, 1.f, false, tid, nthr);   // X2 = X1 A^K
+  __syncthreads();
+  smm<false, false>(p3, ld, p2, ld, bLi, ld, P, r, r, 1.f, false, tid, nthr);  // W
+  __syncthreads();
+
+  // ---- token pass: dW = sum_t dy_t qn_t^T ; dqn_t = W^T dy_t ----
+  float* dW = p0;  // Cn is reloaded later
+  for (int idx = tid; idx < P * r; idx += nthr) dW[(idx / r) * ld + idx % r] = 0.f;
+  float dmq = 0.f;   // <dQn, Qn>
+  const int tchunk = c * CS;
+  for (int k0 = 0; k0 < CS; k0 += kBwdTok) {
+    const int nk = min(kBwdTok, CS - k0);
+    __syncthreads();
+    for (int idx = tid; idx < nk * P; idx += nthr) {
+      const int k = idx / P, p = idx % P, t = tchunk + k0 + k;
+      DYs[k * ldp + p] = (t < T) ? ld_tok<IO>(dy, b, t, h, p) : 0.f;
+    }
+    for (int idx = tid; idx < nk * r; idx += nthr) {
+      const int k = idx / r, j = idx % r, t = tchunk + k0 + k;
+      Qs[k * ld + j] = (t < T) ? ld_tok<IO>(zq, b, t, h, j) * im : 0.f;
+    }
+    __syncthreads();
+    // dW += DY^T Qn   (P x r, K = nk)
+    smm<true, false>(dW, ld, DYs, ldp, Qs, ld, P, r, nk, 1.f, true, tid, nthr);
+    // dqn[k][j] = sum_p DY[k][p] W[p][j]
+    for (int o = tid; o < nk * r; o += nthr) {
+      const int k = o / r, j = o % r, t = tchunk + k0 + k;
+      float a = 0.f;
+      for (int p = 0; p < P; ++p) a = fmaf(DYs[k * ldp + p], p3[p * ld + j], a);
+      if (t < T) {
+        st_tok<IO>(dzq, b, t, h, j, a * im);
+        dmq = fmaf(a, Qs[k * ld + j], dmq);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- reverse chain through W = Cn Li^T A^K Li ----
+  // free r-buffers: bL/bM minus AK (and Bf[4])
+  float* bFree = (AK == bL) ? bM : bL;
+  float* bDLi = bFree;
+  float* dX2 = p3;   // W dead
+  smm<false, true>(dX2, ld, dW, ld, bLi, ld, P, r, r, 1.f, false, tid, nthr);      // dX2 = dW Li^T
+  smm<true, false>(bDLi, ld, p2, ld, dW, ld, r, r, P, 1.f, false, tid, nthr);      // dLi = X2^T dW
+  __syncthreads();
+  float* dX1 = p0;   // dW dead
+  smm<false, true>(dX1, ld, dX2, ld, AK, ld, P, r, r, 1.f, false, tid, nthr);      // dX1 = dX2 AK^T
+  __syncthreads();
+  float* dAK = (AK == bA || AK == bFree) ? Bf[4] : AK;   // AK dead once dX1 exists
+  if (d.K == 0) dAK = Bf[4];
+  smm<true, false>(dAK, ld, p1, ld, dX2, ld, r, r, P, 1.f, false, tid, nthr);      // dAK = X1^T dX2
+  float* Cn = p2;    // X2 dead: reload Cn
+  for (int idx = tid; idx < P * r; idx += nthr) Cn[(idx / r) * ld + idx % r] = rec[2 * r * r + idx] / m;
+  __syncthreads();
+  float* dCn = p1;   // X1 dead
+  smm<false, false>(dCn, ld, dX1, ld, bLi, ld, P, r, r, 1.f, false, tid, nthr);    // dCn = dX1 Li
+  smm<true, false>(bDLi, ld, dX1, ld, Cn, ld, r, r, P, 1.f, true, tid, nthr);      // dLi += dX1^T Cn
+  __syncthreads();
+  float dmc = 0.f;   // <dCn, Cn>
+  {
+    float* out = dstats + bhc * d.SW + 2 * r * r;
+    for (int idx = tid; idx < P * r; idx += nthr) {
+      const int p = idx / r, j = idx % r;
+      const float g = dCn[p * ld + j];
+      dmc = fmaf(g, Cn[p * ld + j], dmc);
+      out[idx] = g / m;
+    }
+  }
+  __syncthreads();
+  // dA from dAK (A^K): Horner over E_s = dAK (A^T)^s,  H <- E_s + A^T H
+  float* dA;
+  if (d.K == 0) {
+    dA = p0;
+    for (int idx = tid; idx < r * r; idx += nthr) dA[(idx / r) * ld + idx % r] = 0.f;
+    __syncthreads();
+  } else if (d.K == 1) {
+    dA = dAK;
+  } else {
+    float* E = dAK;
+    float* H = dAK;
+    float* pool[4] = {p0, p1, p2, p3};
+    int pi = 0;
+    for (int s = 1; s < d.K; ++s) {
+      float* En = pool[pi]; pi = (pi + 1) & 3;
+      float* Hn = pool[pi]; pi = (pi + 1) & 3;
+      smm<false, true>(En, ld, E, ld, bA, ld, r, r, r, 1.f, false, tid, nthr);     // E A^T
+      __syncthreads();
+      for (int idx = tid; idx < r * r; idx += nthr) Hn[(idx / r) * ld + idx % r] = En[(idx / r) * ld + idx % r];
+      __syncthreads();
+      smm<true, false>(Hn, ld, bA, ld, H, ld, r, r, r, 1.f, true, tid, nthr);      // += A^T H
+      __syncthreads();
+      E = En;
+      H = Hn;
+    }
+    dA = H;
+  }
+  // d gamma partial: A = gs * invs * A0  ->  d gs = <dA, A> / gs
+  float dg = 0.f;
+  for (int idx = tid; idx < r * r; idx += nthr) {
+    const int i = idx / r, j = idx % r;
+    dg = fmaf(dA[i * ld + j], bA[i * ld + j], dg);
+  }
+  // recompute S and reload Mn into free buffers
+  float* freeb[4];
+  int nf = 0;
+  {
+    float* cand[7] = {bL, bM, Bf[4], p0, p1, p2, p3};
+    for (int i = 0; i < 7 && nf < 4; ++i) {
+      float* q = cand[i];
+      if (q == dA || q == bDLi || q == bA || q == bLi) continue;
+      freeb[nf++] = q;
+    }
+  }
+  float* S = freeb[0];
+  float* Mn = freeb[1];
+  float* dMn = freeb[2];
+  float* dS = freeb[3];
+  smm<true, false>(S, ld, bLi, ld, bLi, ld, r, r, r, 1.f, false, tid, nthr);
+  for (int idx = tid; idx < r * r; idx += nthr) Mn[(idx / r) * ld + idx % r] = rec[r * r + idx] / m2;
+  __syncthreads();
+  smm<false, false>(dMn, ld, dA, ld, S, ld, r, r, r, kk, false, tid, nthr);        // dMn = kk dA S
+  smm<true, false>(dS, ld, Mn, ld, dA, ld, r, r, r, kk, false, tid, nthr);         // dS = kk Mn^T dA
+  __syncthreads();
+  float dmm = 0.f;   // <dMn, Mn>
+  {
+    float* out = dstats + bhc * d.SW + r * r;
+    for (int idx = tid; idx < r * r; idx += nthr) {
+      const int i = idx / r, j = idx % r;
+      const float g = dMn[i * ld + j];
+      dmm = fmaf(g, Mn[i * ld + j], dmm);
+      out[idx] = g / m2;
+    }
+  }
+  // dS <- dS + dS^T (pairs handled by one thread)
+  for (int idx = tid; idx < r * r; idx += nthr) {
+    const int i = idx / r, j = idx % r;
+    if (j < i) {
+      const float s = dS[i * ld + j] + dS[j * ld + i];
+      dS[i * ld + j] = s;
+      dS[j * ld + i] = s;
+    } else if (j == i) {
+      dS[i * ld + i] *= 2.f;
+    }
+  }
+  __syncthreads();
+  smm<false, false>(bDLi, ld, bLi, ld, dS, ld, r, r, r, 1.f, true, tid, nthr);     // dLi += Li (dS+dS^T)
+  __syncthreads();
+  // Pm = tril(-tril(dLi) Li^T); only the lower triangle of dLi matters (Li lower)
+  float* Pm = dMn;   // written out already
+  for (int idx = tid; idx < r * r; idx += nthr) {
+    const int i = idx / r, j = idx % r;
+    if (j > i) bDLi[i * ld + j] = 0.f;
+  }
+  __syncthreads();
+  smm<false, true>(Pm, ld, bDLi, ld, bLi, ld, r, r, r, -1.f, false, tid, nthr);
+  __syncthreads();
+  // Pm <- 0.5 (tril(Pm) + tril(Pm,-1)^T): symmetric, diagonal halved
+  for (int idx = tid; idx < r * r; idx += nthr) {
+    const int i = idx / r, j = idx % r;
+    if (j < i) {
+      const float s = 0.5f * Pm[i * ld + j];
+      Pm[i * ld + j] = s;
+      Pm[j * ld + i] = s;
+    } else if (j == i) {
+      Pm[i * ld + i] *= 0.5f;
+    }
+  }
+  __syncthreads();
+  float* T1 = dS;
+  smm<false, false>(T1, ld, Pm, ld, bLi, ld, r, r, r, 1.f, false, tid, nthr);      // Pm Li
+  __syncthreads();
+  float* dGn = S;
+  smm<true, false>(dGn, ld, bLi, ld, T1, ld, r, r, r, 1.f, false, tid, nthr);      // Li^T Pm Li
+  __syncthreads();
+  float dmg = 0.f;   // <dGn, G_excl / m^2>
+  {
+    float* out = dstats + bhc * d.SW;
+    for (int idx = tid; idx < r * r; idx += nthr) {
+      const int i = idx / r, j = idx % r;
+      const float g = 0.5f * (dGn[i * ld + j] + dGn[j * ld + i]);
+      dmg = fmaf(g, 0.5f * (rec[i * r + j] + rec[j * r + i]) / m2, dmg);
+      out[idx] = g / m2;
+    }
+  }
+  // d(max norm) partial: -(2<dGn,Gx/m^2> + 2<dMn,Mn> + <dCn,Cn> + <dQn,Qn>) / m
+  float tot = 2.f * dmg + 2.f * dmm + dmc + dmq;
+  tot = block_sum(tot, red);
+  const float dgs = block_sum(dg, red);
+  if (tid == 0) {
+    dmpart[bhc] = -tot / m;
+    dgpart[bhc] = gpass ? dgs / gs : 0.f;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// backward: token pass dz, dv
+// ----------------------------------------------------------------------------
+constexpr int kTokTile = 64;
+
+template <typename IO>
+__global__ void __launch_bounds__(kThreads) k_bwd_tok(Dims d, In z, In v, Out dz, Out dv,
+                                                      const float* __restrict__ dstats,
+                                                      const unsigned long long* __restrict__ cmax,
+                                                      const float* __restrict__ dm) {
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T, tid = threadIdx.x, nthr = blockDim.x;
+  const int ld = odd_ld(r), ldv = odd_ld(P);
+  extern __shared__ float sm[];
+  float* G2 = sm;                       // dG + dG^T        r x ld
+  float* Ms = G2 + r * ld;              // dM (this chunk)  r x ld
+  float* Mp = Ms + r * ld;              // dM (prev chunk)  r x ld
+  float* Cs = Mp + r * ld;              // dC               P x ld
+  float* Zs = Cs + P * ld;              // (kTokTile + 2) x ld : rows t-1 .. t+nk
+  float* Vs = Zs + (kTokTile + 2) * ld; // kTokTile x ldv
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(
+      (reinterpret_cast<uintptr_t>(Vs + kTokTile * ldv) + 7) & ~uintptr_t(7));
+
+  const size_t bh = (size_t)b * d.H + h;
+  const size_t bhc = bh * d.C + c;
+  const float* rec = dstats + bhc * d.SW;
+  for (int idx = tid; idx < r * r; idx += nthr) {
+    const int i = idx / r, j = idx % r;
+    G2[i * ld + j] = rec[i * r + j] + rec[j * r + i];
+    Ms[i * ld + j] = rec[r * r + idx];
+    Mp[i * ld + j] = (c > 0) ? rec[r * r + idx - (long long)d.SW] : 0.f;
+  }
+  for (int idx = tid; idx < P * r; idx += nthr) Cs[(idx / r) * ld + idx % r] = rec[2 * r * r + idx];
+  const SeriesMax sx = series_max(cmax + bh * d.C, d.C, red);
+  const float dmv = dm[bh];
+  const bool route = (sx.raw >= kNormClamp) && (sx.raw > 0.f);
+
+  const int tchunk = c * CS;
+  for (int k0 = 0; k0 < CS; k0 += kTokTile) {
+    const int nk = min(kTokTile, CS - k0);
+    __syncthreads();
+    for (int idx = tid; idx < (nk + 2) * r; idx += nthr) {
+      const int k = idx / r, j = idx % r, t = tchunk + k0 + k - 1;
+      Zs[k * ld + j] = (t >= 0 && t < T) ? ld_tok<IO>(z, b, t, h, j) : 0.f;
+    }
+    for (int idx = tid; idx < nk * P; idx += nthr) {
+      const int k = idx / P, p = idx % P, t = tchunk + k0 + k;
+      Vs[k * ldv + p] = (t < T) ? ld_tok<IO>(v, b, t, h, p) : 0.f;
+    }
+    __syncthreads();
+    // dz_t = (dG+dG^T) z_t + dM^T z_{t+1} + dM' z_{t-1} + dC^T v_t
+    //   dM' = dM of the chunk that owns the transition (t-1 -> t): the previous chunk
+    //   for the first token of a chunk.
+    for (int o = tid; o < nk * r; o += nthr) {
+      const int k = o / r, i = o % r, t = tchunk + k0 + k;
+      if (t >= T) continue;
+      const float* zc = Zs + (k + 1) * ld;
+      const float* zn = Zs + (k + 2) * ld;
+      const float* zp = Zs + k * ld;
+      const float* Mx = (k0 + k == 0) ? Mp : Ms;
+      float a = 0.f;
+      for (int j = 0; j < r; ++j) {
+        a = fmaf(G2[j * ld + i], zc[j], a);
+        a = fmaf(Ms[j * ld + i], zn[j], a);
+        a = fmaf(Mx[i * ld + j], zp[j], a);
+      }
+      for (int p = 0; p < P; ++p) a = fmaf(Cs[p * ld + i], Vs[k * ldv + p], a);
+      if (route && t == sx.tstar) a = fmaf(dmv / sx.raw, zc[i], a);
+      st_tok<IO>(dz, b, t, h, i, a);
+    }
+    // dv_t = dC z_t
+    for (int o = tid; o < nk * P; o += nthr) {
+      const int k = o / P, p = o % P, t = tchunk + k0 + k;
+      if (t >= T) continue;
+      const float* zc = Zs + (k + 1) * ld;
+      float a = 0.f;
+      for (int j = 0; j < r; ++j) a = fmaf(Cs[p * ld + j], zc[j], a);
+      st_tok<IO>(dv, b, t, h, p, a);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// host-side launch helpers (called from ska_capi.cu)
+// ----------------------------------------------------------------------------
+
+size_t smem_fwd_stats(const Dims& d) {
+  const int ldz = odd_ld(d.r), ldv = odd_ld(d.P);
+  return ((size_t)(kStatTok + 1) * ldz + (size_t)kStatTok * ldv + 1) * sizeof(float) + 8 + 32 * 8;
+}
+size_t smem_fwd_chunk(const Dims& d) {
+  const int ld = odd_ld(d.r), MX = d.r > d.P ? d.r : d.P;
+  return ((size_t)6 * MX * ld + (size_t)kReadTok * ld + 64) * sizeof(float);
+}
+size_t smem_bwd_chunk(const Dims& d) {
+  const int ld = odd_ld(d.r), ldp = odd_ld(d.P), MX = d.r > d.P ? d.r : d.P;
+  return ((size_t)9 * MX * ld + (size_t)kBwdTok * ldp + (size_t)kBwdTok * ld + 64) * sizeof(float);
+}
+size_t smem_bwd_tok(const Dims& d) {
+  const int ld = odd_ld(d.r), ldv = odd_ld(d.P);
+  return ((size_t)3 * d.r * ld + (size_t)d.P * ld + (size_t)(kTokTile + 2) * ld + (size_t)kTokTile * ldv) *
+             sizeof(float) + 8 + 32 * 8;
+}
+
+template <typename K>
+static cudaError_t set_smem(K kernel, size_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <typename IO>
+cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
+                       const SavedLayout& L, char* saved, cudaStream_t st) {
+  float* stats = reinterpret_cast<float*>(saved + L.stats);
+  unsigned long long* cmax = reinterpret_cast<unsigned long long*>(saved + L.cmax);
+  float* invs = reinterpret_cast<float*>(saved + L.invs);
+  int* flags = reinterpret_cast<int*>(saved + L.flags);
+  const dim3 grid(d.C, d.H, d.B);
+  cudaError_t e;
+  const size_t s1 = smem_fwd_stats(d), s3 = smem_fwd_chunk(d);
+  if ((e = set_smem(k_fwd_stats<IO>, s1)) != cudaSuccess) return e;
+  if ((e = set_smem(k_fwd_chunk<IO>, s3)) != cudaSuccess) return e;
+  prof_record(0, st);
+  k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
+  prof_record(1, st);
+  k_scan_fwd<<<dim3((d.SW + kThreads - 1) / kThreads, d.B * d.H), kThreads, 0, st>>>(d, stats);
+  prof_record(2, st);
+  k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
+  prof_record(3, st);
+  return cudaGetLastError();
+}
+
+template <typename IO>
+cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const In& dy,
+                       const SavedLayout& L, const char* saved, const ScratchLayout& S, char* scratch,
+                       const Out& dz, const Out& dzq, const Out& dv, float* dgamma, cudaStream_t st) {
+  const float* stats = reinterpret_cast<const float*>(saved + L.stats);
+  const unsigned long long* cmax = reinterpret_cast<const unsigned long long*>(saved + L.cmax);
+  const float* invs = reinterpret_cast<const float*>(saved + L.invs);
+  const int* flags = reinterpret_cast<const int*>(saved + L.flags);
+  float* dstats = reinterpret_cast<float*>(scratch + S.dstats);
+  float* dmpart = reinterpret_cast<float*>(scratch + S.dmpart);
+  float* dgpart = reinterpret_cast<float*>(scratch + S.dgpart);
+  float* dm = reinterpret_cast<float*>(scratch + S.dm);
+  const dim3 grid(d.C, d.H, d.B);
+  cudaError_t e;
+  const size_t s1 = smem_bwd_chunk(d), s3 = smem_bwd_tok(d);
+  if ((e = set_smem(k_bwd_chunk<IO>, s1)) != cudaSuccess) return e;
+  if ((e = set_smem(k_bwd_tok<IO>, s3)) != cudaSuccess) return e;
+  prof_record(4, st);
+  k_bwd_chunk<IO><<<grid, kThreads, s1, st>>>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart,
+                                             dgpart);
+  prof_record(5, st);
+  k_scan_bwd<<<dim3((d.SW + kThreads - 1) / kThreads, d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
+                                                                                     dm, dgamma);
+  prof_record(6, st);
+  k_bwd_tok<IO><<<grid, kThreads, s3, st>>>(d, z, v, dz, dv, dstats, cmax, dm);
+  prof_record(7, st);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_fwd<float>(const Dims&, const In&, const In&, const In&, const float*, const Out&,
+                                       const SavedLayout&, char*, cudaStream_t);
+template cudaError_t launch_fwd<__nv_bfloat16>(const Dims&, const In&, const In&, const In&, const float*,
+                                               const Out&, const SavedLayout&, char*, cudaStream_t);
+template cudaError_t launch_bwd<float>(const Dims&, const In&, const In&, const In&, const float*, const In&,
+                                       const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&,
+                                       const Out&, const Out&, float*, cudaStream_t);
+template cudaError_t launch_bwd<__nv_bfloat16>(const Dims&, const In&, const In&, const In&, const float*,
+                                               const In&, const SavedLayout&, const char*, const ScratchLayout&,
+                                               char*, const Out&, const Out&, const Out&, float*, cudaStream_t);
+
+}  // namespace ska

@@ -1,0 +1,227 @@
+"""Drop-in Spectral Koopman Attention module backed by the sm_100a SKA kernels.
+
+Mirrors ``koopman_lm.ska.SKAModule`` (upstream ``koopman-lm-fast/koopman_lm/ska.py:337-476``):
+the same constructor arguments, parameter names, initialisation, state-dict
+keys, attributes and ``forward(hidden_states[B,T,d_model]) -> [B,T,d_model]``.
+The projections (``ska.py:428-430``) and the ``eta`` / ``out_proj`` epilogue
+(``ska.py:459-460``) stay PyTorch; everything between them (fp32 upcast,
+shared max-key-norm scaling, chunk statistics, exclusive scan, Cholesky with
+jitter, spectral normalisation, filter, readout, and the whole backward) runs in
+``libska_b200.so`` through its C ABI.  There is no other implementation to
+fall back to: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+__all__ = ["SKAModule", "ska_core", "SkaCoreFunction"]
+
+_DTYPES = {torch.float32: _lib.SKA_DTYPE_F32, torch.bfloat16: _lib.SKA_DTYPE_BF16}
+
+
+def _tensor_desc(x: torch.Tensor) -> _lib.SkaTensor:
+    if x.dim() != 4:
+        raise ValueError(f"expected a [B,T,H,D] tensor, got shape {tuple(x.shape)}")
+    if x.numel() > 0 and x.shape[-1] > 1 and x.stride(-1) != 1:
+        raise ValueError("the feature (last) dimension must be contiguous")
+    return _lib.SkaTensor(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2))
+
+
+def _feature_contiguous(x: torch.Tensor) -> torch.Tensor:
+    if x.numel() == 0 or x.shape[-1] <= 1 or x.stride(-1) == 1:
+        return x
+    return x.contiguous()
+
+
+class _Params:
+    __slots__ = ("chunk_size", "ridge_eps", "power_K", "strategy", "decay_alpha")
+
+    def __init__(self, chunk_size, ridge_eps, power_K, strategy, decay_alpha):
+        self.chunk_size = int(chunk_size)
+        self.ridge_eps = float(ridge_eps)
+        self.power_K = int(power_K)
+        self.strategy = int(strategy)
+        self.decay_alpha = float(decay_alpha)
+
+
+def _shape(z, v, p: _Params) -> _lib.SkaShape:
+    B, T, H, r = z.shape
+    return _lib.make_shape(B, T, H, r, v.shape[-1], p.chunk_size, p.power_K, p.ridge_eps,
+                           p.strategy, p.decay_alpha)
+
+
+def _check_inputs(z, zq, v, gamma):
+    for name, t in (("z", z), ("zq", zq), ("v", v)):
+        if not t.is_cuda:
+            raise RuntimeError(f"SKA core: {name} is on {t.device}; the SKA core runs only on CUDA "
+                               "(sm_100a) devices")
+    if not (z.device == zq.device == v.device):
+        raise RuntimeError("SKA core: z, zq, v must be on the same device")
+    if z.dtype not in _DTYPES:
+        raise TypeError(f"SKA core: unsupported dtype {z.dtype} (float32 or bfloat16)")
+    if not (z.dtype == zq.dtype == v.dtype):
+        raise TypeError("SKA core: z, zq, v must share one dtype")
+    if z.shape != zq.shape or z.shape[:3] != v.shape[:3]:
+        raise ValueError(f"SKA core: shape mismatch z{tuple(z.shape)} zq{tuple(zq.shape)} v{tuple(v.shape)}")
+    if gamma.numel() != 1:
+        raise ValueError("SKA core: ssn_gamma must be a scalar")
+
+
+def _stream_ptr(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class SkaCoreFunction(torch.autograd.Function):
+    """autograd wrapper: forward = ``ska_fwd``, backward = ``ska_bwd``."""
+
+    @staticmethod
+    def forward(ctx, z, zq, v, gamma, params: _Params):
+        _check_inputs(z, zq, v, gamma)
+        z, zq, v = (_feature_contiguous(t) for t in (z, zq, v))
+        dev = z.device
+        shape = _shape(z, v, params)
+        saved_bytes, scratch_bytes = _lib.workspace_size(shape)
+        B, T, H, _ = z.shape
+        P = v.shape[-1]
+        y = torch.empty((B, T, H, P), dtype=z.dtype, device=dev)
+        saved = torch.empty(max(saved_bytes, 1), dtype=torch.uint8, device=dev)
+        g32 = gamma.detach().reshape(()).to(device=dev, dtype=torch.float32).contiguous()
+        dz_, dzq_, dv_, dy_ = (_tensor_desc(t) for t in (z, zq, v, y))
+        with torch.cuda.device(dev):
+            rc = _lib.lib().ska_fwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(dz_),
+                                    ctypes.byref(dzq_), ctypes.byref(dv_), ctypes.c_void_p(g32.data_ptr()),
+                                    ctypes.byref(dy_), ctypes.c_void_p(saved.data_ptr()), saved_bytes,
+                                    ctypes.c_void_p(_stream_ptr(dev)))
+        _lib.check("ska_fwd", rc)
+        ctx.params = params
+        ctx.gamma_dtype = gamma.dtype
+        ctx.gamma_shape = gamma.shape
+        ctx.scratch_bytes = scratch_bytes
+        ctx.saved_bytes = saved_bytes
+        ctx.save_for_backward(z, zq, v, g32, saved)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        z, zq, v, g32, saved = ctx.saved_tensors
+        dev = z.device
+        dy = _feature_contiguous(dy.to(z.dtype))
+        shape = _shape(z, v, ctx.params)
+        scratch = torch.empty(max(ctx.scratch_bytes, 1), dtype=torch.uint8, device=dev)
+        dz = torch.empty_like(z, memory_format=torch.contiguous_format)
+        dzq = torch.empty_like(zq, memory_format=torch.contiguous_format)
+        dv = torch.empty_like(v, memory_format=torch.contiguous_format)
+        dgamma = torch.empty((), dtype=torch.float32, device=dev)
+        descs = [_tensor_desc(t) for t in (z, zq, v, dy, dz, dzq, dv)]
+        with torch.cuda.device(dev):
+            rc = _lib.lib().ska_bwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(descs[0]),
+                                    ctypes.byref(descs[1]), ctypes.byref(descs[2]),
+                                    ctypes.c_void_p(g32.data_ptr()), ctypes.byref(descs[3]),
+                                    ctypes.c_void_p(saved.data_ptr()), ctx.saved_bytes,
+                                    ctypes.c_void_p(scratch.data_ptr()), ctx.scratch_bytes,
+                                    ctypes.byref(descs[4]), ctypes.byref(descs[5]), ctypes.byref(descs[6]),
+                                    ctypes.c_void_p(dgamma.data_ptr()), ctypes.c_void_p(_stream_ptr(dev)))
+        _lib.check("ska_bwd", rc)
+        dg = dgamma.to(ctx.gamma_dtype).reshape(ctx.gamma_shape)
+        return dz, dzq, dv, dg, None
+
+
+def ska_core(z, zq, v, gamma, *, chunk_size=64, ridge_eps=1e-3, power_K=2, chunk_strategy="standard",
+             decay_alpha=0.95):
+    """SKA core ``(z, zq, v, ssn_gamma) -> y_hat`` ([B,T,H,P], dtype of ``z``).
+
+    Equivalent to upstream ``ska.py:436-457`` (upcast, max-key-norm scaling,
+    chunk statistics + Cholesky, post-Cholesky chain) for
+    ``chunk_strategy`` in {'standard', 'decay'}; differentiable w.r.t. z, zq, v
+    and gamma.
+    """
+    if not torch.is_tensor(gamma):
+        gamma = torch.tensor(float(gamma), device=z.device)
+    if chunk_strategy == "standard":
+        strategy, alpha = _lib.SKA_STRATEGY_STANDARD, 1.0
+    elif chunk_strategy == "decay":
+        strategy, alpha = _lib.SKA_STRATEGY_DECAY, float(decay_alpha)
+    else:
+        raise NotImplementedError(f"chunk_strategy={chunk_strategy!r} is not supported by the sm_100a SKA core")
+    return SkaCoreFunction.apply(z, zq, v, gamma, _Params(chunk_size, ridge_eps, power_K, strategy, alpha))
+
+
+class SKAModule(nn.Module):
+    """Spectral Koopman Attention with chunk-causal statistics (drop-in for the
+    reference ``SKAModule``).
+
+    Args (same meaning and defaults as upstream ``ska.py:368-371``):
+        d_model, n_heads, rank=48, head_dim=None (d_model // n_heads),
+        ridge_eps=1e-3, scale=1.5 (initial eta), power_K=2, chunk_size=64,
+        backend='auto' (accepted for compatibility; the core always runs on the
+        sm_100a kernels), chunk_strategy='standard' | 'decay' ('overlap' raises
+        NotImplementedError), overlap_fraction=0.5, decay_alpha=0.95.
+    """
+
+    def __init__(self, d_model, n_heads, rank=48, head_dim=None, ridge_eps=1e-3, scale=1.5, power_K=2,
+                 chunk_size=64, backend="auto", chunk_strategy="standard", overlap_fraction=0.5,
+                 decay_alpha=0.95):
+        super().__init__()
+        if chunk_strategy not in ("standard", "decay", "overlap"):
+            raise ValueError(f"unknown chunk_strategy {chunk_strategy!r}")
+        if chunk_strategy == "overlap":
+            raise NotImplementedError("chunk_strategy='overlap' is not supported by the sm_100a SKA core")
+        self.rank = rank
+        self.ridge_eps = ridge_eps
+        self.power_K = power_K
+        self.H = n_heads
+        self.P = head_dim or (d_model // n_heads)
+        self.d_model = d_model
+        self.chunk_size = chunk_size
+        self.chunk_strategy = chunk_strategy
+        self.overlap_fraction = overlap_fraction
+        self.decay_alpha = decay_alpha
+        self.backend = backend
+
+        # same construction and init order as the reference (ska.py:389-400), so a
+        # seeded construction gives identical weights
+        self.key_proj = nn.Linear(d_model, n_heads * rank, bias=False)
+        self.query_proj = nn.Linear(d_model, n_heads * rank, bias=False)
+        self.value_proj = nn.Linear(d_model, n_heads * self.P, bias=False)
+        self.out_proj = nn.Linear(n_heads * self.P, d_model, bias=False)
+
+        nn.init.orthogonal_(self.key_proj.weight)
+        nn.init.orthogonal_(self.query_proj.weight)
+        nn.init.xavier_uniform_(self.value_proj.weight)
+        nn.init.zeros_(self.out_proj.weight)
+
+        self.eta = nn.Parameter(torch.tensor(scale))
+        self.ssn_gamma = nn.Parameter(torch.tensor(1.0))
+
+    def forward(self, hidden_states):
+        B, T, _ = hidden_states.shape
+        r, H, P = self.rank, self.H, self.P
+        z = self.key_proj(hidden_states).reshape(B, T, H, r)
+        zq = self.query_proj(hidden_states).reshape(B, T, H, r)
+        v = self.value_proj(hidden_states).reshape(B, T, H, P)
+        dt = z.dtype if z.dtype in _DTYPES else torch.float32
+        z, zq, v = (t.to(dt) for t in (z, zq, v))
+        with torch.autocast(device_type="cuda", enabled=False):
+            y_hat = ska_core(z, zq, v, self.ssn_gamma, chunk_size=self.chunk_size, ridge_eps=self.ridge_eps,
+                             power_K=self.power_K, chunk_strategy=self.chunk_strategy,
+                             decay_alpha=self.decay_alpha)
+        y_hat = self.eta * y_hat.to(hidden_states.dtype)
+        return self.out_proj(y_hat.reshape(B, T, H * P))
+
+    def extra_repr(self):
+        parts = [
+            f"d_model={self.d_model}",
+            f"n_heads={self.H}",
+            f"rank={self.rank}",
+            f"chunk_size={self.chunk_size}",
+            f"backend={self.backend}",
+            f"chunk_strategy={self.chunk_strategy}",
+        ]
+        if self.chunk_strategy == "decay":
+            parts.append(f"decay_alpha={self.decay_alpha}")
+        return ", ".join(parts)

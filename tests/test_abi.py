@@ -1,0 +1,95 @@
+"""CPU: the C-ABI library builds, loads and exports every symbol the header
+declares; argument validation runs without touching a GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from koopman_mamba_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "ska_b200.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ska_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_expected_functions():
+    assert _declared_functions() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", built_lib], check=True, capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r"\bT (ska_[a-z0-9_]+)$", out, flags=re.M))
+    missing = set(_declared_functions()) - exported
+    assert not missing, missing
+    L = ctypes.CDLL(built_lib)
+    for name in _declared_functions():
+        assert hasattr(L, name)
+
+
+def test_abi_version_and_status_strings(built_lib):
+    assert _lib.lib().ska_abi_version() == _lib.SKA_ABI_VERSION
+    assert _lib.status_string(0) == "ok"
+    for code in range(-8, 0):
+        assert _lib.status_string(code) != "unknown status"
+
+
+def _shape(**kw):
+    base = dict(B=8, T=2048, H=12, r=32, P=64, chunk_size=64, power_K=2, ridge_eps=1e-3)
+    base.update(kw)
+    return _lib.make_shape(**base)
+
+
+def test_workspace_size_config2(built_lib):
+    saved, scratch = _lib.workspace_size(_shape())
+    n = 8 * 12 * 32                 # B*H*C chunk records
+    sw = 2 * 32 * 32 + 64 * 32      # floats per record
+    assert saved >= n * sw * 4 and scratch >= n * sw * 4
+    assert saved % 256 == 0 and scratch % 256 == 0
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(T=0), -2), (dict(H=0), -2), (dict(r=0), -2), (dict(B=-1), -2), (dict(power_K=-1), -2),
+    (dict(chunk_size=0), -2), (dict(r=65), -3), (dict(P=129), -3), (dict(chunk_size=257), -3),
+    (dict(power_K=9), -3), (dict(strategy=7), -8),
+])
+def test_shape_validation(built_lib, kw, code):
+    with pytest.raises(_lib.SkaError) as ei:
+        _lib.workspace_size(_shape(**kw))
+    assert ei.value.code == code
+
+
+def test_fwd_validation_before_any_cuda_call(built_lib):
+    L = _lib.lib()
+    s = _shape(B=1, T=64, H=1)
+    t = _lib.SkaTensor(0, 0, 0, 0)
+    # null data pointers with work to do
+    rc = L.ska_fwd(ctypes.byref(s), 1, ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), None,
+                   ctypes.byref(t), None, 0, None)
+    assert rc == -1
+    # unknown dtype
+    rc = L.ska_fwd(ctypes.byref(s), 5, ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), None,
+                   ctypes.byref(t), None, 0, None)
+    assert rc == -4
+    # misaligned bf16 pointer
+    bad = _lib.SkaTensor(0x1001, 0, 0, 0)
+    rc = L.ska_fwd(ctypes.byref(s), 1, ctypes.byref(bad), ctypes.byref(bad), ctypes.byref(bad), None,
+                   ctypes.byref(bad), None, 0, None)
+    assert rc == -6
+    # B == 0 is a no-op
+    s0 = _shape(B=0)
+    rc = L.ska_fwd(ctypes.byref(s0), 1, ctypes.byref(t), ctypes.byref(t), ctypes.byref(t), None,
+                   ctypes.byref(t), None, 0, None)
+    assert rc == 0
+    # workspace too small
+    ok = _lib.SkaTensor(0x1000, 0, 0, 0)
+    rc = L.ska_fwd(ctypes.byref(s), 1, ctypes.byref(ok), ctypes.byref(ok), ctypes.byref(ok),
+                   ctypes.c_void_p(0x2000), ctypes.byref(ok), ctypes.c_void_p(0x10000), 16, None)
+    assert rc == -5

@@ -1,0 +1,188 @@
+"""GPU parity: the sm_100a SKA core (through the C ABI) against the oracle and
+the reference's golden vectors.
+
+Tolerances (relative Frobenius norm, the parity bar of the spec):
+  * fp32 I/O: 1e-4 on y, dz, dzq, dv;  dgamma within 2e-4 * max(1, |ref|)
+  * bf16 I/O: 2e-2 on y, dz, dzq, dv and dgamma, against the oracle fed the
+    same bf16-rounded inputs (upcast to fp32, as ska.py:436-438 does).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from koopman_mamba_b200 import SKAModule, ska_core
+from koopman_mamba_b200._lib import SkaError
+from oracle.ska_oracle import SkaParams, rel_fro, ska_core_forward, ska_core_fwd_bwd
+from tests._golden import core_cases, load, params_of, strategy_kwargs
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-4
+BF16_TOL = 2e-2
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def run_cuda(z, zq, v, gamma, dy, dtype, **kw):
+    """Forward + backward through the C ABI; returns numpy float64 results."""
+    t = [torch.as_tensor(np.ascontiguousarray(a)).to(DEV, dtype).requires_grad_(True) for a in (z, zq, v)]
+    g = torch.tensor(float(gamma), device=DEV, requires_grad=True)
+    y = ska_core(*t, g, **kw)
+    out = [y.detach()]
+    if dy is not None:
+        y.backward(torch.as_tensor(np.ascontiguousarray(dy)).to(DEV, dtype))
+        out += [t[0].grad, t[1].grad, t[2].grad, g.grad]
+    torch.cuda.synchronize()
+    return [o.double().cpu().numpy() if o.dim() else float(o) for o in out]
+
+
+def bf16_round(a):
+    return torch.as_tensor(np.ascontiguousarray(a)).bfloat16().float().numpy()
+
+
+def assert_close(got, ref, tol, names=("y", "dz", "dzq", "dv")):
+    for g, r, n in zip(got, ref, names):
+        e = rel_fro(g, r)
+        assert e <= tol, f"{n}: rel err {e:.3e} > {tol:.1e}"
+
+
+@pytest.mark.parametrize("case", core_cases())
+def test_golden_fp32(case):
+    d = load(case)
+    y, dz, dzq, dv, dg = run_cuda(d["z"], d["zq"], d["v"], d["meta_gamma"], d["dy"], torch.float32,
+                                  **strategy_kwargs(d))
+    assert_close((y, dz, dzq, dv), (d["y_f64"], d["dz_f64"], d["dzq_f64"], d["dv_f64"]), FP32_TOL)
+    ref = float(d["dgamma_f64"])
+    assert abs(dg - ref) <= 2e-4 * max(1.0, abs(ref)), (dg, ref)
+
+
+@pytest.mark.parametrize("case", core_cases())
+def test_golden_bf16_io(case):
+    d = load(case)
+    z, zq, v, dy = (bf16_round(d[k]) for k in ("z", "zq", "v", "dy"))
+    y, dz, dzq, dv, dg = run_cuda(z, zq, v, d["meta_gamma"], dy, torch.bfloat16, **strategy_kwargs(d))
+    ry, rdz, rdzq, rdv, rdg = ska_core_fwd_bwd(z, zq, v, float(d["meta_gamma"]), dy, params_of(d))
+    assert_close((y, dz, dzq, dv), (ry, rdz, rdzq, rdv), BF16_TOL)
+    assert abs(dg - rdg) <= BF16_TOL * max(1.0, abs(rdg))
+
+
+def _inputs(B, T, H, r, P, seed, bf16=True, dy=True):
+    g = torch.Generator().manual_seed(seed)
+    s = 1.0 / math.sqrt(64)
+    out = [torch.randn(B, T, H, r, generator=g) * s, torch.randn(B, T, H, r, generator=g) * s,
+           torch.randn(B, T, H, P, generator=g) * s]
+    if dy:
+        out.append(torch.randn(B, T, H, P, generator=g))
+    if bf16:
+        out = [t.bfloat16().float() for t in out]
+    return [t.numpy() for t in out]
+
+
+def test_config1_fp32():
+    """Config 1: B=2 H=4 L=512 d=64 r=16, ridge 1e-3, chunk 64, seed 0, fp32."""
+    z, zq, v, dy = _inputs(2, 512, 4, 16, 64, 0, bf16=False)
+    got = run_cuda(z, zq, v, 1.0, dy, torch.float32)
+    ref = ska_core_fwd_bwd(z, zq, v, 1.0, dy, SkaParams())
+    assert_close(got[:4], ref[:4], FP32_TOL)
+    assert abs(got[4] - ref[4]) <= 2e-4 * max(1.0, abs(ref[4]))
+
+
+def test_config2_bf16_full_size():
+    """Config 2: B=8 H=12 L=2048 d=64 r=32, ridge 1e-3, chunk 64, seed 1, bf16 I/O, fwd+bwd."""
+    z, zq, v, dy = _inputs(8, 2048, 12, 32, 64, 1)
+    got = run_cuda(z, zq, v, 1.0, dy, torch.bfloat16)
+    ref = ska_core_fwd_bwd(z, zq, v, 1.0, dy, SkaParams())
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
+def test_config3_bf16_forward_head_subset():
+    """Config 3 (B=1 H=16 L=32768 r=64 chunk 128, seed 2) forward; every (b, h) series is
+    independent, so the oracle checks 3 of the 16 heads at full length."""
+    z, zq, v = _inputs(1, 32768, 16, 64, 64, 2, dy=False)
+    (y,) = run_cuda(z, zq, v, 1.0, None, torch.bfloat16, chunk_size=128)
+    heads = [0, 7, 15]
+    ref, _ = ska_core_forward(z[:, :, heads], zq[:, :, heads], v[:, :, heads], 1.0, SkaParams(chunk_size=128))
+    assert rel_fro(y[:, :, heads], ref) <= BF16_TOL
+    assert np.all(np.isfinite(y))
+
+
+def test_fused_projection_strides_bitwise():
+    """z, zq, v as column slices of one fused projection output (the ska_fast layout)."""
+    B, T, H, r, P = 2, 300, 3, 16, 32
+    g = torch.Generator().manual_seed(5)
+    fused = (torch.randn(B, T, 2 * H * r + H * P, generator=g) / 8).to(DEV, torch.bfloat16)
+    z = fused[:, :, :H * r].reshape(B, T, H, r)
+    zq = fused[:, :, H * r:2 * H * r].reshape(B, T, H, r)
+    v = fused[:, :, 2 * H * r:].reshape(B, T, H, P)
+    gm = torch.tensor(1.1, device=DEV)
+    y1 = ska_core(z, zq, v, gm)
+    y2 = ska_core(z.contiguous(), zq.contiguous(), v.contiguous(), gm)
+    assert torch.equal(y1, y2)
+
+
+def test_deterministic_bitwise():
+    z, zq, v, dy = _inputs(2, 700, 3, 32, 64, 9)
+    a = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16)
+    b = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16)
+    for x, y in zip(a, b):
+        assert np.array_equal(np.asarray(x), np.asarray(y))
+
+
+def test_causality_and_linearity_full_size():
+    """Size-independent properties at config-2 size: v only feeds later chunks (so
+    chunks <= c are bitwise unchanged when v changes in chunk c), chunk 0 is exactly
+    zero, and y is linear in v."""
+    z, zq, v, _ = _inputs(8, 2048, 12, 32, 64, 1)
+    kw = dict(chunk_size=64)
+    (y0,) = run_cuda(z, zq, v, 1.0, None, torch.bfloat16, **kw)
+    assert np.all(y0[:, :64] == 0)
+    v2 = v.copy()
+    v2[:, 5 * 64:6 * 64] = bf16_round(v2[:, 5 * 64:6 * 64] * -3.0)
+    (y1,) = run_cuda(z, zq, v2, 1.0, None, torch.bfloat16, **kw)
+    assert np.array_equal(y0[:, :6 * 64], y1[:, :6 * 64])
+    assert not np.array_equal(y0[:, 6 * 64:], y1[:, 6 * 64:])
+    (y2,) = run_cuda(z, zq, 2.0 * v, 1.0, None, torch.bfloat16, **kw)   # exact in bf16
+    assert rel_fro(y2, 2.0 * y0) <= 1e-2
+
+
+def test_module_end_to_end_against_reference_fixture():
+    d = load("module_small")
+    m = SKAModule(int(d["meta_d_model"]), int(d["meta_H"]), rank=int(d["meta_r"]),
+                  chunk_size=int(d["meta_CS"])).to(DEV)
+    m.load_state_dict({k[3:]: torch.from_numpy(v) for k, v in d.items() if k.startswith("sd_")})
+    x = torch.from_numpy(d["x"]).to(DEV).requires_grad_(True)
+    out = m(x)
+    out.backward(torch.from_numpy(d["dout"]).to(DEV))
+    assert rel_fro(out.detach().cpu().numpy(), d["out"]) <= FP32_TOL
+    assert rel_fro(x.grad.cpu().numpy(), d["dx"]) <= FP32_TOL
+    for name, p in m.named_parameters():
+        ref = d["grad_" + name]
+        got = p.grad.detach().cpu().numpy()
+        if got.ndim == 0:
+            assert abs(float(got) - float(ref)) <= 2e-4 * max(1.0, abs(float(ref))), name
+        else:
+            assert rel_fro(got, ref) <= FP32_TOL, name
+
+
+def test_empty_batch_and_errors():
+    z = torch.zeros(0, 64, 2, 16, device=DEV, requires_grad=True)
+    v = torch.zeros(0, 64, 2, 32, device=DEV, requires_grad=True)
+    g = torch.tensor(1.0, device=DEV, requires_grad=True)
+    y = ska_core(z, z, v, g)
+    assert y.shape == (0, 64, 2, 32)
+    y.sum().backward()
+    assert float(g.grad) == 0.0
+    with pytest.raises(SkaError):
+        ska_core(torch.zeros(1, 8, 1, 65, device=DEV), torch.zeros(1, 8, 1, 65, device=DEV),
+                 torch.zeros(1, 8, 1, 8, device=DEV), g)
+    with pytest.raises(SkaError):
+        ska_core(torch.zeros(1, 0, 1, 8, device=DEV), torch.zeros(1, 0, 1, 8, device=DEV),
+                 torch.zeros(1, 0, 1, 8, device=DEV), g)
