@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""SKA core fwd+bwd throughput on B200 (the Koopman_Mamba SKA hot path).
+
+Workload (one "step" = one forward + one backward of the SKA core between
+the projections and eta/out_proj, over one batch of synthetic input):
+    B=8 per GPU, H=12, L=2048, head dim P=64, rank r=32, chunk 64, ridge 1e-3,
+    power_K=2, bf16 I/O (fp32 arithmetic); z, zq, v ~ N(0,1)/sqrt(64) and
+    dy ~ N(0,1) from seed 1 (+1000*rank), one torch.Generator, in that order.
+Weak scaling: every rank runs its own B=8 shard; no collective in the layer.
+
+Prints ONE JSON line (rank 0):
+  value   tokens/s over all ranks, inputs resident in HBM, device-timed with
+          CUDA events per step (L2 flushed between steps, outside the events),
+          max over ranks
+  e2e     the same metric through the C ABI with pinned HOST buffers: each step
+          copies z, zq, v, dy host->device, runs fwd+bwd, copies y, dz, dzq, dv
+          back; copies inside the timed region
+  roofline  the dominant kernel: algorithmic bytes per launch / its average
+          CUDA-event duration against MEASURED_PEAKS.json HBM bandwidth
+  cpu_baseline  the numpy oracle (port of the reference's CPU path) on the
+          box's host cores, N=1 only
+
+--impl reference times the reference's CPU path (the numpy oracle port, all
+host cores) on the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+B_PER_GPU, H, L, P, R, CS, K, RIDGE = 8, 12, 2048, 64, 32, 64, 2, 1e-3
+SEED = 1
+METRIC = "SKA fwd+bwd tokens/sec/GPU (L=2048,r=32) and % of HBM roofline at 1/2/4/8 B200"
+UNIT = "tokens/s"
+WORKLOAD = "ska_core fwd+bwd B=8/GPU H=12 L=2048 P=64 r=32 chunk=64 K=2 ridge=1e-3 bf16 I/O"
+L2_FLUSH_BYTES = 256 << 20   # > 126 MB L2
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-workers", type=int, default=0, help="oracle processes (0 = all cores, max 8)")
+    return ap.parse_args(argv)
+
+
+# ----------------------------------------------------------------------------
+# CPU side: the oracle port of the reference's CPU path, in a spawn pool
+# ----------------------------------------------------------------------------
+
+def _cpu_task(args):
+    """One batch element of the workload through the numpy oracle (fp32, as the
+    reference computes after .float()); returns seconds."""
+    (b_lo, b_hi, seed) = args
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    import numpy as np
+    from oracle.ska_oracle import SkaParams, ska_core_fwd_bwd
+    z, zq, v, dy = _cpu_inputs(seed)
+    t0 = time.perf_counter()
+    ska_core_fwd_bwd(z[b_lo:b_hi], zq[b_lo:b_hi], v[b_lo:b_hi], 1.0, dy[b_lo:b_hi],
+                     SkaParams(chunk_size=CS, ridge_eps=RIDGE, power_K=K), np.float32)
+    return time.perf_counter() - t0
+
+
+_CPU_CACHE = {}
+
+
+def _cpu_inputs(seed):
+    if seed not in _CPU_CACHE:
+        import torch
+        g = torch.Generator().manual_seed(seed)
+        s = 1.0 / math.sqrt(64)
+        z = torch.randn(B_PER_GPU, L, H, R, generator=g) * s
+        zq = torch.randn(B_PER_GPU, L, H, R, generator=g) * s
+        v = torch.randn(B_PER_GPU, L, H, P, generator=g) * s
+        dy = torch.randn(B_PER_GPU, L, H, P, generator=g)
+        _CPU_CACHE[seed] = [t.bfloat16().float().numpy() for t in (z, zq, v, dy)]
+    return _CPU_CACHE[seed]
+
+
+def _make_pool(workers):
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    env_threads = {"OMP_NUM_THREADS": "1", "OPENBLAS_NUM_THREADS": "1", "MKL_NUM_THREADS": "1"}
+    os.environ.update(env_threads)
+    return ctx.Pool(workers)
+
+
+def cpu_step(pool, workers):
+    """One step of the CPU path: the full B=8 batch split over the workers; the
+    step time is the wall time of the parallel map."""
+    tasks = [(b, b + 1, SEED) for b in range(B_PER_GPU)]
+    t0 = time.perf_counter()
+    pool.map(_cpu_task, tasks, chunksize=1)
+    return time.perf_counter() - t0
+
+
+def cpu_workers(n):
+    cores = os.cpu_count() or 1
+    return max(1, min(B_PER_GPU, cores if n <= 0 else n))
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    workers = cpu_workers(args.cpu_workers)
+    pool = _make_pool(workers)
+    try:
+        pool.map(_cpu_inputs_warm, [SEED] * workers)
+        for _ in range(max(args.warmup, 1)):
+            cpu_step(pool, workers)
+        times = [cpu_step(pool, workers) for _ in range(args.steps)]
+    finally:
+        pool.close()
+        pool.join()
+    total = sum(times)
+    value = B_PER_GPU * L * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1)/8 inputs, bf16-rounded)",
+        "config": {"workload": WORKLOAD, "path": "reference CPU path: numpy oracle port of "
+                   "koopman_lm/ska.py (PyTorch backend) fwd+bwd, fp32", "io_dtype": "bf16-rounded"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
+                         "sample": f"full B=8 batch per step, one batch element per process"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _cpu_inputs_warm(seed):
+    _cpu_inputs(seed)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# GPU side
+# ----------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = os.path.join(REPO, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if gpu_indices and idx not in gpu_indices:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def _visible_gpu_indices(world, local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [int(x) for x in vis.split(",") if x.strip().isdigit()]
+        return ids[:max(world, 1)] if ids else None
+    return list(range(max(world, 1)))
+
+
+def _measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _ncu_traffic():
+    """Per-launch DRAM traffic of each kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+# algorithmic (unique token-tensor) bytes each kernel must move per launch, bf16
+def _kernel_algo_bytes(tokens_heads):
+    es = 2
+    return {
+        "k_fwd_stats": tokens_heads * (R + P) * es,            # read z, v
+        "k_scan_fwd": 0,
+        "k_fwd_chunk": tokens_heads * (R + P) * es,            # read zq, write y
+        "k_bwd_chunk": tokens_heads * (R + P + R) * es,        # read zq, dy; write dzq
+        "k_scan_bwd": 0,
+        "k_bwd_tok": tokens_heads * (R + P + R + P) * es,      # read z, v; write dz, dv
+    }
+
+
+KERNELS = ("k_fwd_stats", "k_scan_fwd", "k_fwd_chunk", "k_bwd_chunk", "k_scan_bwd", "k_bwd_tok")
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    want_cpu = (not args.no_cpu_baseline) and world == 1 and rank == 0
+    pool = None
+    workers = cpu_workers(args.cpu_workers)
+    if want_cpu:
+        pool = _make_pool(workers)   # spawn pool started before any CUDA work
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from koopman_mamba_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- inputs (generated on the host from the seed, moved to HBM untimed) ----
+    g = torch.Generator().manual_seed(SEED + 1000 * rank)
+    s = 1.0 / math.sqrt(64)
+    host = [torch.randn(B_PER_GPU, L, H, n, generator=g) * s for n in (R, R, P)]
+    host.append(torch.randn(B_PER_GPU, L, H, P, generator=g))
+    host = [t.bfloat16().pin_memory() for t in host]
+    z, zq, v, dy = (t.to(dev) for t in host)
+    y = torch.empty(B_PER_GPU, L, H, P, dtype=torch.bfloat16, device=dev)
+    dz, dzq, dv = torch.empty_like(z), torch.empty_like(zq), torch.empty_like(v)
+    gamma = torch.ones((), dtype=torch.float32, device=dev)
+    dgamma = torch.empty((), dtype=torch.float32, device=dev)
+    shape = _lib.make_shape(B_PER_GPU, L, H, R, P, CS, K, RIDGE)
+    saved_bytes, scratch_bytes = _lib.workspace_size(shape)
+    saved = torch.empty(saved_bytes, dtype=torch.uint8, device=dev)
+    scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def desc(t):
+        return _lib.SkaTensor(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+    D = {n: desc(t) for n, t in dict(z=z, zq=zq, v=v, dy=dy, y=y, dz=dz, dzq=dzq, dv=dv).items()}
+    BF16 = _lib.SKA_DTYPE_BF16
+    gp, dgp = ctypes.c_void_p(gamma.data_ptr()), ctypes.c_void_p(dgamma.data_ptr())
+    savp, scrp = ctypes.c_void_p(saved.data_ptr()), ctypes.c_void_p(scratch.data_ptr())
+    byref = ctypes.byref
+
+    def step():
+        rc = lib.ska_fwd(byref(shape), BF16, byref(D["z"]), byref(D["zq"]), byref(D["v"]), gp, byref(D["y"]),
+                         savp, saved_bytes, sp)
+        if rc:
+            _lib.check("ska_fwd", rc)
+        rc = lib.ska_bwd(byref(shape), BF16, byref(D["z"]), byref(D["zq"]), byref(D["v"]), gp, byref(D["dy"]),
+                         savp, saved_bytes, scrp, scratch_bytes, byref(D["dz"]), byref(D["dzq"]), byref(D["dv"]),
+                         dgp, sp)
+        if rc:
+            _lib.check("ska_bwd", rc)
+
+    # per-kernel events (recorded by the library on the launch stream)
+    kev = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.SKA_PROFILE_EVENTS)]
+    for e in kev:
+        e.record(stream)
+    handles = (ctypes.c_void_p * len(kev))(*[e.cuda_event for e in kev])
+    _lib.check("ska_set_profile_events", lib.ska_set_profile_events(handles, len(kev)))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, device-timed per step, L2 flushed in between ----
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    per_kernel = {k: [] for k in KERNELS}
+    clocks = ClockSampler()
+    barrier()
+    torch.cuda.synchronize()
+    if rank == 0:
+        clocks.start()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.zero_()
+        ev0[i].record(stream)
+        step()
+        ev1[i].record(stream)
+        kev[-1].synchronize()
+        spans = [kev[j].elapsed_time(kev[j + 1]) for j in (0, 1, 2)] + \
+                [kev[j].elapsed_time(kev[j + 1]) for j in (4, 5, 6)]
+        for k, ms in zip(KERNELS, spans):
+            per_kernel[k].append(ms)
+    torch.cuda.synchronize()
+    barrier()
+    wall = time.perf_counter() - wall0
+    clock_info = clocks.stop(_visible_gpu_indices(world, local)) if rank == 0 else None
+    dev_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1))
+    t = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms_max = float(t.item())
+    tokens_per_step = world * B_PER_GPU * L
+    value = tokens_per_step * args.steps / (dev_ms_max / 1e3)
+
+    # ---- end to end through the C ABI with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        out_host = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (y, dz, dzq, dv)]
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        d2h = sum(t.numel() * t.element_size() for t in out_host)
+        ea = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        eb = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+        def e2e_step():
+            for src, dst in zip(host, (z, zq, v, dy)):
+                dst.copy_(src, non_blocking=True)
+            step()
+            for src, dst in zip((y, dz, dzq, dv), out_host):
+                dst.copy_(src, non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        for i in range(args.steps):
+            ea[i].record(stream)
+            e2e_step()
+            eb[i].record(stream)
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(ea, eb))], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": tokens_per_step * args.steps / (float(e_ms.item()) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    lib.ska_set_profile_events(None, 0)
+    launches_per_step = 6
+
+    # ---- roofline of the dominant kernel ----
+    peak, peak_kind = _measured_peaks()
+    algo = _kernel_algo_bytes(B_PER_GPU * L * H)
+    avg_ms = {k: statistics.mean(vv) for k, vv in per_kernel.items()}
+    dom = max(avg_ms, key=avg_ms.get)
+    ach = algo[dom] / (avg_ms[dom] / 1e3) / 1e9
+    traffic = _ncu_traffic().get(dom)
+    step_algo = sum(algo.values())
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
+                "frac": ach / peak, "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                "algo_bytes_per_launch": algo[dom],
+                "step": {"algo_bytes": step_algo, "achieved": step_algo / (dev_ms / args.steps / 1e3) / 1e9,
+                         "frac": step_algo / (dev_ms / args.steps / 1e3) / 1e9 / peak},
+                "kernels_ms": {k: round(vv, 4) for k, vv in avg_ms.items()}}
+
+    cpu = None
+    if want_cpu:
+        try:
+            pool.map(_cpu_inputs_warm, [SEED] * workers)
+            cpu_step(pool, workers)
+            ts = [cpu_step(pool, workers) for _ in range(2)]
+            cpu = {"value": B_PER_GPU * L / min(ts), "unit": UNIT, "cores": workers, "kind": "port",
+                   "sample": "full B=8 batch (16384 tokens x 12 heads), numpy oracle fp32, best of 2 after 1 warm-up"}
+        finally:
+            pool.close()
+            pool.join()
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1)/8 inputs, N(0,1) upstream grad)",
+            "config": {"workload": WORKLOAD, "B_per_gpu": B_PER_GPU, "H": H, "L": L, "P": P, "r": R, "chunk": CS,
+                       "power_K": K, "io_dtype": "bf16", "parallelism": f"dp{world} (batch shards, no collective)",
+                       "l2": "flushed between timed steps (256 MiB write outside the events); working set > L2"},
+            "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+            "cpu_baseline": cpu, "clocks": clock_info, "wall_s": wall,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -17,6 +17,9 @@ size_t smem_fwd_stats(const Dims&);
 size_t smem_fwd_chunk(const Dims&);
 size_t smem_bwd_chunk(const Dims&);
 size_t smem_bwd_tok(const Dims&);
+bool warp_path_ok(const Dims&);
+size_t smem_fwd_chunk_w(const Dims&);
+size_t smem_bwd_chunk_w(const Dims&);
 }  // namespace ska
 
 namespace {
@@ -50,9 +53,12 @@ int make_dims(const SkaShape* s, Dims* d) {
   d->SW = 2 * d->r * d->r + d->P * d->r;
   // every kernel's shared-memory tile set must fit one sm_100a CTA (227 KB opt-in)
   const size_t kMaxSmem = 232448;
-  if (ska::smem_fwd_stats(*d) > kMaxSmem || ska::smem_fwd_chunk(*d) > kMaxSmem ||
-      ska::smem_bwd_chunk(*d) > kMaxSmem || ska::smem_bwd_tok(*d) > kMaxSmem)
+  if (ska::smem_fwd_stats(*d) > kMaxSmem || ska::smem_bwd_tok(*d) > kMaxSmem) return SKA_ERR_UNSUPPORTED;
+  if (ska::warp_path_ok(*d)) {
+    if (ska::smem_fwd_chunk_w(*d) == 0 || ska::smem_bwd_chunk_w(*d) == 0) return SKA_ERR_UNSUPPORTED;
+  } else if (ska::smem_fwd_chunk(*d) > kMaxSmem || ska::smem_bwd_chunk(*d) > kMaxSmem) {
     return SKA_ERR_UNSUPPORTED;
+  }
   return SKA_OK;
 }
 

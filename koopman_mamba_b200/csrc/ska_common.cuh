@@ -68,6 +68,10 @@ __device__ __forceinline__ float load_elem<__nv_bfloat16>(const __nv_bfloat16* p
   return __bfloat162float(*p);
 }
 
+// value -> float for an element already held in registers (no memory access)
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+
 template <typename T>
 __device__ __forceinline__ void store_elem(T* p, float v);
 template <>

@@ -59,110 +59,173 @@ __device__ unsigned long long block_max_u64(unsigned long long x, unsigned long 
   return warp_max_u64(s);
 }
 
-// C[M x N] = alpha * op(A) op(B)  (+ C when acc), all operands in shared memory.
+// ---- tensor-core small GEMM (mma.sync m16n8k8 TF32 with a 3-term split) ----
+//
+// x = hi + lo with hi = tf32(x), lo = tf32(x - hi); a*b ~= hi_a hi_b + hi_a lo_b + lo_a hi_b
+// keeps ~fp32 accuracy (error ~2^-21 relative per product) at tensor-core throughput.
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// C[M x N] = alpha * op(A) op(B)  (+ C when acc), all operands fp32 in shared memory.
 //   op(A)(i,k) = TA ? A[k*lda + i] : A[i*lda + k]
 //   op(B)(k,j) = TB ? B[j*ldb + k] : B[k*ldb + j]
-// C must not alias A or B.  Threads tid..nthr-1 of the caller's group share the work;
-// the caller synchronises.
+// C must not alias A or B.  The calling group is the warp-aligned thread range
+// [tid0, tid0 + nthr) given as (tid - tid0, nthr); each warp owns 16x16 output tiles.
+// The caller synchronises.
 template <bool TA, bool TB>
 __device__ void smm(float* __restrict__ Cm, int ldc, const float* __restrict__ A, int lda,
                     const float* __restrict__ Bm, int ldb, int M, int N, int K, float alpha,
                     bool acc, int tid, int nthr) {
-  constexpr int TM = 2, TN = 2;
-  const int tm = (M + TM - 1) / TM, tn = (N + TN - 1) / TN;
-  for (int t = tid; t < tm * tn; t += nthr) {
-    const int i0 = (t / tn) * TM, j0 = (t % tn) * TN;
-    int ii[TM], jj[TN];
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nthr >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int tm = (M + 15) >> 4, tn = (N + 15) >> 4;
+  for (int t = warp; t < tm * tn; t += nwarps) {
+    const int i0 = (t / tn) << 4, j0 = (t % tn) << 4;
+    const int ra = min(i0 + g, M - 1), rb = min(i0 + g + 8, M - 1);
+    const int c0 = min(j0 + g, N - 1), c1 = min(j0 + 8 + g, N - 1);
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      const int ka = k0 + t4, kb = k0 + t4 + 4;
+      const bool va = ka < K, vb = kb < K;
+      const int kas = va ? ka : 0, kbs = vb ? kb : 0;
+      float av[4];
+      av[0] = TA ? A[kas * lda + ra] : A[ra * lda + kas];
+      av[1] = TA ? A[kas * lda + rb] : A[rb * lda + kas];
+      av[2] = TA ? A[kbs * lda + ra] : A[ra * lda + kbs];
+      av[3] = TA ? A[kbs * lda + rb] : A[rb * lda + kbs];
+      if (!va) { av[0] = 0.f; av[1] = 0.f; }
+      if (!vb) { av[2] = 0.f; av[3] = 0.f; }
+      float bv[4];
+      bv[0] = TB ? Bm[c0 * ldb + kas] : Bm[kas * ldb + c0];
+      bv[1] = TB ? Bm[c0 * ldb + kbs] : Bm[kbs * ldb + c0];
+      bv[2] = TB ? Bm[c1 * ldb + kas] : Bm[kas * ldb + c1];
+      bv[3] = TB ? Bm[c1 * ldb + kbs] : Bm[kbs * ldb + c1];
+      if (!va) { bv[0] = 0.f; bv[2] = 0.f; }
+      if (!vb) { bv[1] = 0.f; bv[3] = 0.f; }
+      uint32_t ah[4], al[4], bh[4], bl[4];
 #pragma unroll
-    for (int u = 0; u < TM; ++u) ii[u] = min(i0 + u, M - 1);
-#pragma unroll
-    for (int v = 0; v < TN; ++v) jj[v] = min(j0 + v, N - 1);
-    float c[TM][TN];
-#pragma unroll
-    for (int u = 0; u < TM; ++u)
-#pragma unroll
-      for (int v = 0; v < TN; ++v) c[u][v] = 0.f;
-    for (int k = 0; k < K; ++k) {
-      float a[TM], b[TN];
-#pragma unroll
-      for (int u = 0; u < TM; ++u) a[u] = TA ? A[k * lda + ii[u]] : A[ii[u] * lda + k];
-#pragma unroll
-      for (int v = 0; v < TN; ++v) b[v] = TB ? Bm[jj[v] * ldb + k] : Bm[k * ldb + jj[v]];
-#pragma unroll
-      for (int u = 0; u < TM; ++u)
-#pragma unroll
-        for (int v = 0; v < TN; ++v) c[u][v] = fmaf(a[u], b[v], c[u][v]);
+      for (int q = 0; q < 4; ++q) {
+        split_tf32(av[q], ah[q], al[q]);
+        split_tf32(bv[q], bh[q], bl[q]);
+      }
+      mma_tf32(d0, al, bh[0], bh[1]);
+      mma_tf32(d0, ah, bl[0], bl[1]);
+      mma_tf32(d0, ah, bh[0], bh[1]);
+      mma_tf32(d1, al, bh[2], bh[3]);
+      mma_tf32(d1, ah, bl[2], bl[3]);
+      mma_tf32(d1, ah, bh[2], bh[3]);
     }
+    const int r0 = i0 + g, r1 = i0 + g + 8;
 #pragma unroll
-    for (int u = 0; u < TM; ++u)
+    for (int h = 0; h < 2; ++h) {
+      const float* dd = h ? d1 : d0;
+      const int cc = j0 + 8 * h + 2 * t4;
 #pragma unroll
-      for (int v = 0; v < TN; ++v)
-        if (i0 + u < M && j0 + v < N) {
-          float* p = &Cm[(i0 + u) * ldc + j0 + v];
-          *p = acc ? *p + alpha * c[u][v] : alpha * c[u][v];
+      for (int q = 0; q < 4; ++q) {
+        const int row = (q < 2) ? r0 : r1, col = cc + (q & 1);
+        if (row < M && col < N) {
+          float* p = &Cm[row * ldc + col];
+          *p = acc ? *p + alpha * dd[q] : alpha * dd[q];
         }
+      }
+    }
   }
 }
 
-// Lower Cholesky in place (right-looking, one barrier per column).  Reads the lower
-// triangle; on return the lower triangle holds L and the strict upper triangle is
-// zero.  Returns true (uniformly) when a pivot is not positive, as LAPACK potrf's
-// info > 0 (ska.py:140).
-__device__ bool cta_cholesky(float* G, int n, int ld) {
-  const int tid = threadIdx.x, nthr = blockDim.x;
-  float dprev = 0.f;
+// Lower Cholesky in place by ONE warp (left-looking, as LAPACK potf2): lane i
+// owns rows i and i+32; column j needs the finished rows < j only, so the warp
+// runs without block barriers.  Reads the lower triangle; on success the lower
+// triangle holds L and the strict upper triangle is zero.  Returns true
+// (uniformly over the warp) at the first non-positive pivot, as potrf's info > 0
+// (ska.py:140).  n <= 64.
+__device__ bool warp_cholesky(float* G, int n, int ld) {
+  const int lane = threadIdx.x & 31;
   for (int j = 0; j < n; ++j) {
-    __syncthreads();
-    const float d = G[j * ld + j];
-    if (!(d > 0.f)) {
-      __syncthreads();
-      return true;
+    float s[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = lane + 32 * q;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      if (i >= j && i < n) {
+        const float* ri = G + i * ld;
+        const float* rj = G + j * ld;
+        int k = 0;
+        for (; k + 4 <= j; k += 4) {
+          a0 = fmaf(ri[k], rj[k], a0);
+          a1 = fmaf(ri[k + 1], rj[k + 1], a1);
+          a2 = fmaf(ri[k + 2], rj[k + 2], a2);
+          a3 = fmaf(ri[k + 3], rj[k + 3], a3);
+        }
+        for (; k < j; ++k) a0 = fmaf(ri[k], rj[k], a0);
+        s[q] = ri[j] - ((a0 + a1) + (a2 + a3));
+      } else {
+        s[q] = 0.f;
+      }
     }
-    if (j > 0) {  // finish column j-1: L[i][j-1] = G[i][j-1] / sqrt(d_{j-1})
-      const float sp = sqrtf(dprev);
-      for (int i = j - 1 + tid; i < n; i += nthr)
-        G[i * ld + j - 1] = (i == j - 1) ? sp : G[i * ld + j - 1] / sp;
+    const float dj = __shfl_sync(0xffffffffu, j < 32 ? s[0] : s[1], j & 31);
+    if (!(dj > 0.f)) return true;
+    const float ljj = sqrtf(dj);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int i = lane + 32 * q;
+      if (i == j) G[i * ld + j] = ljj;
+      else if (i > j && i < n) G[i * ld + j] = s[q] / ljj;
     }
-    const int m = n - j - 1;  // trailing update with the unscaled column j
-    for (int idx = tid; idx < m * m; idx += nthr) {
-      const int i = j + 1 + idx / m, k = j + 1 + idx % m;
-      if (k <= i) G[i * ld + k] -= G[i * ld + j] * G[k * ld + j] / d;
-    }
-    dprev = d;
+    __syncwarp();
   }
-  __syncthreads();
-  if (tid == 0) G[(n - 1) * ld + n - 1] = sqrtf(dprev);
-  for (int idx = tid; idx < n * n; idx += nthr) {
+  for (int idx = lane; idx < n * n; idx += 32) {
     const int i = idx / n, k = idx % n;
     if (k > i) G[i * ld + k] = 0.f;
   }
-  __syncthreads();
+  __syncwarp();
   return false;
 }
 
-// X = L^{-1} for lower-triangular L (forward elimination, one barrier per row).
-__device__ void cta_tri_inv(float* X, const float* L, int n, int ld) {
-  const int tid = threadIdx.x, nthr = blockDim.x;
-  for (int idx = tid; idx < n * n; idx += nthr) {
-    const int i = idx / n, c = idx % n;
-    X[i * ld + c] = (i == c) ? 1.f : 0.f;
-  }
-  for (int j = 0; j < n; ++j) {
-    __syncthreads();
-    const float ljj = L[j * ld + j];
-    if (j > 0) {  // finish row j-1
-      const float lp = L[(j - 1) * ld + j - 1];
-      for (int c = tid; c <= j - 1; c += nthr) X[(j - 1) * ld + c] /= lp;
+// X = L^{-1} for lower-triangular L, by ONE warp (forward substitution): lane c
+// owns columns c and c+32, so every lane reads only its own columns of X.
+__device__ void warp_tri_inv(float* X, const float* L, int n, int ld) {
+  const int lane = threadIdx.x & 31;
+  for (int i = 0; i < n; ++i) {
+    const float lii = L[i * ld + i];
+    const float* li = L + i * ld;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int c = lane + 32 * q;
+      if (c >= n) continue;
+      float v;
+      if (c > i) {
+        v = 0.f;
+      } else if (c == i) {
+        v = 1.f / lii;
+      } else {
+        float a0 = 0.f, a1 = 0.f;
+        int k = c;
+        for (; k + 2 <= i; k += 2) {
+          a0 = fmaf(li[k], X[k * ld + c], a0);
+          a1 = fmaf(li[k + 1], X[(k + 1) * ld + c], a1);
+        }
+        if (k < i) a0 = fmaf(li[k], X[k * ld + c], a0);
+        v = -(a0 + a1) / lii;
+      }
+      X[i * ld + c] = v;
     }
-    const int m = n - j - 1, w = j + 1;
-    for (int idx = tid; idx < m * w; idx += nthr) {
-      const int i = j + 1 + idx / w, c = idx % w;
-      X[i * ld + c] -= L[i * ld + j] * X[j * ld + c] / ljj;
-    }
   }
-  __syncthreads();
-  for (int c = tid; c < n; c += nthr) X[(n - 1) * ld + c] /= L[(n - 1) * ld + n - 1];
-  __syncthreads();
+  __syncwarp();
 }
 
 // sigma_max estimate of ska.py:41-58 (6 power iterations from v = 1/sqrt(r)),
@@ -222,7 +285,6 @@ __host__ __device__ __forceinline__ int odd_ld(int n) { return n | 1; }
 // forward: raw chunk statistics
 // ----------------------------------------------------------------------------
 constexpr int kStatTok = 64;      // tokens staged per tile
-constexpr int kStatTiles = 4;     // 4x4 output tiles per thread (covers (2r+P) x r <= 256 x 64)
 
 template <typename IO>
 __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, float* __restrict__ stats,
@@ -232,30 +294,19 @@ __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, floa
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
   const int ldz = odd_ld(r), ldv = odd_ld(P);
   extern __shared__ float sm[];
-  float* Zs = sm;                          // (kStatTok + 1) x ldz
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(sm);   // 32 u64
+  float* Acc = sm + 64;                    // (2r + P) x ldz : [G ; M ; C]
+  float* Zs = Acc + (2 * r + P) * ldz;     // (kStatTok + 1) x ldz
   float* Vs = Zs + (kStatTok + 1) * ldz;   // kStatTok x ldv
-  unsigned long long* red = reinterpret_cast<unsigned long long*>(Vs + kStatTok * ldv + 1) ;
-  red = reinterpret_cast<unsigned long long*>((reinterpret_cast<uintptr_t>(red) + 7) & ~uintptr_t(7));
-
-  const int rows = 2 * r + P;              // stacked left operand [Z ; Z+ ; V]
-  const int tr = (rows + 3) / 4, tc = (r + 3) / 4, ntiles = tr * tc;
-  float acc[kStatTiles][4][4];
-#pragma unroll
-  for (int q = 0; q < kStatTiles; ++q)
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-#pragma unroll
-      for (int w = 0; w < 4; ++w) acc[q][u][w] = 0.f;
 
   unsigned long long key = 0ull;
   const int tchunk = c * CS;
   for (int k0 = 0; k0 < CS; k0 += kStatTok) {
     const int nk = min(kStatTok, CS - k0);
     __syncthreads();
-    // z rows k0 .. k0+nk (one extra: the next token, which may sit in the next chunk)
+    // z rows k0 .. k0+nk (one extra: the next token, possibly in the next chunk)
     for (int idx = tid; idx < (nk + 1) * r; idx += blockDim.x) {
       const int k = idx / r, j = idx % r, t = tchunk + k0 + k;
-      // the extra row belongs to this chunk's transitions only when it exists in [0, T)
       Zs[k * ldz + j] = (t < T) ? ld_tok<IO>(z, b, t, h, j) : 0.f;
     }
     for (int idx = tid; idx < nk * P; idx += blockDim.x) {
@@ -263,8 +314,7 @@ __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, floa
       Vs[k * ldv + j] = (t < T) ? ld_tok<IO>(v, b, t, h, j) : 0.f;
     }
     __syncthreads();
-    // key-norm maxima over the real tokens of this tile
-    for (int k = warp; k < nk; k += nwarp) {
+    for (int k = warp; k < nk; k += nwarp) {   // key-norm maxima over the real tokens
       const int t = tchunk + k0 + k;
       if (t >= T) break;
       float s = 0.f;
@@ -273,51 +323,16 @@ __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, floa
       const unsigned long long kk = pack_max(sqrtf(s), t);
       key = kk > key ? kk : key;
     }
-    // statistics: rows [0,r) = z_t, [r,2r) = z_{t+1}, [2r,2r+P) = v_t ; cols = z_t
-#pragma unroll
-    for (int q = 0; q < kStatTiles; ++q) {
-      const int tile = tid + q * blockDim.x;
-      if (tile >= ntiles) break;
-      const int i0 = (tile / tc) * 4, j0 = (tile % tc) * 4;
-      const float* ap[4];
-      int as[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int row = min(i0 + u, rows - 1);
-        if (row < r) { ap[u] = Zs + row; as[u] = ldz; }
-        else if (row < 2 * r) { ap[u] = Zs + ldz + (row - r); as[u] = ldz; }
-        else { ap[u] = Vs + (row - 2 * r); as[u] = ldv; }
-      }
-      int jj[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) jj[w] = min(j0 + w, r - 1);
-      for (int k = 0; k < nk; ++k) {
-        float a[4], bb[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) a[u] = ap[u][k * as[u]];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) bb[w] = Zs[k * ldz + jj[w]];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int w = 0; w < 4; ++w) acc[q][u][w] = fmaf(a[u], bb[w], acc[q][u][w]);
-      }
-    }
+    const bool acc = k0 > 0;
+    smm<true, false>(Acc, ldz, Zs, ldz, Zs, ldz, r, r, nk, 1.f, acc, tid, blockDim.x);                  // G += Z^T Z
+    smm<true, false>(Acc + r * ldz, ldz, Zs + ldz, ldz, Zs, ldz, r, r, nk, 1.f, acc, tid, blockDim.x);  // M += Z+^T Z
+    smm<true, false>(Acc + 2 * r * ldz, ldz, Vs, ldv, Zs, ldz, P, r, nk, 1.f, acc, tid, blockDim.x);    // C += V^T Z
   }
+  __syncthreads();
   // record = [G ; M ; C] as a (2r+P) x r row-major matrix
   const size_t bhc = ((size_t)b * d.H + h) * d.C + c;
   float* rec = stats + bhc * d.SW;
-#pragma unroll
-  for (int q = 0; q < kStatTiles; ++q) {
-    const int tile = tid + q * blockDim.x;
-    if (tile >= ntiles) break;
-    const int i0 = (tile / tc) * 4, j0 = (tile % tc) * 4;
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-#pragma unroll
-      for (int w = 0; w < 4; ++w)
-        if (i0 + u < rows && j0 + w < r) rec[(i0 + u) * r + j0 + w] = acc[q][u][w];
-  }
+  for (int idx = tid; idx < (2 * r + P) * r; idx += blockDim.x) rec[idx] = Acc[(idx / r) * ldz + idx % r];
   key = block_max_u64(key, red);
   if (tid == 0) cmax[bhc] = key;
 }
@@ -327,52 +342,84 @@ __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, floa
 // ----------------------------------------------------------------------------
 constexpr int kScanBatch = 8;
 
-__global__ void __launch_bounds__(kThreads) k_scan_fwd(Dims d, float* __restrict__ stats) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= d.SW) return;
-  float* base = stats + (size_t)blockIdx.y * d.C * d.SW + e;
-  const size_t s = d.SW;
-  float acc = 0.f;
-  for (int c0 = 0; c0 < d.C; c0 += kScanBatch) {
-    float x[kScanBatch];
-#pragma unroll
-    for (int q = 0; q < kScanBatch; ++q) x[q] = (c0 + q < d.C) ? base[(c0 + q) * s] : 0.f;
+// One thread scans 4 consecutive record floats (a float4 when SW % 4 == 0).
+__device__ __forceinline__ void scan_lanes4(float* base, int n4, size_t s, int C, bool reverse, int decay,
+                                            float alpha) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = 0; c0 < C; c0 += kScanBatch) {
+    float4 x[kScanBatch];
 #pragma unroll
     for (int q = 0; q < kScanBatch; ++q) {
-      if (c0 + q < d.C) {
-        base[(c0 + q) * s] = acc;
-        acc = d.decay ? fmaf(d.alpha, acc, x[q]) : acc + x[q];
+      const int c = reverse ? C - 1 - (c0 + q) : c0 + q;
+      if (c0 + q < C) {
+        if (n4 == 4) {
+          x[q] = *reinterpret_cast<const float4*>(base + c * s);
+        } else {
+          x[q].x = base[c * s];
+          x[q].y = n4 > 1 ? base[c * s + 1] : 0.f;
+          x[q].z = n4 > 2 ? base[c * s + 2] : 0.f;
+          x[q].w = 0.f;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kScanBatch; ++q) {
+      const int c = reverse ? C - 1 - (c0 + q) : c0 + q;
+      if (c0 + q < C) {
+        if (n4 == 4) {
+          *reinterpret_cast<float4*>(base + c * s) = acc;
+        } else {
+          base[c * s] = acc.x;
+          if (n4 > 1) base[c * s + 1] = acc.y;
+          if (n4 > 2) base[c * s + 2] = acc.z;
+        }
+        if (decay) {
+          acc.x = fmaf(alpha, acc.x, x[q].x);
+          acc.y = fmaf(alpha, acc.y, x[q].y);
+          acc.z = fmaf(alpha, acc.z, x[q].z);
+          acc.w = fmaf(alpha, acc.w, x[q].w);
+        } else {
+          acc.x += x[q].x;
+          acc.y += x[q].y;
+          acc.z += x[q].z;
+          acc.w += x[q].w;
+        }
       }
     }
   }
 }
 
+// Exclusive (decayed) scan of every record float over the chunks of one series.
+__global__ void __launch_bounds__(kThreads) k_scan_fwd(Dims d, float* __restrict__ stats) {
+  const int e = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (e >= d.SW) return;
+  const bool vec = (d.SW & 3) == 0;
+  const int n4 = vec ? 4 : min(4, d.SW - e);
+  float* base = stats + (size_t)blockIdx.y * d.C * d.SW + e;
+  if (vec) {
+    scan_lanes4(base, 4, d.SW, d.C, false, d.decay, d.alpha);
+  } else {
+    for (int q = 0; q < n4; ++q) scan_lanes4(base + q, 1, d.SW, d.C, false, d.decay, d.alpha);
+  }
+}
+
+// Exclusive (decayed) suffix scan of the statistic gradients, plus the d(max norm)
+// and d(gamma) reductions.
 __global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict__ dstats,
                                                        const float* __restrict__ dmpart,
                                                        const float* __restrict__ dgpart,
                                                        float* __restrict__ dm, float* __restrict__ dgamma) {
   __shared__ float red[32];
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  const int e = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   const int bh = blockIdx.y;
   if (e < d.SW) {
+    const bool vec = (d.SW & 3) == 0;
     float* base = dstats + (size_t)bh * d.C * d.SW + e;
-    const size_t s = d.SW;
-    float acc = 0.f;
-    for (int c1 = d.C; c1 > 0; c1 -= kScanBatch) {  // chunks c1-1 down to c1-kScanBatch
-      float x[kScanBatch];
-#pragma unroll
-      for (int q = 0; q < kScanBatch; ++q) {
-        const int c = c1 - 1 - q;
-        x[q] = (c >= 0) ? base[c * s] : 0.f;
-      }
-#pragma unroll
-      for (int q = 0; q < kScanBatch; ++q) {
-        const int c = c1 - 1 - q;
-        if (c >= 0) {
-          base[c * s] = acc;
-          acc = d.decay ? fmaf(d.alpha, acc, x[q]) : acc + x[q];
-        }
-      }
+    if (vec) {
+      scan_lanes4(base, 4, d.SW, d.C, true, d.decay, d.alpha);
+    } else {
+      const int n4 = min(4, d.SW - e);
+      for (int q = 0; q < n4; ++q) scan_lanes4(base + q, 1, d.SW, d.C, true, d.decay, d.alpha);
     }
   }
   if (blockIdx.x == 0) {
@@ -394,9 +441,11 @@ __global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict
 // per-chunk operator (shared by forward and backward)
 // ----------------------------------------------------------------------------
 
-// Loads Gn (+ jitter when `jitter`), factors it into `Lb`, returns the failure flag.
+// All threads load Gn (+ jitter when `jitter`) into `Lb`; warp 0 factors it and,
+// when `Li` is given and the factorisation succeeded, also inverts it.  Returns the
+// failure flag (uniform over the block).  Ends with a block barrier.
 __device__ bool load_and_factor(const float* rec, int r, int ld, float m2, float ridge, bool jitter,
-                                float* Lb) {
+                                float* Lb, float* Li, int* s_flag) {
   for (int idx = threadIdx.x; idx < r * r; idx += blockDim.x) {
     const int i = idx / r, j = idx % r;
     // ska.py:119,138: G_excl + ridge I, then symmetrise
@@ -404,7 +453,14 @@ __device__ bool load_and_factor(const float* rec, int r, int ld, float m2, float
     if (i == j) g += ridge + (jitter ? kJitter : 0.f);
     Lb[i * ld + j] = g;
   }
-  return cta_cholesky(Lb, r, ld);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const bool f = warp_cholesky(Lb, r, ld);
+    if (Li) warp_tri_inv(Li, Lb, r, ld);   // also after a failure, so that the result stays deterministic
+    if (threadIdx.x == 0) *s_flag = f ? 1 : 0;
+  }
+  __syncthreads();
+  return *s_flag != 0;
 }
 
 // A^K into a buffer chosen among {b_even, b_odd}; returns the pointer holding it
@@ -450,6 +506,8 @@ __global__ void __launch_bounds__(kThreads) k_fwd_chunk(Dims d, In zq, const flo
   float* P0 = B3 + bs;
   float* P1 = P0 + bs;
   float* Qs = P1 + bs;                              // kReadTok x ld
+  float* Ys = Qs + kReadTok * ld;                   // kReadTok x ldp
+  const int ldp = odd_ld(P);
   __shared__ float s_sigma;
 
   const size_t bh = (size_t)b * d.H + h;
@@ -462,12 +520,12 @@ __global__ void __launch_bounds__(kThreads) k_fwd_chunk(Dims d, In zq, const flo
   for (int idx = tid; idx < r * r; idx += nthr) B2[(idx / r) * ld + idx % r] = rec[r * r + idx] / m2;
   for (int idx = tid; idx < P * r; idx += nthr) P0[(idx / r) * ld + idx % r] = rec[2 * r * r + idx] / m;
   // L -> B0 (jitter retry on failure, ska.py:140-145)
+  __shared__ int s_flag;
   int flag = 0;
-  if (load_and_factor(rec, r, ld, m2, d.ridge, false, B0)) {
+  if (load_and_factor(rec, r, ld, m2, d.ridge, false, B0, B1, &s_flag)) {
     flag = 1;
-    if (load_and_factor(rec, r, ld, m2, d.ridge, true, B0)) flag |= 2;
+    if (load_and_factor(rec, r, ld, m2, d.ridge, true, B0, B1, &s_flag)) flag |= 2;
   }
-  cta_tri_inv(B1, B0, r, ld);                                               // Li
   smm<true, false>(B0, ld, B1, ld, B1, ld, r, r, r, 1.f, false, tid, nthr);  // S = Li^T Li
   __syncthreads();
   smm<false, false>(B3, ld, B2, ld, B0, ld, r, r, r, 1.f, false, tid, nthr); // A0 = Mn S
@@ -502,12 +560,11 @@ __global__ void __launch_bounds__(kThreads) k_fwd_chunk(Dims d, In zq, const flo
       Qs[k * ld + j] = (t < T) ? ld_tok<IO>(zq, b, t, h, j) : 0.f;
     }
     __syncthreads();
+    smm<false, true>(Ys, ldp, Qs, ld, P1, ld, nk, P, r, 1.f, false, tid, nthr);   // Y = Qs (W/m)^T
+    __syncthreads();
     for (int o = tid; o < nk * P; o += nthr) {
       const int k = o / P, p = o % P, t = tchunk + k0 + k;
-      if (t >= T) continue;
-      float a = 0.f;
-      for (int j = 0; j < r; ++j) a = fmaf(P1[p * ld + j], Qs[k * ld + j], a);
-      st_tok<IO>(y, b, t, h, p, a);
+      if (t < T) st_tok<IO>(y, b, t, h, p, Ys[k * ldp + p]);
     }
   }
 }
@@ -534,6 +591,7 @@ __global__ void __launch_bounds__(kThreads) k_bwd_chunk(Dims d, In zq, In dy, co
   for (int i = 0; i < 9; ++i) Bf[i] = sm + 64 + i * bs;
   float* DYs = sm + 64 + 9 * bs;            // kBwdTok x ldp
   float* Qs = DYs + kBwdTok * ldp;          // kBwdTok x ld
+  float* DQs = Qs + kBwdTok * ld;           // kBwdTok x ld
 
   const size_t bh = (size_t)b * d.H + h;
   const size_t bhc = bh * d.C + c;
@@ -551,8 +609,8 @@ __global__ void __launch_bounds__(kThreads) k_bwd_chunk(Dims d, In zq, In dy, co
   float *p0 = Bf[5], *p1 = Bf[6], *p2 = Bf[7], *p3 = Bf[8];
   for (int idx = tid; idx < r * r; idx += nthr) bM[(idx / r) * ld + idx % r] = rec[r * r + idx] / m2;
   for (int idx = tid; idx < P * r; idx += nthr) p0[(idx / r) * ld + idx % r] = rec[2 * r * r + idx] / m;
-  load_and_factor(rec, r, ld, m2, d.ridge, (flag & 1) != 0, bL);
-  cta_tri_inv(bLi, bL, r, ld);
+  __shared__ int s_flag;
+  load_and_factor(rec, r, ld, m2, d.ridge, (flag & 1) != 0, bL, bLi, &s_flag);
   smm<true, false>(bL, ld, bLi, ld, bLi, ld, r, r, r, 1.f, false, tid, nthr);  // S (in bL)
   __syncthreads();
   smm<false, false>(bA, ld, bM, ld, bL, ld, r, r, r, 1.f, false, tid, nthr);   // A0
@@ -586,11 +644,12 @@ __global__ void __launch_bounds__(kThreads) k_bwd_chunk(Dims d, In zq, In dy, co
     __syncthreads();
     // dW += DY^T Qn   (P x r, K = nk)
     smm<true, false>(dW, ld, DYs, ldp, Qs, ld, P, r, nk, 1.f, true, tid, nthr);
-    // dqn[k][j] = sum_p DY[k][p] W[p][j]
+    // dqn = DY W  (nk x r)
+    smm<false, false>(DQs, ld, DYs, ldp, p3, ld, nk, r, P, 1.f, false, tid, nthr);
+    __syncthreads();
     for (int o = tid; o < nk * r; o += nthr) {
       const int k = o / r, j = o % r, t = tchunk + k0 + k;
-      float a = 0.f;
-      for (int p = 0; p < P; ++p) a = fmaf(DYs[k * ldp + p], p3[p * ld + j], a);
+      const float a = DQs[k * ld + j];
       if (t < T) {
         st_tok<IO>(dzq, b, t, h, j, a * im);
         dmq = fmaf(a, Qs[k * ld + j], dmq);
@@ -776,8 +835,10 @@ __global__ void __launch_bounds__(kThreads) k_bwd_tok(Dims d, In z, In v, Out dz
   float* Cs = Mp + r * ld;              // dC               P x ld
   float* Zs = Cs + P * ld;              // (kTokTile + 2) x ld : rows t-1 .. t+nk
   float* Vs = Zs + (kTokTile + 2) * ld; // kTokTile x ldv
+  float* DZ = Vs + kTokTile * ldv;      // kTokTile x ld
+  float* DV = DZ + kTokTile * ld;       // kTokTile x ldv
   unsigned long long* red = reinterpret_cast<unsigned long long*>(
-      (reinterpret_cast<uintptr_t>(Vs + kTokTile * ldv) + 7) & ~uintptr_t(7));
+      (reinterpret_cast<uintptr_t>(DV + kTokTile * ldv) + 7) & ~uintptr_t(7));
 
   const size_t bh = (size_t)b * d.H + h;
   const size_t bhc = bh * d.C + c;
@@ -806,34 +867,35 @@ __global__ void __launch_bounds__(kThreads) k_bwd_tok(Dims d, In z, In v, Out dz
       Vs[k * ldv + p] = (t < T) ? ld_tok<IO>(v, b, t, h, p) : 0.f;
     }
     __syncthreads();
-    // dz_t = (dG+dG^T) z_t + dM^T z_{t+1} + dM' z_{t-1} + dC^T v_t
-    //   dM' = dM of the chunk that owns the transition (t-1 -> t): the previous chunk
-    //   for the first token of a chunk.
+    // dz_t = (dG+dG^T) z_t + dM^T z_{t+1} + dM' z_{t-1} + dC^T v_t   (row form: z_t^T G2 + ...)
+    //   dM' is the dM of the chunk owning the transition (t-1 -> t): the previous
+    //   chunk for the first token of a chunk (fixed up below).
+    const float* Zp = Zs;
+    const float* Zc = Zs + ld;
+    const float* Zn = Zs + 2 * ld;
+    smm<false, false>(DZ, ld, Zc, ld, G2, ld, nk, r, r, 1.f, false, tid, nthr);
+    smm<false, false>(DZ, ld, Zn, ld, Ms, ld, nk, r, r, 1.f, true, tid, nthr);
+    smm<false, true>(DZ, ld, Zp, ld, Ms, ld, nk, r, r, 1.f, true, tid, nthr);
+    smm<false, false>(DZ, ld, Vs, ldv, Cs, ld, nk, r, P, 1.f, true, tid, nthr);
+    smm<false, true>(DV, ldv, Zc, ld, Cs, ld, nk, P, r, 1.f, false, tid, nthr);   // dv_t = dC z_t
+    __syncthreads();
+    if (k0 == 0 && c > 0 && tid < r) {   // first token: (dM_prev - dM) z_{t-1}
+      const int i = tid;
+      float a = 0.f;
+      for (int j = 0; j < r; ++j) a = fmaf(Mp[i * ld + j] - Ms[i * ld + j], Zp[j], a);
+      DZ[i] += a;
+    }
+    __syncthreads();
     for (int o = tid; o < nk * r; o += nthr) {
       const int k = o / r, i = o % r, t = tchunk + k0 + k;
       if (t >= T) continue;
-      const float* zc = Zs + (k + 1) * ld;
-      const float* zn = Zs + (k + 2) * ld;
-      const float* zp = Zs + k * ld;
-      const float* Mx = (k0 + k == 0) ? Mp : Ms;
-      float a = 0.f;
-      for (int j = 0; j < r; ++j) {
-        a = fmaf(G2[j * ld + i], zc[j], a);
-        a = fmaf(Ms[j * ld + i], zn[j], a);
-        a = fmaf(Mx[i * ld + j], zp[j], a);
-      }
-      for (int p = 0; p < P; ++p) a = fmaf(Cs[p * ld + i], Vs[k * ldv + p], a);
-      if (route && t == sx.tstar) a = fmaf(dmv / sx.raw, zc[i], a);
+      float a = DZ[k * ld + i];
+      if (route && t == sx.tstar) a = fmaf(dmv / sx.raw, Zc[k * ld + i], a);
       st_tok<IO>(dz, b, t, h, i, a);
     }
-    // dv_t = dC z_t
     for (int o = tid; o < nk * P; o += nthr) {
       const int k = o / P, p = o % P, t = tchunk + k0 + k;
-      if (t >= T) continue;
-      const float* zc = Zs + (k + 1) * ld;
-      float a = 0.f;
-      for (int j = 0; j < r; ++j) a = fmaf(Cs[p * ld + j], zc[j], a);
-      st_tok<IO>(dv, b, t, h, p, a);
+      if (t < T) st_tok<IO>(dv, b, t, h, p, DV[k * ldv + p]);
     }
   }
 }
@@ -844,21 +906,31 @@ __global__ void __launch_bounds__(kThreads) k_bwd_tok(Dims d, In z, In v, Out dz
 
 size_t smem_fwd_stats(const Dims& d) {
   const int ldz = odd_ld(d.r), ldv = odd_ld(d.P);
-  return ((size_t)(kStatTok + 1) * ldz + (size_t)kStatTok * ldv + 1) * sizeof(float) + 8 + 32 * 8;
+  return ((size_t)64 + (size_t)(2 * d.r + d.P) * ldz + (size_t)(kStatTok + 1) * ldz + (size_t)kStatTok * ldv) *
+         sizeof(float);
 }
 size_t smem_fwd_chunk(const Dims& d) {
-  const int ld = odd_ld(d.r), MX = d.r > d.P ? d.r : d.P;
-  return ((size_t)6 * MX * ld + (size_t)kReadTok * ld + 64) * sizeof(float);
+  const int ld = odd_ld(d.r), ldp = odd_ld(d.P), MX = d.r > d.P ? d.r : d.P;
+  return ((size_t)6 * MX * ld + (size_t)kReadTok * ld + (size_t)kReadTok * ldp + 64) * sizeof(float);
 }
 size_t smem_bwd_chunk(const Dims& d) {
   const int ld = odd_ld(d.r), ldp = odd_ld(d.P), MX = d.r > d.P ? d.r : d.P;
-  return ((size_t)9 * MX * ld + (size_t)kBwdTok * ldp + (size_t)kBwdTok * ld + 64) * sizeof(float);
+  return ((size_t)9 * MX * ld + (size_t)kBwdTok * ldp + (size_t)2 * kBwdTok * ld + 64) * sizeof(float);
 }
 size_t smem_bwd_tok(const Dims& d) {
   const int ld = odd_ld(d.r), ldv = odd_ld(d.P);
-  return ((size_t)3 * d.r * ld + (size_t)d.P * ld + (size_t)(kTokTile + 2) * ld + (size_t)kTokTile * ldv) *
-             sizeof(float) + 8 + 32 * 8;
+  return ((size_t)3 * d.r * ld + (size_t)d.P * ld + (size_t)(kTokTile + 2) * ld + (size_t)kTokTile * ldv +
+          (size_t)kTokTile * ld + (size_t)kTokTile * ldv) * sizeof(float) + 8 + 32 * 8;
 }
+
+bool warp_path_ok(const Dims& d);
+template <typename IO>
+cudaError_t launch_fwd_chunk_w(const Dims&, const In&, const float*, const Out&, const float*,
+                               const unsigned long long*, float*, int*, cudaStream_t);
+template <typename IO>
+cudaError_t launch_bwd_chunk_w(const Dims&, const In&, const In&, const float*, const Out&, const float*,
+                               const unsigned long long*, const float*, const int*, float*, float*, float*,
+                               cudaStream_t);
 
 template <typename K>
 static cudaError_t set_smem(K kernel, size_t bytes) {
@@ -880,9 +952,13 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   prof_record(0, st);
   k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
   prof_record(1, st);
-  k_scan_fwd<<<dim3((d.SW + kThreads - 1) / kThreads, d.B * d.H), kThreads, 0, st>>>(d, stats);
+  k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   prof_record(2, st);
-  k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
+  if (warp_path_ok(d)) {
+    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, y, stats, cmax, invs, flags, st)) != cudaSuccess) return e;
+  } else {
+    k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
+  }
   prof_record(3, st);
   return cudaGetLastError();
 }
@@ -905,10 +981,16 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if ((e = set_smem(k_bwd_chunk<IO>, s1)) != cudaSuccess) return e;
   if ((e = set_smem(k_bwd_tok<IO>, s3)) != cudaSuccess) return e;
   prof_record(4, st);
-  k_bwd_chunk<IO><<<grid, kThreads, s1, st>>>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart,
-                                             dgpart);
+  if (warp_path_ok(d)) {
+    if ((e = launch_bwd_chunk_w<IO>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart, dgpart,
+                                    st)) != cudaSuccess)
+      return e;
+  } else {
+    k_bwd_chunk<IO><<<grid, kThreads, s1, st>>>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart,
+                                               dgpart);
+  }
   prof_record(5, st);
-  k_scan_bwd<<<dim3((d.SW + kThreads - 1) / kThreads, d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
+  k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
                                                                                      dm, dgamma);
   prof_record(6, st);
   k_bwd_tok<IO><<<grid, kThreads, s3, st>>>(d, z, v, dz, dv, dstats, cmax, dm);

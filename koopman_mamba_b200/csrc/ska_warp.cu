@@ -1,0 +1,656 @@
+// ska_warp.cu -- warp-per-chunk SKA chunk-operator kernels for rank r <= 32.
+//
+// One warp owns one (batch, head, chunk).  The Cholesky factor, the triangular
+// inverse and the power iteration keep one matrix row per lane in registers and
+// run on shuffles; every matrix product is a warp-level tensor-core tile GEMM
+// (wmm: mma.sync TF32 with a 3-term split, fp32-level accuracy) on the warp's
+// swizzled shared-memory tiles.  There are no block barriers.
+//
+// Same algebra as the CTA path in ska_exact.cu, written with
+//   U = A^K Li,  V = Li^T U,  W = Cn V           (W = Cn Li^T A^K Li)
+// so that the backward is, besides the token contractions, r x r products only:
+//   dV = Cn^T dW, dCn = dW V^T, dU = Li dV, dLi = U dV^T + A^K^T dU,
+//   dA^K = dU Li^T, then dA, dMn, dS, dLi and dGn as in the CTA path.
+#include "ska_warp.cuh"
+
+namespace ska {
+namespace wpc {
+
+constexpr int kMaxWarps = 8;   // chunks (warps) per CTA, fewer when the tiles do not fit
+constexpr size_t kSmemBudget = 227 * 1024;
+constexpr int kTile = 1024;    // floats per 32 x 32 tile
+
+__host__ __device__ inline int p_blocks(int P) { return (P + 31) >> 5; }
+// forward tiles per warp: T0..T3, TC (P rows: Cn, then Y), TW (P rows: W / m)
+__host__ __device__ inline int fwd_tiles(int P) { return 4 + 2 * p_blocks(P); }
+// backward tiles per warp: Li, A, AK, V, X, Y, W[NPB], DY[NPB], DW[NPB]
+__host__ __device__ inline int bwd_tiles(int P) { return 6 + 3 * p_blocks(P); }
+
+__device__ __forceinline__ void build_gram_row(float (&g)[32], const float (&grow)[32], const float (&gcol)[32],
+                                               int lane, int r, float im2, float ridge, float jit) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float v;
+    if (lane < r && j < r) {
+      v = 0.5f * (grow[j] * im2 + gcol[j] * im2);   // ska.py:119,138
+      if (j == lane) v += ridge + jit;
+    } else {
+      v = (j == lane) ? 1.f : 0.f;
+    }
+    g[j] = v;
+  }
+}
+
+// Global loads are issued unconditionally from clamped (always valid) addresses and
+// masked afterwards, so that a lane's loads are all in flight together.
+
+// row `row` of the nrows x ncols row-major global matrix src, times `scale`, zero padded
+__device__ __forceinline__ void ld_gmem_row(float (&v)[32], const float* src, int row, int nrows, int ncols,
+                                            float scale) {
+  const bool rv = row < nrows;
+  const float* p = src + (size_t)(rv ? row : 0) * ncols;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    float4 x[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] = __ldg(p4 + q);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[4 * q] = rv ? x[q].x * scale : 0.f;
+      v[4 * q + 1] = rv ? x[q].y * scale : 0.f;
+      v[4 * q + 2] = rv ? x[q].z * scale : 0.f;
+      v[4 * q + 3] = rv ? x[q].w * scale : 0.f;
+    }
+  } else {
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __ldg(p + (j < ncols ? j : 0));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rv && j < ncols) ? x[j] * scale : 0.f;
+  }
+}
+
+// features [f0, f0 + n) of token t (n <= 32), times `scale`; zero when !valid
+template <typename IO>
+__device__ __forceinline__ void ld_tok_row(float (&v)[32], const In& x, int b, int t, int h, int f0, int n,
+                                           bool valid, float scale) {
+  const IO* p = static_cast<const IO*>(x.p) + (long long)b * x.sb + (long long)(valid ? t : 0) * x.st +
+                (long long)h * x.sh + f0;
+  constexpr int kVec = 16 / sizeof(IO);          // elements per 16-byte load
+  if (n == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    uint4 raw[32 / kVec];
+#pragma unroll
+    for (int q = 0; q < 32 / kVec; ++q) raw[q] = __ldg(reinterpret_cast<const uint4*>(p) + q);
+#pragma unroll
+    for (int q = 0; q < 32 / kVec; ++q) {
+      const IO* e = reinterpret_cast<const IO*>(&raw[q]);   // registers: plain reads only
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) v[q * kVec + u] = valid ? to_float(e[u]) * scale : 0.f;
+    }
+  } else {
+    float xv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) xv[j] = load_elem<IO>(p + (j < n ? j : 0));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (valid && j < n) ? xv[j] * scale : 0.f;
+  }
+}
+
+__device__ __forceinline__ void pack_store(float* dst, const float (&v)[32], int q, float scale) {
+  *reinterpret_cast<float4*>(dst) = make_float4(v[4 * q] * scale, v[4 * q + 1] * scale, v[4 * q + 2] * scale,
+                                                v[4 * q + 3] * scale);
+}
+__device__ __forceinline__ void pack_store(__nv_bfloat16* dst, const float (&v)[32], int q, float scale) {
+  __nv_bfloat162 p[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) p[u] = __floats2bfloat162_rn(v[8 * q + 2 * u] * scale, v[8 * q + 2 * u + 1] * scale);
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(p);
+}
+
+// features [f0, f0 + n) of token t <- v * scale (n <= 32), when valid
+template <typename IO>
+__device__ __forceinline__ void st_tok_row(const Out& x, int b, int t, int h, int f0, int n, bool valid,
+                                           const float (&v)[32], float scale) {
+  if (!valid) return;
+  IO* p = static_cast<IO*>(x.p) + (long long)b * x.sb + (long long)t * x.st + (long long)h * x.sh + f0;
+  constexpr int kVec = 16 / sizeof(IO);
+  if (n == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < 32 / kVec; ++q) pack_store(p + q * kVec, v, q, scale);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n) store_elem<IO>(p + j, v[j] * scale);
+  }
+}
+
+struct ChunkId {
+  long long q, bh;
+  int b, h, c;
+};
+__device__ __forceinline__ ChunkId chunk_id(const Dims& d, long long q) {
+  ChunkId id;
+  id.q = q;
+  id.c = (int)(q % d.C);
+  id.bh = q / d.C;
+  id.h = (int)(id.bh % d.H);
+  id.b = (int)(id.bh / d.H);
+  return id;
+}
+
+__device__ __forceinline__ float series_norm(const unsigned long long* cmax, const ChunkId& id, int C, int lane) {
+  unsigned long long key = 0ull;
+  for (int cc = lane; cc < C; cc += 32) {
+    const unsigned long long x = cmax[id.bh * C + cc];
+    key = x > key ? x : key;
+  }
+  key = warp_max_u64(key);
+  return fmaxf(unpack_norm(key), kNormClamp);
+}
+
+// this lane's row of the identity -> tile T
+__device__ __forceinline__ void st_identity(float* T, int lane) {
+  float e[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) e[j] = (j == lane) ? 1.f : 0.f;
+  st_row(T, lane, e);
+}
+
+// Gram factor and inverse.  Loads the raw G (scratch tile Tg), builds Gn, factors
+// it (jitter retry as ska.py:140-145, or jitter forced), and writes Li rows into TLi.
+// Returns the jitter flags.
+__device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec, int lane, float im2,
+                                                 bool force_jitter, float* Tg, float* TLi) {
+  const int r = d.r;
+  {
+    float graw[32];
+    ld_gmem_row(graw, rec, lane, r, r, 1.f);
+    st_row(Tg, lane, graw);
+  }
+  __syncwarp();
+  float g[32];
+  int flag = 0;
+  {
+    float grow[32], gcol[32];
+    ld_row(grow, Tg, lane);
+    ld_col<32>(gcol, Tg, lane);
+    // attempt 0: plain (or jittered when forced); attempt 1: jittered (ska.py:140-145)
+    bool jit = force_jitter;
+#pragma unroll 1
+    for (int attempt = 0; attempt < 2; ++attempt) {
+      build_gram_row(g, grow, gcol, lane, r, im2, d.ridge, jit ? kJitter : 0.f);
+      if (jit) flag |= 1;
+      if (chol32(g, lane)) break;
+      if (jit) {
+        flag |= 2;
+        break;
+      }
+      jit = true;
+    }
+  }
+  float x[32];
+  trinv32(g, x, lane);
+  st_col<32>(TLi, lane, x);                 // Li rows
+  __syncwarp();
+  return flag;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+template <typename IO, int NPB>
+__global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, const float* __restrict__ gamma_p,
+                                                                Out y, const float* __restrict__ stats,
+                                                                const unsigned long long* __restrict__ cmax,
+                                                                float* __restrict__ invs_out,
+                                                                int* __restrict__ flags_out) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
+  if (q >= (long long)d.B * d.H * d.C) return;   // warp-uniform; no block barriers below
+  const ChunkId id = chunk_id(d, q);
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T;
+  extern __shared__ float4 sm4[];
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * (4 + 2 * NPB) * kTile;
+  float* T0 = base;
+  float* T1 = T0 + kTile;
+  float* T2 = T1 + kTile;
+  float* T3 = T2 + kTile;
+  float* TC = T3 + kTile;                   // NPB tiles: Cn rows, later Y blocks
+  float* TW = TC + NPB * kTile;             // NPB tiles: (W / m) rows
+  const float* rec = stats + q * d.SW;
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
+
+  const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1);   // T1 = Li
+  if (lane == 0) flags_out[q] = flag;
+  wmm<32, 32, true, false, false, true>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
+  {
+    float mrow[32];
+    ld_gmem_row(mrow, rec + r * r, lane, r, r, im2);
+    st_row(T0, lane, mrow);                                               // T0 = Mn
+  }
+  __syncwarp();
+  wmm<32, 32, false, false, false, true>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
+  __syncwarp();
+  {
+    float a[32];
+    ld_row(a, T3, lane);
+    const float sigma = power_sigma32(a, lane, r);                        // ska.py:41-58
+    const float invs = 1.f / fmaxf(sigma, 1.f);
+    if (lane == 0) invs_out[q] = invs;
+    const float kk = gs * invs;                                           // ska.py:167-169
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a[j] *= kk;
+    __syncwarp();
+    st_row(T3, lane, a);                                                  // T3 = A
+  }
+  __syncwarp();
+  // A^K (K = 0: identity), ping-pong in T0 / T2
+  const float* AK = T3;
+  if (d.K == 0) {
+    st_identity(T0, lane);
+    AK = T0;
+  }
+  for (int s = 1; s < d.K; ++s) {
+    float* out = (AK == T0) ? T2 : T0;
+    wmm<32, 32, false, false, false, true>(out, AK, kTile, T3, 1.f);
+    __syncwarp();
+    AK = out;
+  }
+  __syncwarp();
+  float* TU = (AK == T0) ? T2 : T0;
+  float* TV = (d.K == 1) ? T2 : T3;
+  wmm<32, 32, false, false, false, true>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
+  __syncwarp();
+  wmm<32, 32, true, false, false, true>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
+#pragma unroll
+  for (int pb = 0; pb < NPB; ++pb) {
+    float crow[32];
+    ld_gmem_row(crow, rec + 2 * r * r, pb * 32 + lane, P, r, im);
+    st_row(TC + pb * kTile, lane, crow);                                  // Cn rows
+  }
+  __syncwarp();
+  wmm<32 * NPB, 32, false, false, false, true>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
+  __syncwarp();
+
+  // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T
+  const int tchunk = id.c * CS;
+  for (int t0 = 0; t0 < CS; t0 += 32) {
+    const int tl = t0 + lane, tok = tchunk + tl;
+    const bool live = tl < CS && tok < T;
+    {
+      float qr[32];
+      ld_tok_row<IO>(qr, zq, id.b, tok, id.h, 0, r, live, 1.f);
+      st_row(T0, lane, qr);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int pb = 0; pb < NPB; ++pb)
+      wmm<32, 32, false, true, false, true>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
+    __syncwarp();
+#pragma unroll
+    for (int pb = 0; pb < NPB; ++pb) {
+      float yr[32];
+      ld_row(yr, TC + pb * kTile, lane);
+      st_tok_row<IO>(y, id.b, tok, id.h, pb * 32, min(32, P - pb * 32), live, yr, 1.f);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+template <typename IO, int NPB>
+__global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, In dy,
+                                                                const float* __restrict__ gamma_p, Out dzq,
+                                                                const float* __restrict__ stats,
+                                                                const unsigned long long* __restrict__ cmax,
+                                                                const float* __restrict__ invs_in,
+                                                                const int* __restrict__ flags_in,
+                                                                float* __restrict__ dstats,
+                                                                float* __restrict__ dmpart,
+                                                                float* __restrict__ dgpart) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
+  if (q >= (long long)d.B * d.H * d.C) return;
+  const ChunkId id = chunk_id(d, q);
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T;
+  extern __shared__ float4 sm4[];
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * (6 + 3 * NPB) * kTile;
+  float* TLi = base;
+  float* TA = TLi + kTile;
+  float* TAK = TA + kTile;
+  float* TV = TAK + kTile;
+  float* TX = TV + kTile;
+  float* TY = TX + kTile;
+  float* TW = TY + kTile;                   // NPB tiles: W rows, then dCn rows, then dLi
+  float* TDY = TW + NPB * kTile;            // NPB tiles: Cn rows / dY column blocks
+  float* TDW = TDY + NPB * kTile;           // NPB tiles: dW rows
+  const float* rec = stats + q * d.SW;
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const float gam = *gamma_p;
+  const float gs = fminf(fmaxf(gam, 1.f), 1.5f);
+  const bool gpass = gam >= 1.f && gam <= 1.5f;       // clamp passes gradients inclusively
+  const float kk = gs * invs_in[q];
+  const int flag = flags_in[q];
+  float t[32], u[32];
+
+  // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
+  factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
+  wmm<32, 32, true, false, false, true>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  ld_gmem_row(t, rec + r * r, lane, r, r, im2);
+  st_row(TX, lane, t);                                                    // TX = Mn
+  __syncwarp();
+  wmm<32, 32, false, false, false, true>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  __syncwarp();
+  ld_row(t, TA, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] *= kk;
+  __syncwarp();
+  st_row(TA, lane, t);                                                    // TA = A
+  __syncwarp();
+  const float* AK = TAK;
+  if (d.K == 0) {
+    st_identity(TAK, lane);
+  } else if (d.K == 1) {
+    AK = TA;
+  } else {
+    const float* cur = TA;
+    for (int s = 1; s < d.K; ++s) {
+      float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
+      wmm<32, 32, false, false, false, true>(out, cur, kTile, TA, 1.f);
+      __syncwarp();
+      cur = out;
+    }
+  }
+  __syncwarp();
+  wmm<32, 32, false, false, false, true>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  __syncwarp();
+  wmm<32, 32, true, false, false, true>(TV, TLi, kTile, TX, 1.f);       // TV = V
+#pragma unroll
+  for (int pb = 0; pb < NPB; ++pb) {
+    ld_gmem_row(t, rec + 2 * r * r, pb * 32 + lane, P, r, im);
+    st_row(TDY + pb * kTile, lane, t);                                    // Cn rows
+    zero(t);
+    st_row(TDW + pb * kTile, lane, t);                                    // dW = 0
+  }
+  __syncwarp();
+  wmm<32 * NPB, 32, false, false, false, true>(TW, TDY, kTile, TV, 1.f);  // W = Cn V
+  __syncwarp();
+
+  // ---- token pass: dW += dY^T qn, dqn = dY W  (32 tokens at a time) ----
+  const int tchunk = id.c * CS;
+  float dmq = 0.f;
+  for (int t0 = 0; t0 < CS; t0 += 32) {
+    const int tl = t0 + lane, tok = tchunk + tl;
+    const bool live = tl < CS && tok < T;
+    ld_tok_row<IO>(u, zq, id.b, tok, id.h, 0, r, live, im);             // qn row (kept for dm)
+    st_row(TX, lane, u);
+#pragma unroll
+    for (int pb = 0; pb < NPB; ++pb) {
+      ld_tok_row<IO>(t, dy, id.b, tok, id.h, pb * 32, min(32, P - pb * 32), live, 1.f);
+      st_row(TDY + pb * kTile, lane, t);                                  // dY column block pb
+    }
+    __syncwarp();
+    wmm<32 * NPB, 32, true, false, true, true>(TDW, TDY, kTile, TX, 1.f);  // dW += dY^T qn
+    wmm<32, 32 * NPB, false, false, false, true>(TY, TDY, kTile, TW, 1.f);  // dqn = dY W
+    __syncwarp();
+    ld_row(t, TY, lane);
+    st_tok_row<IO>(dzq, id.b, tok, id.h, 0, r, live, t, im);             // dzq = dqn / m
+    if (live) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) dmq = fmaf(t[j], u[j], dmq);
+    }
+    __syncwarp();
+  }
+
+  // ---- dV = Cn^T dW,  dCn = dW V^T ----
+#pragma unroll
+  for (int pb = 0; pb < NPB; ++pb) {
+    ld_gmem_row(t, rec + 2 * r * r, pb * 32 + lane, P, r, im);
+    st_row(TDY + pb * kTile, lane, t);                                    // Cn rows again
+  }
+  __syncwarp();
+  wmm<32, 32 * NPB, true, false, false, true>(TX, TDY, kTile, TDW, 1.f);  // TX = dV
+  wmm<32 * NPB, 32, false, true, false, true>(TW, TDW, kTile, TV, 1.f);   // TW = dCn
+  __syncwarp();
+  float dmc = 0.f;
+#pragma unroll
+  for (int pb = 0; pb < NPB; ++pb) {
+    const int p = pb * 32 + lane;
+    ld_row(t, TW + pb * kTile, lane);
+    ld_row(u, TDY + pb * kTile, lane);
+    if (p < P) {
+      float* out = dstats + q * d.SW + 2 * r * r + (size_t)p * r;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < r) {
+          out[j] = t[j] * im;
+          dmc = fmaf(t[j], u[j], dmc);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  // free now: TW, TDY, TDW, TV ; live: TLi, TA, AK, TX (dV)
+  float* TdLi = TW;
+  float* TdU = TY;
+  float* TU = TDW;
+  float* TdAK = TDY;
+  wmm<32, 32, false, false, false, true>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmm<32, 32, false, false, false, true>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  __syncwarp();
+  wmm<32, 32, false, true, false, true>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmm<32, 32, false, true, false, true>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  __syncwarp();
+  wmm<32, 32, true, false, true, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  __syncwarp();
+  // dA from dAK; free: TV, TX, TY, TDW
+  const float* TdA;
+  if (d.K == 0) {
+    zero(t);
+    st_row(TV, lane, t);
+    TdA = TV;
+  } else if (d.K == 1) {
+    TdA = TdAK;
+  } else {
+    // Horner over E_s = dAK (A^T)^s:  E <- E A^T,  H <- E + A^T H,  E = H = dAK at start
+    float* pool[4] = {TV, TX, TY, TDW};
+    const float* E = TdAK;
+    const float* Hc = TdAK;
+    int pi = 0;
+    for (int s = 1; s < d.K; ++s) {
+      float* En = pool[pi & 3];
+      float* Hn = pool[(pi + 1) & 3];
+      pi += 2;
+      wmm<32, 32, false, true, false, true>(En, E, kTile, TA, 1.f);      // E A^T
+      __syncwarp();
+      ld_row(t, En, lane);
+      st_row(Hn, lane, t);
+      __syncwarp();
+      wmm<32, 32, true, false, true, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      __syncwarp();
+      E = En;
+      Hc = Hn;
+    }
+    TdA = Hc;
+  }
+  // d gamma: A = gs * invs * A0  ->  d gs = <dA, A> / gs
+  float dg = 0.f;
+  ld_row(t, TdA, lane);
+  ld_row(u, TA, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) dg = fmaf(t[j], u[j], dg);
+  // scratch tiles now: three of {TV, TX, TY, TDW, TdAK} not holding dA
+  float* fr[3];
+  {
+    float* cand[5] = {TV, TX, TY, TDW, TdAK};
+    int nf = 0;
+    for (int i = 0; i < 5 && nf < 3; ++i)
+      if (cand[i] != TdA) fr[nf++] = cand[i];
+  }
+  float* TS = fr[0];
+  float* TdMn = fr[1];
+  float* TdS = fr[2];
+  __syncwarp();
+  wmm<32, 32, true, false, false, true>(TS, TLi, kTile, TLi, 1.f);       // S
+  __syncwarp();
+  wmm<32, 32, false, false, false, true>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  __syncwarp();
+  float dmm = 0.f;
+  ld_row(t, TdMn, lane);
+  ld_gmem_row(u, rec + r * r, lane, r, r, im2);                           // Mn row
+  if (lane < r) {
+    float* out = dstats + q * d.SW + r * r + (size_t)lane * r;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < r) {
+        out[j] = t[j] * im2;
+        dmm = fmaf(t[j], u[j], dmm);
+      }
+    }
+  }
+  st_row(TS, lane, u);                                                    // TS = Mn (S done)
+  __syncwarp();
+  wmm<32, 32, true, false, false, true>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  __syncwarp();
+  ld_row(t, TdS, lane);
+  ld_col<32>(u, TdS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
+  st_row(TdMn, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, false, true, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  __syncwarp();
+  ld_row(t, TdLi, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
+  st_row(TdLi, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, true, false, true>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  __syncwarp();
+  ld_row(t, TS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j > lane) t[j] = 0.f;                                             // Pm = tril(-dLi Li^T)
+  __syncwarp();
+  st_row(TS, lane, t);
+  __syncwarp();
+  ld_col<32>(u, TS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
+  st_row(TdS, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, false, false, true>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  __syncwarp();
+  wmm<32, 32, true, false, false, true>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  __syncwarp();
+  ld_row(t, TdS, lane);
+  ld_col<32>(u, TdS, lane);
+  float grow[32];
+  ld_gmem_row(grow, rec, lane, r, r, 1.f);
+  __syncwarp();
+  st_row(TS, lane, grow);
+  __syncwarp();
+  float gcol[32];
+  ld_col<32>(gcol, TS, lane);
+  float dmg = 0.f;
+  if (lane < r) {
+    float* out = dstats + q * d.SW + (size_t)lane * r;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < r) {
+        const float gsym = 0.5f * (t[j] + u[j]);
+        out[j] = gsym * im2;
+        dmg = fmaf(gsym, 0.5f * (grow[j] + gcol[j]) * im2, dmg);
+      }
+    }
+  }
+  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq);
+  const float dgs = warp_sum32(dg);
+  if (lane == 0) {
+    dmpart[q] = -tot / m;
+    dgpart[q] = gpass ? dgs / gs : 0.f;
+  }
+}
+
+}  // namespace wpc
+
+// ---------------------------------------------------------------------------
+// host launch helpers
+// ---------------------------------------------------------------------------
+bool warp_path_ok(const Dims& d) { return d.r <= 32 && d.P <= 128; }
+
+static int warps_for(size_t per_warp) {
+  const int n = (int)(wpc::kSmemBudget / per_warp);
+  return n < wpc::kMaxWarps ? n : wpc::kMaxWarps;
+}
+static size_t fwd_warp_bytes(const Dims& d) { return (size_t)wpc::fwd_tiles(d.P) * wpc::kTile * sizeof(float); }
+static size_t bwd_warp_bytes(const Dims& d) { return (size_t)wpc::bwd_tiles(d.P) * wpc::kTile * sizeof(float); }
+// bytes for one warp's tiles; 0 when even one warp does not fit
+size_t smem_fwd_chunk_w(const Dims& d) { return warps_for(fwd_warp_bytes(d)) > 0 ? fwd_warp_bytes(d) : 0; }
+size_t smem_bwd_chunk_w(const Dims& d) { return warps_for(bwd_warp_bytes(d)) > 0 ? bwd_warp_bytes(d) : 0; }
+
+template <typename Kern>
+static cudaError_t launch_w(Kern kern, const Dims& d, size_t per_warp, cudaStream_t st, void** args) {
+  const int nw = warps_for(per_warp);
+  const size_t smem = (size_t)nw * per_warp;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const long long nq = (long long)d.B * d.H * d.C;
+  const unsigned grid = (unsigned)((nq + nw - 1) / nw);
+  e = cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(nw * 32), args, smem, st);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <typename IO>
+cudaError_t launch_fwd_chunk_w(const Dims& d, const In& zq, const float* gamma, const Out& y, const float* stats,
+                               const unsigned long long* cmax, float* invs, int* flags, cudaStream_t st) {
+  Dims dd = d;
+  In zz = zq;
+  Out yy = y;
+  void* args[] = {&dd, &zz, (void*)&gamma, &yy, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags};
+  const size_t pw = fwd_warp_bytes(d);
+  switch (wpc::p_blocks(d.P)) {
+    case 1: return launch_w(wpc::k_fwd_chunk_w<IO, 1>, d, pw, st, args);
+    case 2: return launch_w(wpc::k_fwd_chunk_w<IO, 2>, d, pw, st, args);
+    case 3: return launch_w(wpc::k_fwd_chunk_w<IO, 3>, d, pw, st, args);
+    default: return launch_w(wpc::k_fwd_chunk_w<IO, 4>, d, pw, st, args);
+  }
+}
+
+template <typename IO>
+cudaError_t launch_bwd_chunk_w(const Dims& d, const In& zq, const In& dy, const float* gamma, const Out& dzq,
+                               const float* stats, const unsigned long long* cmax, const float* invs,
+                               const int* flags, float* dstats, float* dmpart, float* dgpart, cudaStream_t st) {
+  Dims dd = d;
+  In zz = zq, yy = dy;
+  Out oo = dzq;
+  void* args[] = {&dd, &zz, &yy, (void*)&gamma, &oo, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags,
+                  (void*)&dstats, (void*)&dmpart, (void*)&dgpart};
+  const size_t pw = bwd_warp_bytes(d);
+  switch (wpc::p_blocks(d.P)) {
+    case 1: return launch_w(wpc::k_bwd_chunk_w<IO, 1>, d, pw, st, args);
+    case 2: return launch_w(wpc::k_bwd_chunk_w<IO, 2>, d, pw, st, args);
+    case 3: return launch_w(wpc::k_bwd_chunk_w<IO, 3>, d, pw, st, args);
+    default: return launch_w(wpc::k_bwd_chunk_w<IO, 4>, d, pw, st, args);
+  }
+}
+
+template cudaError_t launch_fwd_chunk_w<float>(const Dims&, const In&, const float*, const Out&, const float*,
+                                               const unsigned long long*, float*, int*, cudaStream_t);
+template cudaError_t launch_fwd_chunk_w<__nv_bfloat16>(const Dims&, const In&, const float*, const Out&,
+                                                       const float*, const unsigned long long*, float*, int*,
+                                                       cudaStream_t);
+template cudaError_t launch_bwd_chunk_w<float>(const Dims&, const In&, const In&, const float*, const Out&,
+                                               const float*, const unsigned long long*, const float*, const int*,
+                                               float*, float*, float*, cudaStream_t);
+template cudaError_t launch_bwd_chunk_w<__nv_bfloat16>(const Dims&, const In&, const In&, const float*,
+                                                       const Out&, const float*, const unsigned long long*,
+                                                       const float*, const int*, float*, float*, float*,
+                                                       cudaStream_t);
+
+}  // namespace ska

@@ -1,0 +1,314 @@
+// ska_warp.cuh -- register-resident warp primitives for the per-chunk SKA algebra
+// (rank r <= 32).  One warp owns one chunk; lane i owns row i of every r x r
+// matrix (rows past r are padding: identity for the Gram factor, zero elsewhere,
+// which leaves every real entry unchanged).
+//
+// Shared-memory tiles are 32 x 32 fp32, row-major with a 16-byte-chunk XOR
+// swizzle (chunk q of row k stored at chunk q ^ (k & 7)): a lane writing its
+// own row with 128-bit stores and a warp reading one row as a broadcast are
+// both conflict-free, and so is a warp reading one column.
+#pragma once
+
+#include "ska_common.cuh"
+
+namespace ska {
+namespace wpc {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float shfl(float v, int src) { return __shfl_sync(kFull, v, src); }
+
+__device__ __forceinline__ int swz(int row, int col) {
+  return row * 32 + ((((col >> 2) ^ (row & 7)) << 2) | (col & 3));
+}
+
+// this lane's 32-float register row -> row `row` of tile T
+__device__ __forceinline__ void st_row(float* T, int row, const float (&v)[32]) {
+  float4* p = reinterpret_cast<float4*>(T + row * 32);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) p[q ^ (row & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+__device__ __forceinline__ void ld_row(float (&v)[32], const float* T, int row) {
+  const float4* p = reinterpret_cast<const float4*>(T + row * 32);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 x = p[q ^ (row & 7)];
+    v[4 * q] = x.x;
+    v[4 * q + 1] = x.y;
+    v[4 * q + 2] = x.z;
+    v[4 * q + 3] = x.w;
+  }
+}
+// column `col` of tile T (K rows) -> v[0..K)
+template <int K>
+__device__ __forceinline__ void ld_col(float (&v)[K], const float* T, int col) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) v[k] = T[swz(k, col)];
+}
+// this lane's register row written as COLUMN `col` of tile T (K rows)
+template <int K>
+__device__ __forceinline__ void st_col(float* T, int col, const float (&v)[K]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) T[swz(k, col)] = v[k];
+}
+
+// (d0, d1) += (a0, a1) * (b0, b1) as one packed fp32x2 FMA (sm_100)
+__device__ __forceinline__ void fma2p(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  unsigned long long dd, bb, aa;
+  float2 dv = make_float2(d0, d1), bv = make_float2(b0, b1), av = make_float2(a0, a1);
+  dd = *reinterpret_cast<unsigned long long*>(&dv);
+  bb = *reinterpret_cast<unsigned long long*>(&bv);
+  aa = *reinterpret_cast<unsigned long long*>(&av);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(dd) : "l"(aa), "l"(bb));
+  dv = *reinterpret_cast<float2*>(&dd);
+  d0 = dv.x;
+  d1 = dv.y;
+}
+
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a, float b0, float b1) {
+  unsigned long long dd, bb, aa;
+  float2 dv = make_float2(d0, d1), bv = make_float2(b0, b1), av = make_float2(a, a);
+  dd = *reinterpret_cast<unsigned long long*>(&dv);
+  bb = *reinterpret_cast<unsigned long long*>(&bv);
+  aa = *reinterpret_cast<unsigned long long*>(&av);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(dd) : "l"(aa), "l"(bb));
+  dv = *reinterpret_cast<float2*>(&dd);
+  d0 = dv.x;
+  d1 = dv.y;
+}
+
+// Compiler-only fence: keeps fully unrolled loops from hoisting every shared-memory
+// load ahead of the arithmetic (which would need ~1000 live registers).
+__device__ __forceinline__ void sched_fence() { asm volatile("" ::: "memory"); }
+
+// acc[j] += sum_{k<K} a[k] T[k][j]  (T: K rows of a swizzled 32-column tile, read as broadcasts)
+template <int K>
+__device__ __forceinline__ void mac_tile(float (&acc)[32], const float (&a)[K], const float* T) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if ((k & 1) == 0) sched_fence();
+    const float4* row = reinterpret_cast<const float4*>(T + k * 32);
+    const float ak = a[k];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = row[q ^ (k & 7)];
+      fma2(acc[4 * q], acc[4 * q + 1], ak, b.x, b.y);
+      fma2(acc[4 * q + 2], acc[4 * q + 3], ak, b.z, b.w);
+    }
+  }
+}
+
+// out[j] = sum_{k<32} a[k] T[j][k]  (a times T^T; T rows read as broadcasts)
+__device__ __forceinline__ void dot_rows(float (&out)[32], const float (&a)[32], const float* T) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if ((j & 1) == 0) sched_fence();
+    const float4* row = reinterpret_cast<const float4*>(T + j * 32);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = row[q ^ (j & 7)];
+      fma2p(s0, s1, a[4 * q], a[4 * q + 1], b.x, b.y);
+      fma2p(s0, s1, a[4 * q + 2], a[4 * q + 3], b.z, b.w);
+    }
+    out[j] = s0 + s1;
+  }
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long y = __shfl_xor_sync(kFull, x, o);
+    x = y > x ? y : x;
+  }
+  return x;
+}
+
+template <int N>
+__device__ __forceinline__ void zero(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = 0.f;
+}
+
+__device__ __forceinline__ float warp_sum32(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
+  return x;
+}
+
+// In-place Cholesky of the 32 x 32 matrix whose row `lane` is g (lower part read):
+// on success g = row `lane` of L with zero upper part.  Returns false at the first
+// non-positive pivot (uniform), like potrf's info > 0 (ska.py:140).  Right-looking:
+// column j is final after step j; the trailing update takes L[k][j] from lane k.
+__device__ __forceinline__ bool chol32(float (&g)[32], int lane) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float djj = shfl(g[j], j);
+    if (!(djj > 0.f)) return false;
+    const float ljj = sqrtf(djj);
+    const float inv = 1.f / ljj;
+    const float lij = lane > j ? g[j] * inv : (lane == j ? ljj : 0.f);
+    g[j] = lij;
+#pragma unroll
+    for (int k = j + 1; k < 32; ++k) g[k] = fmaf(-lij, shfl(lij, k), g[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    if (k > lane) g[k] = 0.f;
+  return true;
+}
+
+// x = column `lane` of L^{-1} (x[i] = Li[i][lane]); l = row `lane` of L.
+// Right-looking forward substitution of L x = e_lane: after step i, x[i] is final
+// and is eliminated from every later row, so the dependent chain per step is one
+// multiply and one FMA (the shuffled L entries do not depend on x).
+__device__ __forceinline__ void trinv32(const float (&l)[32], float (&x)[32], int lane) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.f : 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    x[i] = x[i] / shfl(l[i], i);
+#pragma unroll
+    for (int k = i + 1; k < 32; ++k) x[k] = fmaf(-shfl(l[i], k), x[i], x[k]);
+  }
+}
+
+// one halving step of the butterfly reduce-scatter: keep half N of the live
+// entries t[0..2N), exchange the other half with lane ^ OFF
+template <int N, int OFF>
+__device__ __forceinline__ void rs_step(float (&t)[32], int lane) {
+  const bool up = (lane & OFF) != 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const float send = up ? t[i] : t[i + N];
+    const float keep = up ? t[i + N] : t[i];
+    t[i] = keep + __shfl_xor_sync(kFull, send, OFF);
+  }
+}
+// out_lane = sum over lanes j of t_j[lane]  (butterfly reduce-scatter, 31 shuffles)
+__device__ __forceinline__ float reduce_scatter32(float (&t)[32], int lane) {
+  rs_step<16, 16>(t, lane);
+  rs_step<8, 8>(t, lane);
+  rs_step<4, 4>(t, lane);
+  rs_step<2, 2>(t, lane);
+  rs_step<1, 1>(t, lane);
+  return t[0];
+}
+
+// sigma_max estimate of ska.py:41-58: 6 power iterations from v = 1/sqrt(r) on the
+// matrix whose row `lane` is a (zero rows/cols past r).
+__device__ __forceinline__ float power_sigma32(const float (&a)[32], int lane, int r) {
+  float v = lane < r ? 1.f / sqrtf((float)r) : 0.f;
+  float u = 0.f;
+#pragma unroll 1
+  for (int it = 0; it <= kPowerIters; ++it) {
+    u = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) u = fmaf(a[j], shfl(v, j), u);
+    if (it == kPowerIters) break;
+    u = u / fmaxf(sqrtf(warp_sum32(u * u)), kPowerEps);
+    float t[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t[i] = u * a[i];
+    const float w = reduce_scatter32(t, lane);
+    v = w / fmaxf(sqrtf(warp_sum32(w * w)), kPowerEps);
+  }
+  return sqrtf(warp_sum32(u * u));
+}
+
+// ---- tensor-core readout helpers (mma.sync m16n8k8 TF32) ----
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32_acc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- warp-level tile GEMM on tensor cores (mma.sync m16n8k8 TF32) ----
+//
+// C[M x 32] (=|+=) alpha * op(A)[M x K] op(B)[K x 32], all swizzled tiles (rows of
+// 32 floats; "tall" operands are consecutive tiles, i.e. more rows):
+//   op(A)(i,k) = TA ? A[(i >> 5) * SA + swz(k, i & 31)]   (A stored K x M in 32-col blocks)
+//                   : A[(k >> 5) * SA + swz(i, k & 31)]   (A stored M x K in 32-col blocks)
+//   op(B)(k,j) = TB ? B[swz(j, k)]  (B stored 32 x K, K <= 32) : B[swz(k, j)]  (tall)
+//   C(i,j)     = C[swz(i, j)]
+// SPLIT: x = hi + lo (hi = tf32(x), lo = tf32(x - hi)) and a*b ~= hl*hb + ha*lb + la*hb,
+// i.e. fp32-level products.  C may not alias A or B.  All 32 lanes must call.
+// Not inlined: one copy per shape keeps the kernels small enough for the
+// instruction cache (inlining every call site made instruction fetch the main stall).
+template <int M, int K, bool TA, bool TB, bool ACC, bool SPLIT>
+__device__ __noinline__ void wmm(float* __restrict__ C, const float* __restrict__ A, int SA,
+                                 const float* __restrict__ B, float alpha) {
+  static_assert(M % 16 == 0 && K % 8 == 0, "tile shape");
+  static_assert(!TB || K <= 32, "transposed B holds 32 x K");
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+#pragma unroll 1
+  for (int i0 = 0; i0 < M; i0 += 16) {
+    float d[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) d[n][0] = d[n][1] = d[n][2] = d[n][3] = 0.f;
+#pragma unroll 2
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      const int ra = i0 + g, rb = i0 + g + 8, ka = k0 + t4, kb = k0 + t4 + 4;
+      float av[4];
+      if (TA) {
+        av[0] = A[(ra >> 5) * SA + swz(ka, ra & 31)];
+        av[1] = A[(rb >> 5) * SA + swz(ka, rb & 31)];
+        av[2] = A[(ra >> 5) * SA + swz(kb, ra & 31)];
+        av[3] = A[(rb >> 5) * SA + swz(kb, rb & 31)];
+      } else {
+        av[0] = A[(ka >> 5) * SA + swz(ra, ka & 31)];
+        av[1] = A[(ka >> 5) * SA + swz(rb, ka & 31)];
+        av[2] = A[(kb >> 5) * SA + swz(ra, kb & 31)];
+        av[3] = A[(kb >> 5) * SA + swz(rb, kb & 31)];
+      }
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ah[u] = tf32_bits(av[u]);
+        al[u] = SPLIT ? tf32_bits(av[u] - __uint_as_float(ah[u])) : 0u;
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int col = n * 8 + g;
+        const float b0 = TB ? B[swz(col, ka)] : B[swz(ka, col)];
+        const float b1 = TB ? B[swz(col, kb)] : B[swz(kb, col)];
+        const uint32_t bh0 = tf32_bits(b0), bh1 = tf32_bits(b1);
+        if (SPLIT) {
+          mma_tf32_acc(d[n], al, bh0, bh1);
+          mma_tf32_acc(d[n], ah, tf32_bits(b0 - __uint_as_float(bh0)), tf32_bits(b1 - __uint_as_float(bh1)));
+        }
+        mma_tf32_acc(d[n], ah, bh0, bh1);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int col = n * 8 + 2 * t4;
+      const int r0 = i0 + g, r1 = i0 + g + 8;
+      float* c00 = C + swz(r0, col);
+      float* c01 = C + swz(r0, col + 1);
+      float* c10 = C + swz(r1, col);
+      float* c11 = C + swz(r1, col + 1);
+      if (ACC) {
+        *c00 += alpha * d[n][0];
+        *c01 += alpha * d[n][1];
+        *c10 += alpha * d[n][2];
+        *c11 += alpha * d[n][3];
+      } else {
+        *c00 = alpha * d[n][0];
+        *c01 = alpha * d[n][1];
+        *c10 = alpha * d[n][2];
+        *c11 = alpha * d[n][3];
+      }
+    }
+  }
+}
+
+}  // namespace wpc
+}  // namespace ska
