@@ -133,6 +133,28 @@ int ska_bwd(const SkaShape* shape, int io_dtype,
 #define SKA_PROFILE_EVENTS 8
 int ska_set_profile_events(void* const* events, int count);
 
+/* Forward with no allocation anywhere (no counterpart in the reference, whose
+ * PyTorch path always allocates through the caching allocator).  Same
+ * computation and arguments as ska_fwd, minus the `saved` buffer: the
+ * workspace is a fixed array of SKA_NOALLOC_SCRATCH_BYTES compiled into this
+ * library as device memory, which every GPU that loads the library holds until
+ * the process exits.  It serves callers that cannot call cudaMalloc: FFI hosts
+ * with no CUDA allocator of their own, and inference loops that must not
+ * allocate between launches (cudaMalloc can synchronise the device).
+ *   - Problems whose ska_workspace_size saved_bytes exceed
+ *     SKA_NOALLOC_SCRATCH_BYTES return SKA_ERR_WORKSPACE and launch nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share the one array and it keeps the previous call's contents
+ *     (every part of it that is read is rewritten first).  Calls whose work
+ *     overlaps on the GPU race on it: serialise them, e.g. on one stream.
+ *   - Forward only: ska_bwd still needs the `saved` buffer of ska_fwd. */
+#define SKA_NOALLOC_SCRATCH_BYTES (16u << 20)
+int ska_fwd_noalloc(const SkaShape* shape, int io_dtype,
+                    const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+                    const float* gamma, const SkaTensor* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,7 +26,9 @@ EXPORTED = (
     "ska_fwd",
     "ska_bwd",
     "ska_set_profile_events",
+    "ska_fwd_noalloc",
 )
+SKA_NOALLOC_SCRATCH_BYTES = 16 << 20
 SKA_PROFILE_EVENTS = 8
 
 
@@ -84,6 +86,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.ska_bwd.restype = ctypes.c_int
     L.ska_set_profile_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
     L.ska_set_profile_events.restype = ctypes.c_int
+    L.ska_fwd_noalloc.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), P(SkaTensor),
+                                  ctypes.c_void_p, P(SkaTensor), ctypes.c_void_p]
+    L.ska_fwd_noalloc.restype = ctypes.c_int
 
 
 def lib() -> ctypes.CDLL:
