@@ -16,6 +16,10 @@
 namespace ska {
 namespace wpc {
 
+// tokens stored as bf16 are exact in tf32, so the tensor-core products need not split them
+template <typename IO> constexpr bool kIoExact = false;
+template <> constexpr bool kIoExact<__nv_bfloat16> = true;
+
 constexpr int kMaxWarps = 8;   // chunks (warps) per CTA, fewer when the tiles do not fit
 constexpr size_t kSmemBudget = 227 * 1024;
 constexpr int kTile = 1024;    // floats per 32 x 32 tile
@@ -168,7 +172,7 @@ __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec
     st_row(Tg, lane, graw);
   }
   __syncwarp();
-  float g[32];
+  float g[32], x[32];
   int flag = 0;
   {
     float grow[32], gcol[32];
@@ -180,7 +184,7 @@ __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec
     for (int attempt = 0; attempt < 2; ++attempt) {
       build_gram_row(g, grow, gcol, lane, r, im2, d.ridge, jit ? kJitter : 0.f);
       if (jit) flag |= 1;
-      if (chol32(g, lane)) break;
+      if (chol_inv32(g, x, lane)) break;
       if (jit) {
         flag |= 2;
         break;
@@ -188,8 +192,6 @@ __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec
       jit = true;
     }
   }
-  float x[32];
-  trinv32(g, x, lane);
   st_col<32>(TLi, lane, x);                 // Li rows
   __syncwarp();
   return flag;
@@ -223,14 +225,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
 
   const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
-  wmm<32, 32, true, false, false, true>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
+  wmm<32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
   {
     float mrow[32];
     ld_gmem_row(mrow, rec + r * r, lane, r, r, im2);
     st_row(T0, lane, mrow);                                               // T0 = Mn
   }
   __syncwarp();
-  wmm<32, 32, false, false, false, true>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
+  wmm<32, 32, false, false, false>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
   __syncwarp();
   {
     float a[32];
@@ -253,16 +255,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   }
   for (int s = 1; s < d.K; ++s) {
     float* out = (AK == T0) ? T2 : T0;
-    wmm<32, 32, false, false, false, true>(out, AK, kTile, T3, 1.f);
+    wmm<32, 32, false, false, false>(out, AK, kTile, T3, 1.f);
     __syncwarp();
     AK = out;
   }
   __syncwarp();
   float* TU = (AK == T0) ? T2 : T0;
   float* TV = (d.K == 1) ? T2 : T3;
-  wmm<32, 32, false, false, false, true>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
+  wmm<32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
   __syncwarp();
-  wmm<32, 32, true, false, false, true>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
+  wmm<32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
 #pragma unroll
   for (int pb = 0; pb < NPB; ++pb) {
     float crow[32];
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     st_row(TC + pb * kTile, lane, crow);                                  // Cn rows
   }
   __syncwarp();
-  wmm<32 * NPB, 32, false, false, false, true>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
+  wmm<32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
   __syncwarp();
 
   // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T
@@ -285,8 +287,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     }
     __syncwarp();
 #pragma unroll
-    for (int pb = 0; pb < NPB; ++pb)
-      wmm<32, 32, false, true, false, true>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
+    for (int pb = 0; pb < NPB; ++pb)   // bf16 zq is exact in tf32: split only W / m
+      wmm2<32, 32, false, true, false, !kIoExact<IO>, true>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
     __syncwarp();
 #pragma unroll
     for (int pb = 0; pb < NPB; ++pb) {
@@ -338,11 +340,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
 
   // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
   factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
-  wmm<32, 32, true, false, false, true>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  wmm<32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
   ld_gmem_row(t, rec + r * r, lane, r, r, im2);
   st_row(TX, lane, t);                                                    // TX = Mn
   __syncwarp();
-  wmm<32, 32, false, false, false, true>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  wmm<32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
   __syncwarp();
   ld_row(t, TA, lane);
 #pragma unroll
@@ -359,15 +361,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     const float* cur = TA;
     for (int s = 1; s < d.K; ++s) {
       float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
-      wmm<32, 32, false, false, false, true>(out, cur, kTile, TA, 1.f);
+      wmm<32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
       __syncwarp();
       cur = out;
     }
   }
   __syncwarp();
-  wmm<32, 32, false, false, false, true>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  wmm<32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
   __syncwarp();
-  wmm<32, 32, true, false, false, true>(TV, TLi, kTile, TX, 1.f);       // TV = V
+  wmm<32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
 #pragma unroll
   for (int pb = 0; pb < NPB; ++pb) {
     ld_gmem_row(t, rec + 2 * r * r, pb * 32 + lane, P, r, im);
@@ -376,7 +378,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     st_row(TDW + pb * kTile, lane, t);                                    // dW = 0
   }
   __syncwarp();
-  wmm<32 * NPB, 32, false, false, false, true>(TW, TDY, kTile, TV, 1.f);  // W = Cn V
+  wmm<32 * NPB, 32, false, false, false>(TW, TDY, kTile, TV, 1.f);  // W = Cn V
   __syncwarp();
 
   // ---- token pass: dW += dY^T qn, dqn = dY W  (32 tokens at a time) ----
@@ -385,7 +387,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   for (int t0 = 0; t0 < CS; t0 += 32) {
     const int tl = t0 + lane, tok = tchunk + tl;
     const bool live = tl < CS && tok < T;
-    ld_tok_row<IO>(u, zq, id.b, tok, id.h, 0, r, live, im);             // qn row (kept for dm)
+    ld_tok_row<IO>(u, zq, id.b, tok, id.h, 0, r, live, 1.f);            // zq row (kept for dm)
     st_row(TX, lane, u);
 #pragma unroll
     for (int pb = 0; pb < NPB; ++pb) {
@@ -393,14 +395,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
       st_row(TDY + pb * kTile, lane, t);                                  // dY column block pb
     }
     __syncwarp();
-    wmm<32 * NPB, 32, true, false, true, true>(TDW, TDY, kTile, TX, 1.f);  // dW += dY^T qn
-    wmm<32, 32 * NPB, false, false, false, true>(TY, TDY, kTile, TW, 1.f);  // dqn = dY W
+    // bf16 dy and zq are exact in tf32: dW needs one product per tile, dqn two
+    wmm2<32 * NPB, 32, true, false, true, !kIoExact<IO>, !kIoExact<IO>>(TDW, TDY, kTile, TX, im);  // dW += dY^T qn
+    wmm2<32, 32 * NPB, false, false, false, !kIoExact<IO>, true>(TY, TDY, kTile, TW, 1.f);         // dqn = dY W
     __syncwarp();
     ld_row(t, TY, lane);
     st_tok_row<IO>(dzq, id.b, tok, id.h, 0, r, live, t, im);             // dzq = dqn / m
     if (live) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) dmq = fmaf(t[j], u[j], dmq);
+      for (int j = 0; j < 32; ++j) dmq = fmaf(t[j], u[j], dmq);   // dqn . zq
     }
     __syncwarp();
   }
@@ -412,8 +415,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     st_row(TDY + pb * kTile, lane, t);                                    // Cn rows again
   }
   __syncwarp();
-  wmm<32, 32 * NPB, true, false, false, true>(TX, TDY, kTile, TDW, 1.f);  // TX = dV
-  wmm<32 * NPB, 32, false, true, false, true>(TW, TDW, kTile, TV, 1.f);   // TW = dCn
+  wmm<32, 32 * NPB, true, false, false>(TX, TDY, kTile, TDW, 1.f);  // TX = dV
+  wmm<32 * NPB, 32, false, true, false>(TW, TDW, kTile, TV, 1.f);   // TW = dCn
   __syncwarp();
   float dmc = 0.f;
 #pragma unroll
@@ -438,13 +441,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   float* TdU = TY;
   float* TU = TDW;
   float* TdAK = TDY;
-  wmm<32, 32, false, false, false, true>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
-  wmm<32, 32, false, false, false, true>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  wmm<32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmm<32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
   __syncwarp();
-  wmm<32, 32, false, true, false, true>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
-  wmm<32, 32, false, true, false, true>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmm<32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmm<32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
   __syncwarp();
-  wmm<32, 32, true, false, true, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  wmm<32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
   __syncwarp();
   // dA from dAK; free: TV, TX, TY, TDW
   const float* TdA;
@@ -464,12 +467,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
       float* En = pool[pi & 3];
       float* Hn = pool[(pi + 1) & 3];
       pi += 2;
-      wmm<32, 32, false, true, false, true>(En, E, kTile, TA, 1.f);      // E A^T
+      wmm<32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
       __syncwarp();
       ld_row(t, En, lane);
       st_row(Hn, lane, t);
       __syncwarp();
-      wmm<32, 32, true, false, true, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      wmm<32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
       __syncwarp();
       E = En;
       Hc = Hn;
@@ -494,9 +497,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   float* TdMn = fr[1];
   float* TdS = fr[2];
   __syncwarp();
-  wmm<32, 32, true, false, false, true>(TS, TLi, kTile, TLi, 1.f);       // S
+  wmm<32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
   __syncwarp();
-  wmm<32, 32, false, false, false, true>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  wmm<32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
   ld_row(t, TdMn, lane);
@@ -513,7 +516,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   }
   st_row(TS, lane, u);                                                    // TS = Mn (S done)
   __syncwarp();
-  wmm<32, 32, true, false, false, true>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  wmm<32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
   st_row(TdMn, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, true, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  wmm<32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
   __syncwarp();
   ld_row(t, TdLi, lane);
 #pragma unroll
@@ -529,7 +532,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmm<32, 32, false, true, false, true>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  wmm<32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -543,9 +546,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
   st_row(TdS, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, false, true>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  wmm<32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
   __syncwarp();
-  wmm<32, 32, true, false, false, true>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  wmm<32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -568,7 +571,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
       }
     }
   }
-  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq);
+  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq * im);
   const float dgs = warp_sum32(dg);
   if (lane == 0) {
     dmpart[q] = -tot / m;

@@ -136,41 +136,35 @@ __device__ __forceinline__ float warp_sum32(float x) {
   return x;
 }
 
-// In-place Cholesky of the 32 x 32 matrix whose row `lane` is g (lower part read):
-// on success g = row `lane` of L with zero upper part.  Returns false at the first
-// non-positive pivot (uniform), like potrf's info > 0 (ska.py:140).  Right-looking:
-// column j is final after step j; the trailing update takes L[k][j] from lane k.
-__device__ __forceinline__ bool chol32(float (&g)[32], int lane) {
+// In-place Cholesky of the 32 x 32 matrix whose row `lane` is g (lower part read),
+// fused with the inverse of the factor.  On success g = row `lane` of L (zero upper
+// part) and x = column `lane` of L^{-1}.  Returns false at the first non-positive
+// pivot (uniform), like potrf's info > 0 (ska.py:140).
+// Right-looking: at step j the warp broadcasts column j of L (L[k][j] from lane k);
+// the same values drive the forward substitution L x = e_lane, so the inverse costs
+// no extra shuffles.  1/L[j][j] comes from rsqrtf (a few ulp).
+__device__ __forceinline__ bool chol_inv32(float (&g)[32], float (&x)[32], int lane) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.f : 0.f;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float djj = shfl(g[j], j);
     if (!(djj > 0.f)) return false;
-    const float ljj = sqrtf(djj);
-    const float inv = 1.f / ljj;
-    const float lij = lane > j ? g[j] * inv : (lane == j ? ljj : 0.f);
+    const float rs = rsqrtf(djj);                      // 1 / L[j][j]
+    const float lij = lane > j ? g[j] * rs : (lane == j ? djj * rs : 0.f);
     g[j] = lij;
+    x[j] *= rs;                                        // Li[j][lane] is final
 #pragma unroll
-    for (int k = j + 1; k < 32; ++k) g[k] = fmaf(-lij, shfl(lij, k), g[k]);
+    for (int k = j + 1; k < 32; ++k) {
+      const float lkj = shfl(lij, k);                  // L[k][j]
+      g[k] = fmaf(-lij, lkj, g[k]);
+      x[k] = fmaf(-lkj, x[j], x[k]);
+    }
   }
 #pragma unroll
   for (int k = 0; k < 32; ++k)
     if (k > lane) g[k] = 0.f;
   return true;
-}
-
-// x = column `lane` of L^{-1} (x[i] = Li[i][lane]); l = row `lane` of L.
-// Right-looking forward substitution of L x = e_lane: after step i, x[i] is final
-// and is eliminated from every later row, so the dependent chain per step is one
-// multiply and one FMA (the shuffled L entries do not depend on x).
-__device__ __forceinline__ void trinv32(const float (&l)[32], float (&x)[32], int lane) {
-#pragma unroll
-  for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.f : 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    x[i] = x[i] / shfl(l[i], i);
-#pragma unroll
-    for (int k = i + 1; k < 32; ++k) x[k] = fmaf(-shfl(l[i], k), x[i], x[k]);
-  }
 }
 
 // one halving step of the butterfly reduce-scatter: keep half N of the live
@@ -196,22 +190,29 @@ __device__ __forceinline__ float reduce_scatter32(float (&t)[32], int lane) {
 }
 
 // sigma_max estimate of ska.py:41-58: 6 power iterations from v = 1/sqrt(r) on the
-// matrix whose row `lane` is a (zero rows/cols past r).
+// matrix whose row `lane` is a (zero rows/cols past r).  x / max(||x||, 1e-8) is
+// taken as x * min(rsqrt(||x||^2), 1e8).
 __device__ __forceinline__ float power_sigma32(const float (&a)[32], int lane, int r) {
-  float v = lane < r ? 1.f / sqrtf((float)r) : 0.f;
+  float v = lane < r ? rsqrtf((float)r) : 0.f;
   float u = 0.f;
 #pragma unroll 1
   for (int it = 0; it <= kPowerIters; ++it) {
-    u = 0.f;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) u = fmaf(a[j], shfl(v, j), u);
+    for (int j = 0; j < 32; j += 4) {
+      s0 = fmaf(a[j], shfl(v, j), s0);
+      s1 = fmaf(a[j + 1], shfl(v, j + 1), s1);
+      s2 = fmaf(a[j + 2], shfl(v, j + 2), s2);
+      s3 = fmaf(a[j + 3], shfl(v, j + 3), s3);
+    }
+    u = (s0 + s1) + (s2 + s3);
     if (it == kPowerIters) break;
-    u = u / fmaxf(sqrtf(warp_sum32(u * u)), kPowerEps);
+    u *= fminf(rsqrtf(warp_sum32(u * u)), 1.f / kPowerEps);
     float t[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) t[i] = u * a[i];
     const float w = reduce_scatter32(t, lane);
-    v = w / fmaxf(sqrtf(warp_sum32(w * w)), kPowerEps);
+    v = w * fminf(rsqrtf(warp_sum32(w * w)), 1.f / kPowerEps);
   }
   return sqrtf(warp_sum32(u * u));
 }
@@ -238,76 +239,130 @@ __device__ __forceinline__ void mma_tf32_acc(float (&d)[4], const uint32_t (&a)[
 //                   : A[(k >> 5) * SA + swz(i, k & 31)]   (A stored M x K in 32-col blocks)
 //   op(B)(k,j) = TB ? B[swz(j, k)]  (B stored 32 x K, K <= 32) : B[swz(k, j)]  (tall)
 //   C(i,j)     = C[swz(i, j)]
-// SPLIT: x = hi + lo (hi = tf32(x), lo = tf32(x - hi)) and a*b ~= hl*hb + ha*lb + la*hb,
-// i.e. fp32-level products.  C may not alias A or B.  All 32 lanes must call.
+// Operands are split x = hi + lo with hi = x with its low 13 mantissa bits cleared
+// (exactly a tf32 value) and lo = x - hi (exact); the TF32 MMA reads the top 19 bits
+// of lo.  a*b ~= hi_a hi_b + hi_a lo_b + lo_a hi_b has ~2^-20 relative error, i.e.
+// fp32-level products, at two ALU ops per operand value.  SPLIT = false uses hi only.
+// C may not alias A or B.  All 32 lanes must call.
+__device__ __forceinline__ void split_trunc(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
 // Not inlined: one copy per shape keeps the kernels small enough for the
 // instruction cache (inlining every call site made instruction fetch the main stall).
-template <int M, int K, bool TA, bool TB, bool ACC, bool SPLIT>
-__device__ __noinline__ void wmm(float* __restrict__ C, const float* __restrict__ A, int SA,
-                                 const float* __restrict__ B, float alpha) {
-  static_assert(M % 16 == 0 && K % 8 == 0, "tile shape");
+// SA_ / SB_: split that operand (an operand holding bf16 values is exact in tf32 and
+// is passed unsplit).  Two 16-row blocks are processed together so that they share
+// the B fragments; M is a multiple of 32.
+template <int M, int K, bool TA, bool TB, bool ACC, bool SA_, bool SB_>
+__device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict__ A, int SA,
+                                  const float* __restrict__ B, float alpha) {
+  static_assert(M % 32 == 0 && K % 8 == 0, "tile shape");
   static_assert(!TB || K <= 32, "transposed B holds 32 x K");
   const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int g2 = g >> 2, g3 = g & 3;
 #pragma unroll 1
-  for (int i0 = 0; i0 < M; i0 += 16) {
-    float d[4][4];
+  for (int i0 = 0; i0 < M; i0 += 32) {
+    float d[2][4][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n) d[n][0] = d[n][1] = d[n][2] = d[n][3] = 0.f;
-#pragma unroll 2
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int n = 0; n < 4; ++n) d[h][n][0] = d[h][n][1] = d[h][n][2] = d[h][n][3] = 0.f;
+#pragma unroll
     for (int k0 = 0; k0 < K; k0 += 8) {
-      const int ra = i0 + g, rb = i0 + g + 8, ka = k0 + t4, kb = k0 + t4 + 4;
-      float av[4];
-      if (TA) {
-        av[0] = A[(ra >> 5) * SA + swz(ka, ra & 31)];
-        av[1] = A[(rb >> 5) * SA + swz(ka, rb & 31)];
-        av[2] = A[(ra >> 5) * SA + swz(kb, ra & 31)];
-        av[3] = A[(rb >> 5) * SA + swz(kb, rb & 31)];
-      } else {
-        av[0] = A[(ka >> 5) * SA + swz(ra, ka & 31)];
-        av[1] = A[(ka >> 5) * SA + swz(rb, ka & 31)];
-        av[2] = A[(kb >> 5) * SA + swz(ra, kb & 31)];
-        av[3] = A[(kb >> 5) * SA + swz(rb, kb & 31)];
-      }
-      uint32_t ah[4], al[4];
+      if ((k0 & 15) == 0) sched_fence();
+      const int kc = (k0 & 31) >> 2;         // 16-byte chunk of column ka; kb is kc + 1
+      uint32_t ah[2][4], al[2][4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        ah[u] = tf32_bits(av[u]);
-        al[u] = SPLIT ? tf32_bits(av[u] - __uint_as_float(ah[u])) : 0u;
+      for (int h = 0; h < 2; ++h) {
+        const int ra = i0 + 16 * h + g, rb = ra + 8;
+        float av[4];
+        if (TA) {
+          // A(i,k) = T[(i>>5)*SA + k*32 + ((((i&31)>>2) ^ (k&7)) << 2) + (i&3)], k&7 = t4 (+4)
+          const int ca = (((ra & 31) >> 2) ^ t4) << 2, cb = (((rb & 31) >> 2) ^ t4) << 2;
+          const int ca4 = (((ra & 31) >> 2) ^ (t4 + 4)) << 2, cb4 = (((rb & 31) >> 2) ^ (t4 + 4)) << 2;
+          const float* Pa = A + (ra >> 5) * SA + g3;
+          const float* Pb = A + (rb >> 5) * SA + g3;
+          av[0] = Pa[(k0 + t4) * 32 + ca];
+          av[1] = Pb[(k0 + t4) * 32 + cb];
+          av[2] = Pa[(k0 + t4 + 4) * 32 + ca4];
+          av[3] = Pb[(k0 + t4 + 4) * 32 + cb4];
+        } else {
+          const float* P0 = A + (k0 >> 5) * SA + t4;
+          const int sa = (kc ^ g) << 2, sb = ((kc + 1) ^ g) << 2;
+          av[0] = P0[ra * 32 + sa];
+          av[1] = P0[rb * 32 + sa];
+          av[2] = P0[ra * 32 + sb];
+          av[3] = P0[rb * 32 + sb];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (SA_) {
+            split_trunc(av[u], ah[h][u], al[h][u]);
+          } else {
+            ah[h][u] = __float_as_uint(av[u]);
+            al[h][u] = 0u;
+          }
+        }
       }
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
-        const int col = n * 8 + g;
-        const float b0 = TB ? B[swz(col, ka)] : B[swz(ka, col)];
-        const float b1 = TB ? B[swz(col, kb)] : B[swz(kb, col)];
-        const uint32_t bh0 = tf32_bits(b0), bh1 = tf32_bits(b1);
-        if (SPLIT) {
-          mma_tf32_acc(d[n], al, bh0, bh1);
-          mma_tf32_acc(d[n], ah, tf32_bits(b0 - __uint_as_float(bh0)), tf32_bits(b1 - __uint_as_float(bh1)));
+        float b0, b1;
+        if (TB) {
+          const float* Q = B + (n * 8 + g) * 32 + t4;
+          b0 = Q[(kc ^ g) << 2];
+          b1 = Q[((kc + 1) ^ g) << 2];
+        } else {
+          const int cc = 2 * n + g2;
+          b0 = B[(k0 + t4) * 32 + ((cc ^ t4) << 2) + g3];
+          b1 = B[(k0 + t4 + 4) * 32 + ((cc ^ (t4 + 4)) << 2) + g3];
         }
-        mma_tf32_acc(d[n], ah, bh0, bh1);
+        uint32_t bh0, bl0, bh1, bl1;
+        if (SB_) {
+          split_trunc(b0, bh0, bl0);
+          split_trunc(b1, bh1, bl1);
+        } else {
+          bh0 = __float_as_uint(b0);
+          bh1 = __float_as_uint(b1);
+          bl0 = bl1 = 0u;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (SA_) mma_tf32_acc(d[h][n], al[h], bh0, bh1);
+          if (SB_) mma_tf32_acc(d[h][n], ah[h], bl0, bl1);
+          mma_tf32_acc(d[h][n], ah[h], bh0, bh1);
+        }
       }
     }
 #pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      const int col = n * 8 + 2 * t4;
-      const int r0 = i0 + g, r1 = i0 + g + 8;
-      float* c00 = C + swz(r0, col);
-      float* c01 = C + swz(r0, col + 1);
-      float* c10 = C + swz(r1, col);
-      float* c11 = C + swz(r1, col + 1);
-      if (ACC) {
-        *c00 += alpha * d[n][0];
-        *c01 += alpha * d[n][1];
-        *c10 += alpha * d[n][2];
-        *c11 += alpha * d[n][3];
-      } else {
-        *c00 = alpha * d[n][0];
-        *c01 = alpha * d[n][1];
-        *c10 = alpha * d[n][2];
-        *c11 = alpha * d[n][3];
+    for (int h = 0; h < 2; ++h) {
+      const int ra = i0 + 16 * h + g, rb = ra + 8;
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        // C(r, col) for col = n*8 + 2*t4 (+1): chunk (2n + (t4 >> 1)) ^ g, word (2*t4) & 3 (+1)
+        const int cw = ((((2 * n + (t4 >> 1)) ^ g) << 2) | ((2 * t4) & 3));
+        float* c0 = C + ra * 32 + cw;
+        float* c1 = C + rb * 32 + cw;
+        if (ACC) {
+          c0[0] += alpha * d[h][n][0];
+          c0[1] += alpha * d[h][n][1];
+          c1[0] += alpha * d[h][n][2];
+          c1[1] += alpha * d[h][n][3];
+        } else {
+          c0[0] = alpha * d[h][n][0];
+          c0[1] = alpha * d[h][n][1];
+          c1[0] = alpha * d[h][n][2];
+          c1[1] = alpha * d[h][n][3];
+        }
       }
     }
   }
+}
+
+// fp32-level product of two fp32 tiles
+template <int M, int K, bool TA, bool TB, bool ACC>
+__device__ __forceinline__ void wmm(float* C, const float* A, int SA, const float* B, float alpha) {
+  wmm2<M, K, TA, TB, ACC, true, true>(C, A, SA, B, alpha);
 }
 
 }  // namespace wpc
