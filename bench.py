@@ -273,6 +273,7 @@ def main(argv=None):
     from datetime import timedelta
 
     from koopman_mamba_b200 import _lib
+    from koopman_mamba_b200.sharding import max_over_ranks
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -359,10 +360,7 @@ def main(argv=None):
     wall = time.perf_counter() - wall0
     clock_info = clocks.stop(_visible_gpu_indices(world, local)) if rank == 0 else None
     dev_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1))
-    t = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms_max = float(t.item())
+    dev_ms_max = max_over_ranks(dev_ms, dev)
     tokens_per_step = world * B_PER_GPU * L
     value = tokens_per_step * args.steps / (dev_ms_max / 1e3)
 
@@ -391,10 +389,8 @@ def main(argv=None):
             e2e_step()
             eb[i].record(stream)
         torch.cuda.synchronize()
-        e_ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(ea, eb))], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-        e2e = {"value": tokens_per_step * args.steps / (float(e_ms.item()) / 1e3), "unit": UNIT,
+        e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ea, eb)), dev)
+        e2e = {"value": tokens_per_step * args.steps / (e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     lib.ska_set_profile_events(None, 0)
