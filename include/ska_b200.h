@@ -133,6 +133,20 @@ int ska_bwd(const SkaShape* shape, int io_dtype,
 #define SKA_PROFILE_EVENTS 8
 int ska_set_profile_events(void* const* events, int count);
 
+/* Which kernels ska_fwd / ska_bwd launch for these arguments (no counterpart in
+ * the reference; for integrators checking that a layout reaches the fast
+ * kernels).  Returns a non-negative mask of SKA_PATH_* bits, or a negative
+ * SKA_ERR_* code for arguments ska_fwd would reject.  Launches nothing.
+ *   SKA_PATH_TC_STATS    chunk statistics on TMA + tcgen05 (bf16 tensors with
+ *                        16-byte aligned base and strides, r in {32, 64},
+ *                        P % 8 == 0, chunk_size % 16 == 0); otherwise on
+ *                        CUDA-core fp32 kernels
+ *   SKA_PATH_WARP_CHUNK  chunk operators on the warp-per-chunk register
+ *                        kernels (r <= 32); otherwise one CTA per chunk */
+#define SKA_PATH_TC_STATS 1
+#define SKA_PATH_WARP_CHUNK 2
+int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
+
 /* Forward with no allocation anywhere (no counterpart in the reference, whose
  * PyTorch path always allocates through the caching allocator).  Same
  * computation and arguments as ska_fwd, minus the `saved` buffer: the

@@ -27,7 +27,10 @@ EXPORTED = (
     "ska_bwd",
     "ska_set_profile_events",
     "ska_fwd_noalloc",
+    "ska_kernel_path",
 )
+SKA_PATH_TC_STATS = 1
+SKA_PATH_WARP_CHUNK = 2
 SKA_NOALLOC_SCRATCH_BYTES = 16 << 20
 SKA_PROFILE_EVENTS = 8
 
@@ -86,6 +89,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.ska_bwd.restype = ctypes.c_int
     L.ska_set_profile_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
     L.ska_set_profile_events.restype = ctypes.c_int
+    L.ska_kernel_path.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor)]
+    L.ska_kernel_path.restype = ctypes.c_int
     L.ska_fwd_noalloc.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), P(SkaTensor),
                                   ctypes.c_void_p, P(SkaTensor), ctypes.c_void_p]
     L.ska_fwd_noalloc.restype = ctypes.c_int

@@ -20,6 +20,9 @@ size_t smem_bwd_tok(const Dims&);
 bool warp_path_ok(const Dims&);
 size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
+namespace tc {
+bool stats_tc_ok(const Dims& d, const In& z, const In& v);
+}
 }  // namespace ska
 
 namespace {
@@ -118,6 +121,20 @@ int ska_set_profile_events(void* const* events, int count) {
   }
   p->on = true;
   return SKA_OK;
+}
+
+int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  const int es = elem_size(io_dtype);
+  if (!es) return SKA_ERR_DTYPE;
+  ska::In iz{}, iv{};
+  if ((rc = check_tensor(z, es, true, &iz)) || (rc = check_tensor(v, es, true, &iv))) return rc;
+  int mask = 0;
+  if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
+  if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
+  return mask;
 }
 
 const char* ska_status_string(int code) {

@@ -101,6 +101,8 @@ struct SavedLayout {
   size_t cmax;      // u64   [B][H][C]      packed (norm bits, ~t) chunk maxima
   size_t invs;      // float [B][H][C]      1 / max(sigma, 1)
   size_t flags;     // int   [B][H][C]      bit0: jittered, bit1: jitter failed too
+  size_t status;    // int   [B][H][C]      tensor-core statistics kernel: 0 ok,
+                    //                      1 TMA wait expired, 2 MMA wait expired
   size_t total;
 };
 
@@ -120,6 +122,7 @@ __host__ __device__ inline SavedLayout saved_layout(long long B, long long H, lo
   L.cmax = off;  off = align256(off + n * sizeof(unsigned long long));
   L.invs = off;  off = align256(off + n * sizeof(float));
   L.flags = off; off = align256(off + n * sizeof(int));
+  L.status = off; off = align256(off + n * sizeof(int));
   L.total = off;
   return L;
 }

@@ -15,6 +15,8 @@
 //
 // Every small matrix lives in shared memory with an odd leading dimension so that
 // row- and column-wise accesses are bank-conflict free.  All arithmetic is fp32.
+#include <type_traits>
+
 #include "ska_common.cuh"
 
 namespace ska {
@@ -932,10 +934,28 @@ cudaError_t launch_bwd_chunk_w(const Dims&, const In&, const In&, const float*, 
                                const unsigned long long*, const float*, const int*, float*, float*, float*,
                                cudaStream_t);
 
+namespace tc {
+bool stats_tc_ok(const Dims& d, const In& z, const In& v);
+cudaError_t launch_stats_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
+                            int* status, cudaStream_t st);
+}  // namespace tc
+
 template <typename K>
 static cudaError_t set_smem(K kernel, size_t bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
+
+// bf16 token tensors with TMA-compatible alignment take the TMA + tcgen05 statistics kernel
+template <typename IO>
+bool tc_stats_path(const Dims& d, const In& z, const In& v) {
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
+    return tc::stats_tc_ok(d, z, v);
+  } else {
+    return false;
+  }
+}
+template bool tc_stats_path<float>(const Dims&, const In&, const In&);
+template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 
 template <typename IO>
 cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
@@ -950,7 +970,12 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if ((e = set_smem(k_fwd_stats<IO>, s1)) != cudaSuccess) return e;
   if ((e = set_smem(k_fwd_chunk<IO>, s3)) != cudaSuccess) return e;
   prof_record(0, st);
-  k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
+  if (tc_stats_path<IO>(d, z, v)) {
+    int* status = reinterpret_cast<int*>(saved + L.status);
+    if ((e = tc::launch_stats_tc(d, z, v, stats, cmax, status, st)) != cudaSuccess) return e;
+  } else {
+    k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
+  }
   prof_record(1, st);
   k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   prof_record(2, st);

@@ -93,3 +93,37 @@ def test_fwd_validation_before_any_cuda_call(built_lib):
     rc = L.ska_fwd(ctypes.byref(s), 1, ctypes.byref(ok), ctypes.byref(ok), ctypes.byref(ok),
                    ctypes.c_void_p(0x2000), ctypes.byref(ok), ctypes.c_void_p(0x10000), 16, None)
     assert rc == -5
+
+
+def _contig(base, B, T, H, D):
+    return _lib.SkaTensor(base, T * H * D, H * D, D)
+
+
+@pytest.mark.parametrize("kw,dtype,zt,want", [
+    # config 2 in bf16, contiguous: tensor-core statistics + warp chunk operators
+    (dict(), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK),
+    # fp32 tensors: CUDA-core statistics
+    (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
+    # r = 64 (config 3): tensor-core statistics, one CTA per chunk operator
+    (dict(r=64, chunk_size=128), 1, None, _lib.SKA_PATH_TC_STATS),
+    # r = 16: CUDA-core statistics
+    (dict(r=16), 1, None, _lib.SKA_PATH_WARP_CHUNK),
+    # token stride not a multiple of 16 bytes: CUDA-core statistics
+    (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
+    # decay strategy shares the statistics kernel
+    (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None,
+     _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK),
+])
+def test_kernel_path_selection(built_lib, kw, dtype, zt, want):
+    s = _shape(**kw)
+    z = zt or _contig(0x1000, s.B, s.T, s.H, s.r)
+    v = _contig(0x100000, s.B, s.T, s.H, s.P)
+    assert _lib.lib().ska_kernel_path(ctypes.byref(s), dtype, ctypes.byref(z), ctypes.byref(v)) == want
+
+
+def test_kernel_path_rejects_what_ska_fwd_rejects(built_lib):
+    L = _lib.lib()
+    s = _shape()
+    t = _lib.SkaTensor(0, 0, 0, 0)
+    assert L.ska_kernel_path(ctypes.byref(s), 1, ctypes.byref(t), ctypes.byref(t)) == -1
+    assert L.ska_kernel_path(ctypes.byref(s), 9, ctypes.byref(t), ctypes.byref(t)) == -4

@@ -128,6 +128,44 @@ def test_fused_projection_strides_bitwise():
     assert torch.equal(y1, y2)
 
 
+def _path(z, v, r, P, chunk=64):
+    from koopman_mamba_b200 import _lib
+    import ctypes
+    B, T, H = z.shape[0], z.shape[1], z.shape[2]
+    s = _lib.make_shape(B, T, H, r, P, chunk, 2, 1e-3)
+    tz = _lib.SkaTensor(z.data_ptr(), z.stride(0), z.stride(1), z.stride(2))
+    tv = _lib.SkaTensor(v.data_ptr(), v.stride(0), v.stride(1), v.stride(2))
+    return _lib.lib().ska_kernel_path(ctypes.byref(s), _lib.SKA_DTYPE_BF16, ctypes.byref(tz), ctypes.byref(tv))
+
+
+def test_fused_projection_strides_tensor_core_stats():
+    """r = 32 slices of one fused projection: strided TMA tiles give the bits of the
+    contiguous layout, and both take the TMA + tcgen05 statistics kernel."""
+    from koopman_mamba_b200 import _lib
+    B, T, H, r, P = 2, 333, 3, 32, 64
+    g = torch.Generator().manual_seed(6)
+    fused = (torch.randn(B, T, 2 * H * r + H * P, generator=g) / 8).to(DEV, torch.bfloat16)
+    z = fused[:, :, :H * r].reshape(B, T, H, r)
+    zq = fused[:, :, H * r:2 * H * r].reshape(B, T, H, r)
+    v = fused[:, :, 2 * H * r:].reshape(B, T, H, P)
+    assert _path(z, v, r, P) & _lib.SKA_PATH_TC_STATS
+    assert _path(z.contiguous(), v.contiguous(), r, P) & _lib.SKA_PATH_TC_STATS
+    gm = torch.tensor(1.1, device=DEV)
+    y1 = ska_core(z, zq, v, gm)
+    y2 = ska_core(z.contiguous(), zq.contiguous(), v.contiguous(), gm)
+    assert torch.equal(y1, y2)
+    ref, _ = ska_core_forward(z.float().cpu().numpy(), zq.float().cpu().numpy(), v.float().cpu().numpy(), 1.1,
+                              SkaParams())
+    assert rel_fro(y1.double().cpu().numpy(), ref) <= BF16_TOL
+
+
+def test_config2_takes_the_tensor_core_statistics_kernel():
+    from koopman_mamba_b200 import _lib
+    z = torch.empty(8, 2048, 12, 32, dtype=torch.bfloat16, device=DEV)
+    v = torch.empty(8, 2048, 12, 64, dtype=torch.bfloat16, device=DEV)
+    assert _path(z, v, 32, 64) == _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK
+
+
 def test_deterministic_bitwise():
     z, zq, v, dy = _inputs(2, 700, 3, 32, 64, 9)
     a = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16)
