@@ -142,9 +142,13 @@ int ska_set_profile_events(void* const* events, int count);
  *                        P % 8 == 0, chunk_size % 16 == 0); otherwise on
  *                        CUDA-core fp32 kernels
  *   SKA_PATH_WARP_CHUNK  chunk operators on the warp-per-chunk register
- *                        kernels (r <= 32); otherwise one CTA per chunk */
+ *                        kernels (r <= 32); otherwise one CTA per chunk
+ *   SKA_PATH_TC_TOKEN_BWD  per-token dz, dv on TMA + tcgen05 (as TC_STATS, plus
+ *                        chunk_size <= 128 and P % 16 == 0, with dz and dv laid
+ *                        out like z and v); otherwise on CUDA cores */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
+#define SKA_PATH_TC_TOKEN_BWD 4
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Forward with no allocation anywhere (no counterpart in the reference, whose

@@ -31,6 +31,7 @@ EXPORTED = (
 )
 SKA_PATH_TC_STATS = 1
 SKA_PATH_WARP_CHUNK = 2
+SKA_PATH_TC_TOKEN_BWD = 4
 SKA_NOALLOC_SCRATCH_BYTES = 16 << 20
 SKA_PROFILE_EVENTS = 8
 

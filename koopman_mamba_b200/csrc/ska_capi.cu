@@ -22,6 +22,7 @@ size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
 namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
+bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const Out& dz, const Out& dv);
 }
 }  // namespace ska
 
@@ -134,6 +135,8 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   int mask = 0;
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
   if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
+  const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
+  if (io_dtype == SKA_DTYPE_BF16 && ska::tc::tok_bwd_tc_ok(d, iz, iv, gz, gv)) mask |= SKA_PATH_TC_TOKEN_BWD;
   return mask;
 }
 

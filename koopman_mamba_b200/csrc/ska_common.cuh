@@ -111,6 +111,8 @@ struct ScratchLayout {
   size_t dmpart;    // float [B][H][C]      per-chunk partial d(max norm)
   size_t dgpart;    // float [B][H][C]      per-chunk partial d(gamma)
   size_t dm;        // float [B][H]
+  size_t status;    // int   [B][H][C]      tensor-core token kernel: 0 ok,
+                    //                      1 TMA wait expired, 2 MMA wait expired
   size_t total;
 };
 
@@ -135,6 +137,7 @@ __host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H
   L.dmpart = off; off = align256(off + n * sizeof(float));
   L.dgpart = off; off = align256(off + n * sizeof(float));
   L.dm = off;     off = align256(off + (size_t)B * H * sizeof(float));
+  L.status = off; off = align256(off + n * sizeof(int));
   L.total = off;
   return L;
 }

@@ -938,6 +938,10 @@ namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
 cudaError_t launch_stats_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
                             int* status, cudaStream_t st);
+bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const Out& dz, const Out& dv);
+cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const float* dstats,
+                              const unsigned long long* cmax, const float* dm, const Out& dz, const Out& dv,
+                              int* status, cudaStream_t st);
 }  // namespace tc
 
 template <typename K>
@@ -1018,7 +1022,14 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
                                                                                      dm, dgamma);
   prof_record(6, st);
-  k_bwd_tok<IO><<<grid, kThreads, s3, st>>>(d, z, v, dz, dv, dstats, cmax, dm);
+  bool tc_tok = false;
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) tc_tok = tc::tok_bwd_tc_ok(d, z, v, dz, dv);
+  if (tc_tok) {
+    int* status = reinterpret_cast<int*>(scratch + S.status);
+    if ((e = tc::launch_tok_bwd_tc(d, z, v, dstats, cmax, dm, dz, dv, status, st)) != cudaSuccess) return e;
+  } else {
+    k_bwd_tok<IO><<<grid, kThreads, s3, st>>>(d, z, v, dz, dv, dstats, cmax, dm);
+  }
   prof_record(7, st);
   return cudaGetLastError();
 }

@@ -95,24 +95,30 @@ def test_fwd_validation_before_any_cuda_call(built_lib):
     assert rc == -5
 
 
+TC = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD
+
+
 def _contig(base, B, T, H, D):
     return _lib.SkaTensor(base, T * H * D, H * D, D)
 
 
 @pytest.mark.parametrize("kw,dtype,zt,want", [
-    # config 2 in bf16, contiguous: tensor-core statistics + warp chunk operators
-    (dict(), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK),
-    # fp32 tensors: CUDA-core statistics
+    # config 2 in bf16, contiguous: every tensor-core kernel + warp chunk operators
+    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK),
+    # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
-    # r = 64 (config 3): tensor-core statistics, one CTA per chunk operator
-    (dict(r=64, chunk_size=128), 1, None, _lib.SKA_PATH_TC_STATS),
-    # r = 16: CUDA-core statistics
+    # r = 64 (config 3): tensor-core token kernels, one CTA per chunk operator
+    (dict(r=64, chunk_size=128), 1, None, TC),
+    # chunk 256: tensor-core statistics only
+    (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
+    # P % 16 != 0: tensor-core statistics only
+    (dict(P=40), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK),
+    # r = 16: CUDA-core token kernels
     (dict(r=16), 1, None, _lib.SKA_PATH_WARP_CHUNK),
-    # token stride not a multiple of 16 bytes: CUDA-core statistics
+    # token stride not a multiple of 16 bytes: CUDA-core token kernels
     (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
-    # decay strategy shares the statistics kernel
-    (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None,
-     _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK),
+    # decay strategy shares the token kernels
+    (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK),
 ])
 def test_kernel_path_selection(built_lib, kw, dtype, zt, want):
     s = _shape(**kw)

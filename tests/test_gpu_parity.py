@@ -148,22 +148,31 @@ def test_fused_projection_strides_tensor_core_stats():
     z = fused[:, :, :H * r].reshape(B, T, H, r)
     zq = fused[:, :, H * r:2 * H * r].reshape(B, T, H, r)
     v = fused[:, :, 2 * H * r:].reshape(B, T, H, P)
-    assert _path(z, v, r, P) & _lib.SKA_PATH_TC_STATS
-    assert _path(z.contiguous(), v.contiguous(), r, P) & _lib.SKA_PATH_TC_STATS
-    gm = torch.tensor(1.1, device=DEV)
-    y1 = ska_core(z, zq, v, gm)
-    y2 = ska_core(z.contiguous(), zq.contiguous(), v.contiguous(), gm)
-    assert torch.equal(y1, y2)
-    ref, _ = ska_core_forward(z.float().cpu().numpy(), zq.float().cpu().numpy(), v.float().cpu().numpy(), 1.1,
-                              SkaParams())
-    assert rel_fro(y1.double().cpu().numpy(), ref) <= BF16_TOL
+    tc = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD
+    assert _path(z, v, r, P) & tc == tc
+    assert _path(z.contiguous(), v.contiguous(), r, P) & tc == tc
+    dy = (torch.randn(B, T, H, P, generator=g)).to(DEV, torch.bfloat16)
+    outs = []
+    for views in ((z, zq, v), (z.contiguous(), zq.contiguous(), v.contiguous())):
+        leaves = [t.detach().requires_grad_(True) for t in views]
+        gm = torch.tensor(1.1, device=DEV, requires_grad=True)
+        y = ska_core(*leaves, gm)
+        y.backward(dy)
+        outs.append([y.detach()] + [t.grad for t in leaves] + [gm.grad])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    np_in = [t.float().cpu().numpy() for t in (z, zq, v)]
+    ref = ska_core_fwd_bwd(*np_in, 1.1, dy.float().cpu().numpy(), SkaParams())
+    got = [t.double().cpu().numpy() for t in outs[0][:4]]
+    assert_close(got, ref[:4], BF16_TOL)
 
 
 def test_config2_takes_the_tensor_core_statistics_kernel():
     from koopman_mamba_b200 import _lib
     z = torch.empty(8, 2048, 12, 32, dtype=torch.bfloat16, device=DEV)
     v = torch.empty(8, 2048, 12, 64, dtype=torch.bfloat16, device=DEV)
-    assert _path(z, v, 32, 64) == _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK
+    assert _path(z, v, 32, 64) == (_lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD |
+                                   _lib.SKA_PATH_WARP_CHUNK)
 
 
 def test_deterministic_bitwise():
