@@ -134,7 +134,9 @@ def run_reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "compute": "bf16 token tensors and tensor-core operands (fp32 values as bf16 hi+lo pairs), "
+                       "fp32 accumulation; fp32 Cholesky, inverse and power iteration",
         "data": "synthetic (seeded N(0,1)/8 inputs, bf16-rounded)",
         "config": {"workload": WORKLOAD, "path": "reference CPU path: numpy oracle port of "
                    "koopman_lm/ska.py (PyTorch backend) fwd+bwd, fp32", "io_dtype": "bf16-rounded"},
@@ -156,58 +158,72 @@ def _cpu_inputs_warm(seed):
 # ----------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock, power and clock-event reasons sampled by NVML every 2 ms in a
+    background thread; `stop` keeps the samples taken inside [t0, t1] (the timed
+    region), or all of them when that window is shorter than the sampling period."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80))
 
     def __init__(self):
-        self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.thread = None
+        self.samples = []
+        self.handle = None
 
-    def start(self):
+    def start(self, device_index):
+        import threading
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = self._handle(pynvml, device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            self.handle = None
+            return
+        self.stop_flag = threading.Event()
 
-    def stop(self, gpu_indices):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
+        def run():
+            nv, h = self.nvml, self.handle
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self.stop_flag.is_set():
+                try:
+                    self.samples.append((time.perf_counter(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                         get_reasons(h), nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        time.sleep(0.02)   # first samples before the timed region
+
+    @staticmethod
+    def _handle(nv, device_index):
+        import torch
         try:
-            self.proc.wait(timeout=5)
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            return nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
         except Exception:
-            self.proc.kill()
-        self.fh.close()
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                idx = int(f[0])
-            except ValueError:
-                continue
-            if gpu_indices and idx not in gpu_indices:
-                continue
-            try:
-                sms.append(float(f[1]))
-                maxes.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(n)
-        if not sms:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [int(x) for x in vis.split(",") if x.strip().isdigit()]
+            return nv.nvmlDeviceGetHandleByIndex(ids[device_index] if ids else device_index)
+
+    def stop(self, t0, t1):
+        if self.thread is None:
             return None
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(sms)}
+        time.sleep(0.01)
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        inside = [x for x in self.samples if t0 <= x[0] <= t1]
+        use = inside if len(inside) >= 3 else self.samples
+        if not use:
+            return None
+        reasons = sorted({n for _, _, bits, _ in use for n, b in self.REASONS if bits & b})
+        return {"sm_mhz": statistics.median(x[1] for x in use), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "power_w_max": max(x[3] for x in use), "samples": len(use),
+                "window": "timed region" if use is inside else "warm-up + timed region (timed region < 3 samples)"}
 
 
 def _visible_gpu_indices(world, local_rank):
@@ -238,20 +254,27 @@ def _ncu_traffic():
         return {}
 
 
-# algorithmic (unique token-tensor) bytes each kernel must move per launch, bf16
+# Bytes each kernel must move per launch (bf16 token tensors, fp32 chunk records):
+# its token-tensor reads and writes plus the per-chunk records it reads or
+# writes, each once.  C = chunks per series; SW = floats per statistics record.
 def _kernel_algo_bytes(tokens_heads):
     es = 2
+    chunks = tokens_heads // CS
+    rec = (2 * R * R + P * R) * 4          # one statistics record
+    wrec = P * R * 4                       # dW' record / W planes
     return {
-        "k_fwd_stats": tokens_heads * (R + P) * es,            # read z, v
-        "k_scan_fwd": 0,
-        "k_fwd_chunk": tokens_heads * (R + P) * es,            # read zq, write y
-        "k_bwd_chunk": tokens_heads * (R + P + R) * es,        # read zq, dy; write dzq
-        "k_scan_bwd": 0,
-        "k_bwd_tok": tokens_heads * (R + P + R + P) * es,      # read z, v; write dz, dv
+        "k_fwd_stats": tokens_heads * (R + P) * es + chunks * rec,          # z, v -> records
+        "k_scan_fwd": 2 * chunks * rec,                                      # records in place
+        "k_fwd_chunk": tokens_heads * (R + P) * es + chunks * rec,          # records, zq -> y
+        "k_dw": tokens_heads * (R + P) * es + chunks * wrec,                # zq, dy -> dW'
+        "k_bwd_chunk": chunks * (2 * rec + 2 * wrec),                        # records, dW' -> d records, W
+        "k_scan_bwd": 2 * chunks * rec,                                      # d records in place
+        "k_bwd_tok": tokens_heads * (R + 2 * P + 2 * R + P) * es + chunks * (rec + wrec),
+        # z, v, dy, d records, W -> dz, dzq, dv
     }
 
 
-KERNELS = ("k_fwd_stats", "k_scan_fwd", "k_fwd_chunk", "k_bwd_chunk", "k_scan_bwd", "k_bwd_tok")
+KERNELS = ("k_fwd_stats", "k_scan_fwd", "k_fwd_chunk", "k_dw", "k_bwd_chunk", "k_scan_bwd", "k_bwd_tok")
 
 
 def main(argv=None):
@@ -340,10 +363,9 @@ def main(argv=None):
     ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     per_kernel = {k: [] for k in KERNELS}
     clocks = ClockSampler()
+    clocks.start(local)
     barrier()
     torch.cuda.synchronize()
-    if rank == 0:
-        clocks.start()
     wall0 = time.perf_counter()
     for i in range(args.steps):
         flush.zero_()
@@ -352,13 +374,14 @@ def main(argv=None):
         ev1[i].record(stream)
         kev[-1].synchronize()
         spans = [kev[j].elapsed_time(kev[j + 1]) for j in (0, 1, 2)] + \
-                [kev[j].elapsed_time(kev[j + 1]) for j in (4, 5, 6)]
+                [kev[j].elapsed_time(kev[j + 1]) for j in (4, 5, 6, 7)]
         for k, ms in zip(KERNELS, spans):
             per_kernel[k].append(ms)
     torch.cuda.synchronize()
     barrier()
-    wall = time.perf_counter() - wall0
-    clock_info = clocks.stop(_visible_gpu_indices(world, local)) if rank == 0 else None
+    wall1 = time.perf_counter()
+    wall = wall1 - wall0
+    clock_info = clocks.stop(wall0, wall1)
     dev_ms = sum(a.elapsed_time(b) for a, b in zip(ev0, ev1))
     dev_ms_max = max_over_ranks(dev_ms, dev)
     tokens_per_step = world * B_PER_GPU * L
@@ -394,7 +417,7 @@ def main(argv=None):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     lib.ska_set_profile_events(None, 0)
-    launches_per_step = 6
+    launches_per_step = 7   # stats, scan, chunk operators; dW', chunk backward, scan, token backward
 
     # ---- roofline of the dominant kernel ----
     peak, peak_kind = _measured_peaks()
@@ -403,7 +426,8 @@ def main(argv=None):
     dom = max(avg_ms, key=avg_ms.get)
     ach = algo[dom] / (avg_ms[dom] / 1e3) / 1e9
     traffic = _ncu_traffic().get(dom)
-    step_algo = sum(algo.values())
+    # the step's unique token traffic: forward z, zq, v -> y; backward z, zq, v, dy -> dz, dzq, dv
+    step_algo = B_PER_GPU * L * H * (4 * R + 4 * P) * 2
     roofline = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
                 "frac": ach / peak, "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                 "algo_bytes_per_launch": algo[dom],
@@ -430,7 +454,9 @@ def main(argv=None):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "compute": "bf16 token tensors and tensor-core operands (fp32 values as bf16 hi+lo pairs), "
+                       "fp32 accumulation; fp32 Cholesky, inverse and power iteration",
             "data": "synthetic (seeded N(0,1)/8 inputs, N(0,1) upstream grad)",
             "config": {"workload": WORKLOAD, "B_per_gpu": B_PER_GPU, "H": H, "L": L, "P": P, "r": R, "chunk": CS,
                        "power_K": K, "io_dtype": "bf16", "parallelism": f"dp{world} (batch shards, no collective)",

@@ -128,9 +128,12 @@ int ska_bwd(const SkaShape* shape, int io_dtype,
  * reference, which has no per-kernel timing).  With `events` non-NULL and
  * count >= SKA_PROFILE_EVENTS, every later ska_fwd records events[0] on its
  * stream before its first kernel and events[i] after its i-th kernel
- * (i = 1..3); ska_bwd does the same with events[4..7].  The handles are
- * cudaEvent_t values created by the caller.  NULL disables recording. */
-#define SKA_PROFILE_EVENTS 8
+ * (i = 1..3: statistics, scan, chunk operators); ska_bwd records events[4]
+ * before its first kernel and events[5..8] after the readout-gradient kernel
+ * (recorded back to back when that kernel does not run), the chunk operators,
+ * the scan and the token kernel.  The handles are cudaEvent_t values created
+ * by the caller.  NULL disables recording. */
+#define SKA_PROFILE_EVENTS 9
 int ska_set_profile_events(void* const* events, int count);
 
 /* Which kernels ska_fwd / ska_bwd launch for these arguments (no counterpart in
@@ -145,10 +148,16 @@ int ska_set_profile_events(void* const* events, int count);
  *                        kernels (r <= 32); otherwise one CTA per chunk
  *   SKA_PATH_TC_TOKEN_BWD  per-token dz, dv on TMA + tcgen05 (as TC_STATS, plus
  *                        chunk_size <= 128 and P % 16 == 0, with dz and dv laid
- *                        out like z and v); otherwise on CUDA cores */
+ *                        out like z and v); otherwise on CUDA cores
+ *   SKA_PATH_TC_READOUT_BWD  the readout gradient (dW and dzq) on TMA + tcgen05
+ *                        too, and the chunk operators' backward without a token
+ *                        pass (TC_TOKEN_BWD and WARP_CHUNK, with zq, dy and dzq
+ *                        laid out like z and v); otherwise inside the chunk
+ *                        kernel */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
+#define SKA_PATH_TC_READOUT_BWD 8
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Forward with no allocation anywhere (no counterpart in the reference, whose

@@ -22,8 +22,10 @@ size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
 namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
-bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const Out& dz, const Out& dv);
 }
+template <typename IO>
+void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
+                  const Out& dzq, const Out& dv, bool* full, bool* tok);
 }  // namespace ska
 
 namespace {
@@ -135,8 +137,13 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   int mask = 0;
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
   if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
-  const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
-  if (io_dtype == SKA_DTYPE_BF16 && ska::tc::tok_bwd_tc_ok(d, iz, iv, gz, gv)) mask |= SKA_PATH_TC_TOKEN_BWD;
+  if (io_dtype == SKA_DTYPE_BF16) {   // gradients and zq, dy assumed laid out like z and v
+    const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
+    bool full = false, tok = false;
+    ska::bwd_tc_paths<__nv_bfloat16>(d, iz, iz, iv, iv, gz, gz, gv, &full, &tok);
+    if (tok) mask |= SKA_PATH_TC_TOKEN_BWD;
+    if (full) mask |= SKA_PATH_TC_READOUT_BWD;
+  }
   return mask;
 }
 
@@ -160,7 +167,7 @@ int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scrat
   const int rc = make_dims(shape, &d);
   if (rc) return rc;
   if (saved_bytes) *saved_bytes = ska::saved_layout(d.B, d.H, d.C, d.SW).total;
-  if (scratch_bytes) *scratch_bytes = ska::scratch_layout(d.B, d.H, d.C, d.SW).total;
+  if (scratch_bytes) *scratch_bytes = ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P).total;
   return SKA_OK;
 }
 
@@ -216,7 +223,7 @@ int ska_bwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   if (!gamma || !saved || !scratch) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256 || reinterpret_cast<uintptr_t>(scratch) % 256) return SKA_ERR_ALIGN;
   const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW);
-  const ska::ScratchLayout S = ska::scratch_layout(d.B, d.H, d.C, d.SW);
+  const ska::ScratchLayout S = ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
   if (saved_bytes < L.total || scratch_bytes < S.total) return SKA_ERR_WORKSPACE;
   cudaError_t e;
   if (io_dtype == SKA_DTYPE_F32)

@@ -111,8 +111,10 @@ struct ScratchLayout {
   size_t dmpart;    // float [B][H][C]      per-chunk partial d(max norm)
   size_t dgpart;    // float [B][H][C]      per-chunk partial d(gamma)
   size_t dm;        // float [B][H]
-  size_t status;    // int   [B][H][C]      tensor-core token kernel: 0 ok,
+  size_t status;    // int   [B][H][C]      tensor-core token kernels: 0 ok,
                     //                      1 TMA wait expired, 2 MMA wait expired
+  size_t dw;        // float [B][H][C][P r] raw readout gradient sum_t dy_t zq_t^T
+  size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the dzq operand
   size_t total;
 };
 
@@ -129,7 +131,8 @@ __host__ __device__ inline SavedLayout saved_layout(long long B, long long H, lo
   return L;
 }
 
-__host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H, long long C, long long SW) {
+__host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H, long long C, long long SW,
+                                                       long long r, long long P) {
   ScratchLayout L{};
   const size_t n = (size_t)B * H * C;
   size_t off = 0;
@@ -138,8 +141,25 @@ __host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H
   L.dgpart = off; off = align256(off + n * sizeof(float));
   L.dm = off;     off = align256(off + (size_t)B * H * sizeof(float));
   L.status = off; off = align256(off + n * sizeof(int));
+  L.dw = off;     off = align256(off + n * (size_t)P * r * sizeof(float));
+  L.wm = off;     off = align256(off + n * (size_t)P * r * 4);
   L.total = off;
   return L;
+}
+
+// x = hi + lo as bf16 pairs (round to nearest twice): 8 floats -> two 16-byte rows
+__device__ __forceinline__ void split_bf16x8(const float (&x)[8], uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
+    const float2 hf = __bfloat1622float2(hh);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(x[2 * e] - hf.x, x[2 * e + 1] - hf.y);
+    h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[e] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // Packed arg-max key: larger norm wins, ties go to the smaller token index
@@ -157,7 +177,7 @@ __device__ __forceinline__ int unpack_t(unsigned long long k) {
 
 // Caller-provided timing events (ska_set_profile_events); nullptr = off.
 struct ProfileEvents {
-  cudaEvent_t ev[8];
+  cudaEvent_t ev[9];
   bool on;
 };
 ProfileEvents* profile_events();

@@ -938,11 +938,35 @@ namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
 cudaError_t launch_stats_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
                             int* status, cudaStream_t st);
-bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const Out& dz, const Out& dv);
-cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const float* dstats,
-                              const unsigned long long* cmax, const float* dm, const Out& dz, const Out& dv,
-                              int* status, cudaStream_t st);
+bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const In& dy, const Out& dz, const Out& dv,
+                   const Out& dzq, bool dzq_on);
+cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In& dy, const float* dstats,
+                              const unsigned char* wm, const unsigned long long* cmax, const float* dm,
+                              const Out& dz, const Out& dv, const Out& dzq, bool dzq_on, int* status,
+                              cudaStream_t st);
+bool dw_tc_ok(const Dims& d, const In& zq, const In& dy);
+cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st);
 }  // namespace tc
+cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               const float* invs, const int* flags, const float* dwraw, float* dstats,
+                               float* dmpart, float* dgpart, unsigned char* wm, cudaStream_t st);
+
+// Which backward kernels run (bf16 token tensors with TMA-compatible layouts):
+//   full: dW' and dzq on tcgen05, chunk operators without a token pass (r <= 32)
+//   tok : dz, dv on tcgen05; the chunk kernel does the readout's token pass
+template <typename IO>
+void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
+                  const Out& dzq, const Out& dv, bool* full, bool* tok) {
+  *full = *tok = false;
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
+    *full = warp_path_ok(d) && tc::dw_tc_ok(d, zq, dy) && tc::tok_bwd_tc_ok(d, z, v, dy, dz, dv, dzq, true);
+    *tok = *full || tc::tok_bwd_tc_ok(d, z, v, dy, dz, dv, dzq, false);
+  }
+}
+template void bwd_tc_paths<float>(const Dims&, const In&, const In&, const In&, const In&, const Out&,
+                                  const Out&, const Out&, bool*, bool*);
+template void bwd_tc_paths<__nv_bfloat16>(const Dims&, const In&, const In&, const In&, const In&, const Out&,
+                                          const Out&, const Out&, bool*, bool*);
 
 template <typename K>
 static cudaError_t set_smem(K kernel, size_t bytes) {
@@ -1009,8 +1033,19 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   const size_t s1 = smem_bwd_chunk(d), s3 = smem_bwd_tok(d);
   if ((e = set_smem(k_bwd_chunk<IO>, s1)) != cudaSuccess) return e;
   if ((e = set_smem(k_bwd_tok<IO>, s3)) != cudaSuccess) return e;
+  bool full = false, tc_tok = false;
+  bwd_tc_paths<IO>(d, z, zq, v, dy, dz, dzq, dv, &full, &tc_tok);
+  float* dw = reinterpret_cast<float*>(scratch + S.dw);
+  unsigned char* wm = reinterpret_cast<unsigned char*>(scratch + S.wm);
+  int* status = reinterpret_cast<int*>(scratch + S.status);
   prof_record(4, st);
-  if (warp_path_ok(d)) {
+  if (full && (e = tc::launch_dw_tc(d, zq, dy, dw, status, st)) != cudaSuccess) return e;
+  prof_record(5, st);
+  if (full) {
+    if ((e = launch_bwd_chunk_s(d, gamma, stats, cmax, invs, flags, dw, dstats, dmpart, dgpart, wm, st)) !=
+        cudaSuccess)
+      return e;
+  } else if (warp_path_ok(d)) {
     if ((e = launch_bwd_chunk_w<IO>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart, dgpart,
                                     st)) != cudaSuccess)
       return e;
@@ -1018,19 +1053,18 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
     k_bwd_chunk<IO><<<grid, kThreads, s1, st>>>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart,
                                                dgpart);
   }
-  prof_record(5, st);
+  prof_record(6, st);
   k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
                                                                                      dm, dgamma);
-  prof_record(6, st);
-  bool tc_tok = false;
-  if constexpr (std::is_same<IO, __nv_bfloat16>::value) tc_tok = tc::tok_bwd_tc_ok(d, z, v, dz, dv);
+  prof_record(7, st);
   if (tc_tok) {
-    int* status = reinterpret_cast<int*>(scratch + S.status);
-    if ((e = tc::launch_tok_bwd_tc(d, z, v, dstats, cmax, dm, dz, dv, status, st)) != cudaSuccess) return e;
+    if ((e = tc::launch_tok_bwd_tc(d, z, v, dy, dstats, wm, cmax, dm, dz, dv, dzq, full, status, st)) !=
+        cudaSuccess)
+      return e;
   } else {
     k_bwd_tok<IO><<<grid, kThreads, s3, st>>>(d, z, v, dz, dv, dstats, cmax, dm);
   }
-  prof_record(7, st);
+  prof_record(8, st);
   return cudaGetLastError();
 }
 

@@ -177,6 +177,90 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
+// k_dw_tc: raw per-chunk readout gradient  dW'_c = sum_{t in c} dy_t zq_t^T  (P x r)
+// for the backward, the token part of d(W qn) (ska.py:180-181 differentiated; the
+// 1/m of qn = zq/m is applied by the chunk kernel).  Same structure as k_stats_tc:
+// one CTA per chunk, A = dY^T (P rows, tokens as K) and B = ZQ read MN-major from
+// the TMA tiles [ZQ | dY], one TMEM-accumulated bf16 product.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constant__ CUtensorMap mzq,
+                                                            const __grid_constant__ CUtensorMap mdy, Dims d,
+                                                            StatsGeom g, float* __restrict__ dw,
+                                                            int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_slot;
+  unsigned char* tile = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long q = blockIdx.x;
+  const int c = (int)(q % d.C);
+  const long long bh = q / d.C;
+  const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+  const int r = d.r, P = d.P, CS = d.CS;
+  unsigned char* tq = tile;                            // ZQ : r/8 groups
+  unsigned char* ty = tile + (size_t)(r / 8) * g.grp;  // dY : P/8 groups (+ room for rows P..127)
+
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    mbar_fence_init();
+    tma_prefetch_map(&mzq);
+    tma_prefetch_map(&mdy);
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, g.ncols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+  const int t0 = c * CS;
+  if (tid == 0) {
+    mbar_expect_tx(&bar_load, (uint32_t)(r + P) * (uint32_t)CS * 2u);
+    for (int k = 0; k < r / 8; ++k) tma_load_4d(tq + (size_t)k * g.grp, &mzq, &bar_load, 8 * k, h, t0, b);
+    for (int k = 0; k < P / 8; ++k) tma_load_4d(ty + (size_t)k * g.grp, &mdy, &bar_load, 8 * k, h, t0, b);
+  }
+  int st = 0;
+  if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
+    st = 1;
+    mbar_wait(&bar_load, 0);
+  }
+  if (st == 0 && tid == 0) {
+    fence_after_sync();
+    const uint32_t id = idesc_bf16(128, r, true, true);
+    const uint32_t a0 = smem_u32(ty), b0 = smem_u32(tq);
+    for (int ks = 0; ks < CS / 16; ++ks)
+      mma_bf16(tbase, sdesc(a0 + 256u * ks, 128u, g.grp), sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+    mma_commit(&bar_mma);
+  }
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
+    st = 2;
+    mbar_wait(&bar_mma, 0);
+  }
+  __syncthreads();
+  fence_after_sync();
+  float* rec = dw + q * (long long)P * r;
+  const int row = 32 * warp + lane;
+  for (int j0 = 0; j0 < r; j0 += 16) {
+    float v[16];
+    tmem_ld16(tbase + (uint32_t)j0 + ((uint32_t)(32 * warp) << 16), v);
+    if (row < P) {
+      float4* dst = reinterpret_cast<float4*>(rec + (size_t)row * r + j0);
+      const float nan = __int_as_float(0x7fc00000);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        dst[e] = st ? make_float4(nan, nan, nan, nan)
+                    : make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    }
+  }
+  if (tid == 0) status[q] = st;
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, g.ncols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // k_tok_bwd_tc: per-token gradients of one chunk from its scanned statistic
 // gradients dG, dM, dC (and the previous chunk's dM), KLF/koopman_lm/ska.py:96-133
 // differentiated by hand:
@@ -184,13 +268,18 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 //   dv_t = dC z_t
 // where dM~ is the dM of the chunk that owns the transition (t-1 -> t): this
 // chunk's, except the previous chunk's for the first token.  Plus the arg-max
-// key's share of d(max norm): dz_t* += dm / ||z_t*|| * z_t*  (ska.py:441).
+// key's share of d(max norm): dz_t* += dm / ||z_t*|| * z_t*  (ska.py:441), and
+// the readout's  dzq_t = (W / m)^T dy_t  (ska.py:180-181).
 // In matrix form with tokens as M:
-//   dZ (CS x r) = [Z | Z+ | Z- | V] (CS x (3r+P)) . Bz,   dV (CS x P) = Z . Bv
-// A is the TMA token tile read K-major; Bz / Bv are built in shared memory from
-// the fp32 gradients as bf16 hi + lo pairs (x = hi + lo to ~2^-16 relative), so
-// each product runs twice on the tensor cores, accumulating in fp32 in TMEM.
-// The first token's dM fix-up, the arg-max term and the bf16 stores are the
+//   dZ  (CS x r) = [Z | Z+ | Z- | V] (CS x (3r+P)) . Bz
+//   dV  (CS x P) = Z . Bv
+//   dZQ (CS x r) = dY (CS x P) . (W / m)
+// A is the TMA token tile [Z | Z+ | Z- | V | dY] read K-major.  Bz and Bv are
+// built in shared memory from the fp32 gradients (read straight from global
+// memory) as bf16 hi + lo pairs (x = hi + lo to ~2^-16 relative); W / m arrives
+// already split, in the layout the backward chunk kernel wrote.  Each product
+// runs once per half on the tensor cores, accumulating in fp32 in TMEM.  The
+// first token's dM fix-up, the arg-max term and the bf16 stores are the
 // epilogue.  Requires CS <= 128 (one 128-row MMA block; rows past CS are
 // ignored), r in {32, 64}, P % 16 == 0.
 // ---------------------------------------------------------------------------
@@ -199,10 +288,9 @@ constexpr int kTokThreads = 128;
 // Shared-memory plan of k_tok_bwd_tc; every region starts on a 128-byte boundary.
 struct TokGeom {
   uint32_t grp;        // bytes of one feature group of the token tile: CS x 16 B
-  uint32_t rec;        // fp32 statistic-gradient record bytes: SW * 4
-  uint32_t mprev;      // previous chunk's dM bytes: r * r * 4
-  uint32_t o_rec, o_mprev, o_bzh, o_bzl, o_bvh, o_bvl, o_corr;   // region offsets
-  uint32_t ncols;      // TMEM columns: dZ at [0, r), dV at [r, r + P)
+  uint32_t wbytes;     // W / m hi + lo planes: P * r * 4
+  uint32_t o_bzh, o_bzl, o_bvh, o_bvl, o_bw, o_corr;   // region offsets
+  uint32_t ncols;      // TMEM columns: dZ at [0, r), dV at [r, r + P), dZQ at [r + P, 2r + P)
   size_t smem;
 };
 
@@ -211,43 +299,26 @@ __host__ __device__ inline uint32_t up128(uint32_t x) { return (x + 127u) & ~127
 __host__ __device__ inline TokGeom tok_geom(int r, int P, int CS) {
   TokGeom g{};
   g.grp = (uint32_t)CS * 16u;
-  // token tile: (3r + P) / 8 groups, plus room for the ignored rows CS..127
-  const uint32_t tile = (uint32_t)((3 * r + P) / 8) * g.grp + (uint32_t)(128 - CS) * 16u;
-  g.rec = (uint32_t)(2 * r * r + P * r) * 4u;
-  g.mprev = (uint32_t)(r * r) * 4u;
+  // token tile: (3r + 2P) / 8 groups, plus room for the ignored rows CS..127
+  const uint32_t tile = (uint32_t)((3 * r + 2 * P) / 8) * g.grp + (uint32_t)(128 - CS) * 16u;
   const uint32_t bz = (uint32_t)((3 * r + P) * r) * 2u, bv = (uint32_t)(r * P) * 2u;
-  g.o_rec = up128(tile);
-  g.o_mprev = up128(g.o_rec + g.rec);
-  g.o_bzh = up128(g.o_mprev + g.mprev);
+  g.wbytes = (uint32_t)(P * r) * 4u;
+  g.o_bzh = up128(tile);
   g.o_bzl = up128(g.o_bzh + bz);
   g.o_bvh = up128(g.o_bzl + bz);
   g.o_bvl = up128(g.o_bvh + bv);
-  g.o_corr = up128(g.o_bvl + bv);
+  g.o_bw = up128(g.o_bvl + bv);
+  g.o_corr = up128(g.o_bw + g.wbytes);
   uint32_t c = 32;
-  while (c < (uint32_t)(r + P)) c <<= 1;
+  while (c < (uint32_t)(2 * r + P)) c <<= 1;
   g.ncols = c;
   g.smem = (size_t)g.o_corr + (size_t)r * 4 + 128;   // + alignment slack of the base
   return g;
 }
 
-// x = hi + lo in bf16 (round to nearest twice)
-__device__ __forceinline__ void split_bf16x8(const float (&x)[8], uint4& hi, uint4& lo) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const __nv_bfloat162 hh = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
-    const float2 hf = __bfloat1622float2(hh);
-    const __nv_bfloat162 ll = __floats2bfloat162_rn(x[2 * e] - hf.x, x[2 * e + 1] - hf.y);
-    h[e] = *reinterpret_cast<const uint32_t*>(&hh);
-    l[e] = *reinterpret_cast<const uint32_t*>(&ll);
-  }
-  hi = make_uint4(h[0], h[1], h[2], h[3]);
-  lo = make_uint4(l[0], l[1], l[2], l[3]);
-}
-
 __device__ __forceinline__ void load_row8(const float* src, float (&x)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(src);
-  const float4 b = *reinterpret_cast<const float4*>(src + 4);
+  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
   x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
 }
 
@@ -267,18 +338,36 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// two bf16 of a 16-byte token row -> float (element e of 8)
+// bf16 element e of a 16-byte token row -> float
 __device__ __forceinline__ float bf16_at(const unsigned char* row, int e) {
   const uint16_t u = *reinterpret_cast<const uint16_t*>(row + 2 * e);
   return __uint_as_float((uint32_t)u << 16);
 }
 
+// 16 fp32 accumulator columns -> 16 bf16 at dst (32 bytes, 16-byte aligned)
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&x)[16]) {
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const __nv_bfloat162 pr = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
+    w[e] = *reinterpret_cast<const uint32_t*>(&pr);
+  }
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ __nv_bfloat16* tok_ptr(const Out& o, int b, int t, int h) {
+  return static_cast<__nv_bfloat16*>(o.p) + (long long)b * o.sb + (long long)t * o.st + (long long)h * o.sh;
+}
+
 __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_constant__ CUtensorMap mz,
-                                                               const __grid_constant__ CUtensorMap mv, Dims d,
+                                                               const __grid_constant__ CUtensorMap mv,
+                                                               const __grid_constant__ CUtensorMap mdy, Dims d,
                                                                TokGeom g, const float* __restrict__ dstats,
+                                                               const unsigned char* __restrict__ wm,
                                                                const unsigned long long* __restrict__ cmax,
                                                                const float* __restrict__ dm, Out dz, Out dv,
-                                                               int* __restrict__ status) {
+                                                               Out dzq, bool dzq_on, int* __restrict__ status) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint64_t bar_load, bar_mma;
   __shared__ uint32_t tmem_slot;
@@ -291,14 +380,16 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   const int h = (int)(bh % d.H), b = (int)(bh / d.H);
   const int r = d.r, P = d.P, CS = d.CS, T = d.T;
   const int t0 = c * CS;
-  unsigned char* tile = base;                          // [Z | Z+ | Z- | V] feature groups
-  float* rec = reinterpret_cast<float*>(base + g.o_rec);
-  float* mprev = reinterpret_cast<float*>(base + g.o_mprev);
+  const int rg = r / 8;
+  unsigned char* tile = base;                          // [Z | Z+ | Z- | V | dY] feature groups
   unsigned char* bzh = base + g.o_bzh;
   unsigned char* bzl = base + g.o_bzl;
   unsigned char* bvh = base + g.o_bvh;
   unsigned char* bvl = base + g.o_bvl;
+  unsigned char* bw = base + g.o_bw;                   // W / m: hi plane, then lo plane
   float* corr = reinterpret_cast<float*>(base + g.o_corr);   // first-token fix-up, r floats
+  const size_t zg = (size_t)rg * g.grp;
+  const size_t dyg = (size_t)((3 * r + P) / 8) * g.grp;
 
   if (tid == 0) {
     mbar_init(&bar_load, 1);
@@ -306,6 +397,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     mbar_fence_init();
     tma_prefetch_map(&mz);
     tma_prefetch_map(&mv);
+    tma_prefetch_map(&mdy);
   }
   if (warp == 0) tmem_alloc(&tmem_slot, g.ncols);
   fence_before_sync();
@@ -314,20 +406,62 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   const uint32_t tbase = tmem_slot;
 
   if (tid == 0) {
-    const uint32_t tok_bytes = (uint32_t)(3 * r + P) * (uint32_t)CS * 2u;
-    mbar_expect_tx(&bar_load, tok_bytes + g.rec + (c > 0 ? g.mprev : 0u));
-    const uint32_t zg = (uint32_t)(r / 8) * g.grp;
-    for (int k = 0; k < r / 8; ++k) {
+    const uint32_t tok_bytes = (uint32_t)(3 * r + (dzq_on ? 2 : 1) * P) * (uint32_t)CS * 2u;
+    mbar_expect_tx(&bar_load, tok_bytes + (dzq_on ? g.wbytes : 0u));
+    for (int k = 0; k < rg; ++k) {
       tma_load_4d(tile + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0, b);
       tma_load_4d(tile + zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 + 1, b);
       tma_load_4d(tile + 2 * zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 - 1, b);
     }
-    for (int k = 0; k < P / 8; ++k) tma_load_4d(tile + 3 * zg + (size_t)k * g.grp, &mv, &bar_load, 8 * k, h, t0, b);
-    const float* src = dstats + q * d.SW;
-    bulk_load(rec, src, g.rec, &bar_load);
-    if (c > 0) bulk_load(mprev, src - d.SW + r * r, g.mprev, &bar_load);
+    for (int k = 0; k < P / 8; ++k) {
+      tma_load_4d(tile + 3 * zg + (size_t)k * g.grp, &mv, &bar_load, 8 * k, h, t0, b);
+      if (dzq_on) tma_load_4d(tile + dyg + (size_t)k * g.grp, &mdy, &bar_load, 8 * k, h, t0, b);
+    }
+    if (dzq_on) bulk_load(bw, wm + (size_t)q * g.wbytes, g.wbytes, &bar_load);
   }
-  // series arg-max key (overlaps the copies)
+
+  // Bz = [(dG + dG^T); dM; dM^T; dC] and Bv = dC^T as K-major operands (overlapping
+  // the copies): one 16-byte row holds 8 consecutive k for one n, at
+  // (k-group * N + n) * 16.  Column reads (x[i][n], i = 8 kg + e) let the 32 lanes
+  // take 32 n; row reads (x[n][8 kg ..]) give each lane its own n and k-group.
+  const float* dG = dstats + q * d.SW;
+  const float* dM = dG + r * r;
+  const float* dC = dG + 2 * r * r;
+  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups 0 .. r/8: dG + dG^T
+    const int n = it / rg, kg = it % rg;
+    float x[8];
+    load_row8(dG + n * r + kg * 8, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] += __ldg(dG + (kg * 8 + e) * r + n);
+    store_split(bzh, bzl, kg * r + n, x);
+  }
+  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/8 .. r/4: dM
+    const int kg = it / r, n = it % r;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __ldg(dM + (kg * 8 + e) * r + n);
+    store_split(bzh, bzl, (rg + kg) * r + n, x);
+  }
+  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/4 .. 3r/8: dM^T
+    const int n = it / rg, kg = it % rg;
+    float x[8];
+    load_row8(dM + n * r + kg * 8, x);
+    store_split(bzh, bzl, (2 * rg + kg) * r + n, x);
+  }
+  for (int it = tid; it < (P / 8) * r; it += kTokThreads) {        // k-groups 3r/8 ..: dC
+    const int kg = it / r, n = it % r;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __ldg(dC + (kg * 8 + e) * r + n);
+    store_split(bzh, bzl, (3 * rg + kg) * r + n, x);
+  }
+  for (int it = tid; it < rg * P; it += kTokThreads) {             // Bv[p][i] = dC[p][i]
+    const int p = it / rg, ig = it % rg;
+    float x[8];
+    load_row8(dC + p * r + ig * 8, x);
+    store_split(bvh, bvl, ig * P + p, x);
+  }
+  // series arg-max key
   if (warp == 0) {
     unsigned long long k = 0ull;
     for (int i = lane; i < d.C; i += 32) {
@@ -341,88 +475,48 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     }
     if (lane == 0) s_max = k;
   }
+  fence_async_smem();                                  // B operands -> tensor-core proxy
   int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
     st = 1;
     mbar_wait(&bar_load, 0);
   }
 
-  if (st == 0) {
-    // Bz = [(dG + dG^T); dM; dM^T; dC] and Bv = dC^T as K-major operands: one 16-byte
-    // row holds 8 consecutive k for one n, at (k-group * N + n) * 16.  Column reads
-    // of the fp32 record (x[i][n], i = 8 kg + e) let the 32 lanes take 32 n;
-    // row reads (x[n][8 kg ..]) let 8 lanes share an n across the k-groups, so
-    // shared-memory banks stay (nearly) conflict-free either way.
-    const int rg = r / 8;
-    const float* dG = rec;
-    const float* dM = rec + r * r;
-    const float* dC = rec + 2 * r * r;
-    for (int it = tid; it < rg * r; it += kTokThreads) {           // k-groups 0 .. r/8: dG + dG^T
-      const int n = it / rg, kg = it % rg;
-      float x[8];
-      load_row8(dG + n * r + kg * 8, x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] += dG[(kg * 8 + e) * r + n];
-      store_split(bzh, bzl, kg * r + n, x);
-    }
-    for (int it = tid; it < rg * r; it += kTokThreads) {           // k-groups r/8 .. r/4: dM
-      const int kg = it / r, n = it % r;
-      float x[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = dM[(kg * 8 + e) * r + n];
-      store_split(bzh, bzl, (rg + kg) * r + n, x);
-    }
-    for (int it = tid; it < rg * r; it += kTokThreads) {           // k-groups r/4 .. 3r/8: dM^T
-      const int n = it / rg, kg = it % rg;
-      float x[8];
-      load_row8(dM + n * r + kg * 8, x);
-      store_split(bzh, bzl, (2 * rg + kg) * r + n, x);
-    }
-    for (int it = tid; it < (P / 8) * r; it += kTokThreads) {      // k-groups 3r/8 ..: dC
-      const int kg = it / r, n = it % r;
-      float x[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = dC[(kg * 8 + e) * r + n];
-      store_split(bzh, bzl, (3 * rg + kg) * r + n, x);
-    }
-    for (int it = tid; it < rg * P; it += kTokThreads) {           // Bv[p][i] = dC[p][i]
-      const int p = it / rg, ig = it % rg;
-      float x[8];
-      load_row8(dC + p * r + ig * 8, x);
-      store_split(bvh, bvl, ig * P + p, x);
-    }
-    // first token of a chunk: (dM_prev - dM) z_{t-1}, z_{t-1} = row 0 of Z-; one warp per row
-    if (c > 0) {
-      const unsigned char* zm = tile + 2 * (size_t)rg * g.grp;
-      for (int i = warp; i < r; i += kTokThreads / 32) {
-        float a = 0.f;
-        for (int j = lane; j < r; j += 32)
-          a = fmaf(mprev[i * r + j] - dM[i * r + j], bf16_at(zm + (size_t)(j / 8) * g.grp, j % 8), a);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) corr[i] = a;
-      }
-    }
-  }
-  fence_async_smem();                                  // B operands -> tensor-core proxy
-  __syncthreads();
-
   if (st == 0 && tid == 0) {
     fence_after_sync();
-    const uint32_t a0 = smem_u32(tile);
-    const uint32_t lbo_z = (uint32_t)(r / 8) * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
+    const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
+    const uint32_t lbo_z = (uint32_t)rg * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
     const uint32_t idz = idesc_bf16(128, r, false, false), idv = idesc_bf16(128, P, false, false);
-    const int kz = (3 * r + P) / 16, kv = r / 16;
+    const uint32_t idq = idesc_bf16(128, r, false, true);   // B = W / m, MN-major
+    const int kz = (3 * r + P) / 16, kv = r / 16, kq = P / 16;
     for (int part = 0; part < 2; ++part) {
       const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
+      const uint32_t bw0 = smem_u32(bw) + (part ? (uint32_t)(P * r * 2) : 0u);
       for (int ks = 0; ks < kz; ++ks)
         mma_bf16(tbase, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz,
                  part > 0 || ks > 0);
       for (int ks = 0; ks < kv; ++ks)
         mma_bf16(tbase + (uint32_t)r, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u),
                  sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv, part > 0 || ks > 0);
+      // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
+      for (int ks = 0; ks < (dzq_on ? kq : 0); ++ks)
+        mma_bf16(tbase + (uint32_t)(r + P), sdesc(ay + 2u * g.grp * ks, g.grp, 128u),
+                 sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq, part > 0 || ks > 0);
     }
     mma_commit(&bar_mma);
+  }
+  // first token of a chunk: (dM_prev - dM) z_{t-1}, z_{t-1} = row 0 of Z-; one warp per row
+  if (st == 0 && c > 0) {
+    const unsigned char* zm = tile + 2 * zg;
+    const float* mprev = dM - d.SW;
+    for (int i = warp; i < r; i += kTokThreads / 32) {
+      float a = 0.f;
+      for (int j = lane; j < r; j += 32)
+        a = fmaf(__ldg(mprev + i * r + j) - __ldg(dM + i * r + j), bf16_at(zm + (size_t)(j / 8) * g.grp, j % 8), a);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) corr[i] = a;
+    }
   }
   if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
     st = 2;
@@ -439,14 +533,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   const int tstar = unpack_t(kmax);
   const float arg = (raw >= kNormClamp && raw > 0.f && t == tstar) ? dm[bh] / raw : 0.f;
   const bool first = (m == 0 && c > 0);
-  __nv_bfloat16* pz = static_cast<__nv_bfloat16*>(dz.p) + (long long)b * dz.sb + (long long)t * dz.st +
-                      (long long)h * dz.sh;
-  __nv_bfloat16* pv = static_cast<__nv_bfloat16*>(dv.p) + (long long)b * dv.sb + (long long)t * dv.st +
-                      (long long)h * dv.sh;
   const float nan = __int_as_float(0x7fc00000);
-  for (int j0 = 0; j0 < r; j0 += 16) {
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  for (int j0 = 0; j0 < r; j0 += 16) {                 // dz
     float x[16];
-    tmem_ld16(tbase + (uint32_t)j0 + ((uint32_t)(32 * warp) << 16), x);
+    tmem_ld16(tbase + lane_base + (uint32_t)j0, x);
     if (live) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
@@ -456,28 +547,29 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
         if (arg != 0.f) a = fmaf(arg, bf16_at(tile + (size_t)(j / 8) * g.grp + (size_t)m * 16, j % 8), a);
         x[e] = st ? nan : a;
       }
-      uint32_t w[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const __nv_bfloat162 pr = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
-        w[e] = *reinterpret_cast<const uint32_t*>(&pr);
-      }
-      reinterpret_cast<uint4*>(pz + j0)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      reinterpret_cast<uint4*>(pz + j0)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      store_bf16x16(tok_ptr(dz, b, t, h) + j0, x);
     }
   }
-  for (int j0 = 0; j0 < P; j0 += 16) {
+  for (int j0 = 0; j0 < P; j0 += 16) {                 // dv
     float x[16];
-    tmem_ld16(tbase + (uint32_t)(r + j0) + ((uint32_t)(32 * warp) << 16), x);
+    tmem_ld16(tbase + lane_base + (uint32_t)(r + j0), x);
     if (live) {
-      uint32_t w[8];
+      if (st) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const __nv_bfloat162 pr = __floats2bfloat162_rn(st ? nan : x[2 * e], st ? nan : x[2 * e + 1]);
-        w[e] = *reinterpret_cast<const uint32_t*>(&pr);
+        for (int e = 0; e < 16; ++e) x[e] = nan;
       }
-      reinterpret_cast<uint4*>(pv + j0)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      reinterpret_cast<uint4*>(pv + j0)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      store_bf16x16(tok_ptr(dv, b, t, h) + j0, x);
+    }
+  }
+  for (int j0 = 0; dzq_on && j0 < r; j0 += 16) {      // dzq
+    float x[16];
+    tmem_ld16(tbase + lane_base + (uint32_t)(r + P + j0), x);
+    if (live) {
+      if (st) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = nan;
+      }
+      store_bf16x16(tok_ptr(dzq, b, t, h) + j0, x);
     }
   }
   if (tid == 0) status[q] = st;
@@ -551,28 +643,55 @@ static size_t tmem_safe_smem(uint32_t ncols, int threads, size_t smem) {
   return smem < need ? need : smem;
 }
 
-bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const Out& dz, const Out& dv) {
+// dzq_on: also dzq = dY (W / m) (needs dy and dzq; W / m from k_bwd_chunk_s)
+bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const In& dy, const Out& dz, const Out& dv,
+                   const Out& dzq, bool dzq_on) {
   if (!stats_tc_ok(d, z, v) || d.CS > 128 || d.P % 16 != 0) return false;
+  if (dzq_on && !stats_tc_ok(d, z, dy)) return false;
   if (tok_geom(d.r, d.P, d.CS).smem > 227u * 1024u - 64u) return false;   // 64 B of static barriers
   const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const auto s8 = [](long long s, long long extent) { return extent == 1 || s % 8 == 0; };
-  // 16-byte vector stores of dz / dv rows
-  return al(dz.p) && al(dv.p) && s8(dz.st, d.T) && s8(dz.sh, d.H) && s8(dz.sb, d.B) && s8(dv.st, d.T) &&
-         s8(dv.sh, d.H) && s8(dv.sb, d.B);
+  const auto out_ok = [&](const Out& o) {   // 16-byte vector stores of token rows
+    return al(o.p) && s8(o.st, d.T) && s8(o.sh, d.H) && s8(o.sb, d.B);
+  };
+  return out_ok(dz) && out_ok(dv) && (!dzq_on || out_ok(dzq));
 }
 
-cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const float* dstats,
-                              const unsigned long long* cmax, const float* dm, const Out& dz, const Out& dv,
-                              int* status, cudaStream_t st) {
-  CUtensorMap mz, mv;
+cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In& dy, const float* dstats,
+                              const unsigned char* wm, const unsigned long long* cmax, const float* dm,
+                              const Out& dz, const Out& dv, const Out& dzq, bool dzq_on, int* status,
+                              cudaStream_t st) {
+  CUtensorMap mz, mv, my;
   if (!token_map(&mz, z, d.B, d.T, d.H, d.r, d.CS) || !token_map(&mv, v, d.B, d.T, d.H, d.P, d.CS))
+    return cudaErrorInvalidValue;
+  if (dzq_on ? !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS) : !token_map(&my, v, d.B, d.T, d.H, d.P, d.CS))
     return cudaErrorInvalidValue;
   const TokGeom g = tok_geom(d.r, d.P, d.CS);
   const size_t smem = tmem_safe_smem(g.ncols, kTokThreads, g.smem);
   cudaError_t e = cudaFuncSetAttribute(k_tok_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const long long n = (long long)d.B * d.H * d.C;
-  k_tok_bwd_tc<<<(unsigned)n, kTokThreads, smem, st>>>(mz, mv, d, g, dstats, cmax, dm, dz, dv, status);
+  k_tok_bwd_tc<<<(unsigned)n, kTokThreads, smem, st>>>(mz, mv, my, d, g, dstats, wm, cmax, dm, dz, dv, dzq, dzq_on,
+                                                         status);
+  return cudaGetLastError();
+}
+
+// dW' needs the A block (P rows) inside one 128-row MMA
+bool dw_tc_ok(const Dims& d, const In& zq, const In& dy) { return d.P <= 128 && stats_tc_ok(d, zq, dy); }
+
+cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st) {
+  CUtensorMap mq, my;
+  if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS) || !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS))
+    return cudaErrorInvalidValue;
+  StatsGeom g = stats_geom(d.r, d.P, d.CS);
+  g.nb = 1;
+  g.ncols = d.r < 32 ? 32u : (uint32_t)d.r;
+  g.smem = (size_t)(d.r / 8 + 16) * g.grp + 128;     // ZQ groups + 16 groups of A rows (P real)
+  const size_t smem = tmem_safe_smem(g.ncols, kStatsThreads, g.smem);
+  cudaError_t e = cudaFuncSetAttribute(k_dw_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const long long n = (long long)d.B * d.H * d.C;
+  k_dw_tc<<<(unsigned)n, kStatsThreads, smem, st>>>(mq, my, d, g, dw, status);
   return cudaGetLastError();
 }
 

@@ -579,6 +579,284 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// backward without the token pass (bf16 token tensors on the tensor-core path)
+//
+// The token-level products leave this kernel: dW' = sum_t dy_t zq_t^T comes from
+// k_dw_tc, and dzq = dy (W / m) is formed by k_tok_bwd_tc from the W / m this
+// kernel writes.  What remains is the chunk operator's chain rule.  The P x r
+// blocks of Cn, W and dW stream through two tiles, so a warp holds 8 tiles
+// whatever P is (7 warps per SM instead of 4 at P = 64).  Also
+//   sum_t dqn_t . zq_t = sum_t dy_t^T W zq_t = <W, dW'>,
+// so the d(max norm) share of the readout needs no tokens either.
+// W / m is stored as bf16 hi and lo planes, each in the MN-major canonical
+// layout of a B operand with N = r and K = P: the 16-byte row of n-group ng and
+// k (= p) sits at byte ng * P * 16 + p * 16.
+// ---------------------------------------------------------------------------
+constexpr int kBwdStreamTiles = 8;
+
+__global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const float* __restrict__ gamma_p,
+                                                                const float* __restrict__ stats,
+                                                                const unsigned long long* __restrict__ cmax,
+                                                                const float* __restrict__ invs_in,
+                                                                const int* __restrict__ flags_in,
+                                                                const float* __restrict__ dwraw,
+                                                                float* __restrict__ dstats,
+                                                                float* __restrict__ dmpart,
+                                                                float* __restrict__ dgpart,
+                                                                unsigned char* __restrict__ wm) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
+  if (q >= (long long)d.B * d.H * d.C) return;
+  const ChunkId id = chunk_id(d, q);
+  const int r = d.r, P = d.P;
+  extern __shared__ float4 sm4[];
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * kBwdStreamTiles * kTile;
+  float* TLi = base;
+  float* TA = TLi + kTile;
+  float* TAK = TA + kTile;
+  float* TV = TAK + kTile;
+  float* TX = TV + kTile;
+  float* TY = TX + kTile;
+  float* TP0 = TY + kTile;
+  float* TP1 = TP0 + kTile;
+  const float* rec = stats + q * d.SW;
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const float gam = *gamma_p;
+  const float gs = fminf(fmaxf(gam, 1.f), 1.5f);
+  const bool gpass = gam >= 1.f && gam <= 1.5f;
+  const float kk = gs * invs_in[q];
+  const int flag = flags_in[q];
+  float t[32], u[32];
+
+  // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
+  factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
+  wmm<32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  ld_gmem_row(t, rec + r * r, lane, r, r, im2);
+  st_row(TX, lane, t);                                                    // TX = Mn
+  __syncwarp();
+  wmm<32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  __syncwarp();
+  ld_row(t, TA, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] *= kk;
+  __syncwarp();
+  st_row(TA, lane, t);                                                    // TA = A
+  __syncwarp();
+  const float* AK = TAK;
+  if (d.K == 0) {
+    st_identity(TAK, lane);
+  } else if (d.K == 1) {
+    AK = TA;
+  } else {
+    const float* cur = TA;
+    for (int s = 1; s < d.K; ++s) {
+      float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
+      wmm<32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
+      __syncwarp();
+      cur = out;
+    }
+  }
+  __syncwarp();
+  wmm<32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  __syncwarp();
+  wmm<32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
+
+  // ---- P blocks: W = Cn V, dW = dW' / m, dV = Cn^T dW, dCn = dW V^T ----
+  float dmq = 0.f, dmc = 0.f;
+  const float* dwq = dwraw + q * (long long)P * r;
+  unsigned char* wq = wm + (size_t)q * P * r * 4;
+#pragma unroll 1
+  for (int pb = 0; pb < p_blocks(P); ++pb) {
+    const int p = pb * 32 + lane;
+    ld_gmem_row(t, rec + 2 * r * r, p, P, r, im);
+    __syncwarp();
+    st_row(TP0, lane, t);                                                 // Cn rows of block pb
+    __syncwarp();
+    wmm<32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
+    __syncwarp();
+    ld_row(u, TP1, lane);
+    ld_gmem_row(t, dwq, p, P, r, 1.f);                                    // dW' rows (raw)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dmq = fmaf(u[j], t[j], dmq);
+    if (p < P) {
+#pragma unroll
+      for (int ng = 0; ng < 4; ++ng) {
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = u[8 * ng + e] * im;
+        uint4 hi, lo;
+        split_bf16x8(x, hi, lo);
+        *reinterpret_cast<uint4*>(wq + (size_t)ng * P * 16 + (size_t)p * 16) = hi;
+        *reinterpret_cast<uint4*>(wq + (size_t)P * r * 2 + (size_t)ng * P * 16 + (size_t)p * 16) = lo;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] *= im;
+    __syncwarp();
+    st_row(TP1, lane, t);                                                 // dW rows
+    __syncwarp();
+    if (pb == 0)
+      wmm<32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
+    else
+      wmm<32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
+    wmm<32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
+    __syncwarp();
+    ld_row(t, TY, lane);
+    ld_row(u, TP0, lane);
+    if (p < P) {
+      float* out = dstats + q * d.SW + 2 * r * r + (size_t)p * r;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < r) {
+          out[j] = t[j] * im;
+          dmc = fmaf(t[j], u[j], dmc);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  // live: TLi, TA, AK, TX (dV); free: TV, TY, TP0, TP1
+  float* TdLi = TP0;
+  float* TdU = TY;
+  float* TU = TP1;
+  float* TdAK = TV;
+  wmm<32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmm<32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  __syncwarp();
+  wmm<32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmm<32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  __syncwarp();
+  wmm<32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  __syncwarp();
+  // dA from dAK; free: TX, TY, TP1, and TAK unless it is A (K = 1)
+  const float* TdA;
+  if (d.K == 0) {
+    zero(t);
+    st_row(TV, lane, t);
+    TdA = TV;
+  } else if (d.K == 1) {
+    TdA = TdAK;
+  } else {
+    // Horner over E_s = dAK (A^T)^s:  E <- E A^T,  H <- E + A^T H,  E = H = dAK at start
+    float* pool[4] = {TX, TY, TP1, TAK};
+    const float* E = TdAK;
+    const float* Hc = TdAK;
+    int pi = 0;
+    for (int s = 1; s < d.K; ++s) {
+      float* En = pool[pi & 3];
+      float* Hn = pool[(pi + 1) & 3];
+      pi += 2;
+      wmm<32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
+      __syncwarp();
+      ld_row(t, En, lane);
+      st_row(Hn, lane, t);
+      __syncwarp();
+      wmm<32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      __syncwarp();
+      E = En;
+      Hc = Hn;
+    }
+    TdA = Hc;
+  }
+  float dg = 0.f;
+  ld_row(t, TdA, lane);
+  ld_row(u, TA, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) dg = fmaf(t[j], u[j], dg);
+  float* fr[3];
+  {
+    float* cand[5] = {TV, TX, TY, TP1, TAK};
+    int nf = 0;
+    for (int i = 0; i < 5 && nf < 3; ++i)
+      if (cand[i] != TdA) fr[nf++] = cand[i];
+  }
+  float* TS = fr[0];
+  float* TdMn = fr[1];
+  float* TdS = fr[2];
+  __syncwarp();
+  wmm<32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
+  __syncwarp();
+  wmm<32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  __syncwarp();
+  float dmm = 0.f;
+  ld_row(t, TdMn, lane);
+  ld_gmem_row(u, rec + r * r, lane, r, r, im2);                           // Mn row
+  if (lane < r) {
+    float* out = dstats + q * d.SW + r * r + (size_t)lane * r;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < r) {
+        out[j] = t[j] * im2;
+        dmm = fmaf(t[j], u[j], dmm);
+      }
+    }
+  }
+  st_row(TS, lane, u);                                                    // TS = Mn (S done)
+  __syncwarp();
+  wmm<32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  __syncwarp();
+  ld_row(t, TdS, lane);
+  ld_col<32>(u, TdS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
+  st_row(TdMn, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  __syncwarp();
+  ld_row(t, TdLi, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
+  st_row(TdLi, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  __syncwarp();
+  ld_row(t, TS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j > lane) t[j] = 0.f;                                             // Pm = tril(-dLi Li^T)
+  __syncwarp();
+  st_row(TS, lane, t);
+  __syncwarp();
+  ld_col<32>(u, TS, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
+  st_row(TdS, lane, t);
+  __syncwarp();
+  wmm<32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  __syncwarp();
+  wmm<32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  __syncwarp();
+  ld_row(t, TdS, lane);
+  ld_col<32>(u, TdS, lane);
+  float grow[32];
+  ld_gmem_row(grow, rec, lane, r, r, 1.f);
+  __syncwarp();
+  st_row(TS, lane, grow);
+  __syncwarp();
+  float gcol[32];
+  ld_col<32>(gcol, TS, lane);
+  float dmg = 0.f;
+  if (lane < r) {
+    float* out = dstats + q * d.SW + (size_t)lane * r;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < r) {
+        const float gsym = 0.5f * (t[j] + u[j]);
+        out[j] = gsym * im2;
+        dmg = fmaf(gsym, 0.5f * (grow[j] + gcol[j]) * im2, dmg);
+      }
+    }
+  }
+  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq * im);
+  const float dgs = warp_sum32(dg);
+  if (lane == 0) {
+    dmpart[q] = -tot / m;
+    dgpart[q] = gpass ? dgs / gs : 0.f;
+  }
+}
 }  // namespace wpc
 
 // ---------------------------------------------------------------------------
@@ -641,6 +919,15 @@ cudaError_t launch_bwd_chunk_w(const Dims& d, const In& zq, const In& dy, const 
     case 3: return launch_w(wpc::k_bwd_chunk_w<IO, 3>, d, pw, st, args);
     default: return launch_w(wpc::k_bwd_chunk_w<IO, 4>, d, pw, st, args);
   }
+}
+
+cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               const float* invs, const int* flags, const float* dwraw, float* dstats,
+                               float* dmpart, float* dgpart, unsigned char* wm, cudaStream_t st) {
+  Dims dd = d;
+  void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags, (void*)&dwraw,
+                  (void*)&dstats, (void*)&dmpart, (void*)&dgpart, (void*)&wm};
+  return launch_w(wpc::k_bwd_chunk_s, d, (size_t)wpc::kBwdStreamTiles * wpc::kTile * sizeof(float), st, args);
 }
 
 template cudaError_t launch_fwd_chunk_w<float>(const Dims&, const In&, const float*, const Out&, const float*,

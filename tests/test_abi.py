@@ -104,10 +104,11 @@ def _contig(base, B, T, H, D):
 
 @pytest.mark.parametrize("kw,dtype,zt,want", [
     # config 2 in bf16, contiguous: every tensor-core kernel + warp chunk operators
-    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK),
+    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD),
     # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
-    # r = 64 (config 3): tensor-core token kernels, one CTA per chunk operator
+    # r = 64 (config 3): tensor-core token kernels, one CTA per chunk operator (which
+    # keeps the readout's token pass)
     (dict(r=64, chunk_size=128), 1, None, TC),
     # chunk 256: tensor-core statistics only
     (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
@@ -118,7 +119,8 @@ def _contig(base, B, T, H, D):
     # token stride not a multiple of 16 bytes: CUDA-core token kernels
     (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
     # decay strategy shares the token kernels
-    (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK),
+    (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None,
+     TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD),
 ])
 def test_kernel_path_selection(built_lib, kw, dtype, zt, want):
     s = _shape(**kw)

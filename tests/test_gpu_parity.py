@@ -148,7 +148,7 @@ def test_fused_projection_strides_tensor_core_stats():
     z = fused[:, :, :H * r].reshape(B, T, H, r)
     zq = fused[:, :, H * r:2 * H * r].reshape(B, T, H, r)
     v = fused[:, :, 2 * H * r:].reshape(B, T, H, P)
-    tc = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD
+    tc = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD | _lib.SKA_PATH_TC_READOUT_BWD
     assert _path(z, v, r, P) & tc == tc
     assert _path(z.contiguous(), v.contiguous(), r, P) & tc == tc
     dy = (torch.randn(B, T, H, P, generator=g)).to(DEV, torch.bfloat16)
@@ -172,7 +172,7 @@ def test_config2_takes_the_tensor_core_statistics_kernel():
     z = torch.empty(8, 2048, 12, 32, dtype=torch.bfloat16, device=DEV)
     v = torch.empty(8, 2048, 12, 64, dtype=torch.bfloat16, device=DEV)
     assert _path(z, v, 32, 64) == (_lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD |
-                                   _lib.SKA_PATH_WARP_CHUNK)
+                                   _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD)
 
 
 def test_deterministic_bitwise():
