@@ -426,8 +426,9 @@ def main(argv=None):
     dom = max(avg_ms, key=avg_ms.get)
     ach = algo[dom] / (avg_ms[dom] / 1e3) / 1e9
     traffic = _ncu_traffic().get(dom)
-    # the step's unique token traffic: forward z, zq, v -> y; backward z, zq, v, dy -> dz, dzq, dv
-    step_algo = B_PER_GPU * L * H * (4 * R + 4 * P) * 2
+    # the step's unique token traffic: forward z, zq, v -> y (2r + 2P); backward z, zq, v, dy -> dz, dzq,
+    # dv (2r + 2P read, 2r + P written): (6r + 5P) bf16 values per token and head
+    step_algo = B_PER_GPU * L * H * (6 * R + 5 * P) * 2
     roofline = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
                 "frac": ach / peak, "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                 "algo_bytes_per_launch": algo[dom],

@@ -3,7 +3,8 @@
 // One warp owns one (batch, head, chunk).  The Cholesky factor, the triangular
 // inverse and the power iteration keep one matrix row per lane in registers and
 // run on shuffles; every matrix product is a warp-level tensor-core tile GEMM
-// (wmm: mma.sync TF32 with a 3-term split, fp32-level accuracy) on the warp's
+// (wmmp: mma.sync TF32; a 3-term split gives fp32-level products for fp32
+// tensors, one round-to-nearest TF32 product serves bf16 tensors) on the warp's
 // swizzled shared-memory tiles.  There are no block barriers.
 //
 // Same algebra as the CTA path in ska_exact.cu, written with
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
                                                                 const unsigned long long* __restrict__ cmax,
                                                                 float* __restrict__ invs_out,
                                                                 int* __restrict__ flags_out) {
+  constexpr bool kFast = kIoExact<IO>;   // bf16 tensors: TF32 chunk algebra
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
   if (q >= (long long)d.B * d.H * d.C) return;   // warp-uniform; no block barriers below
@@ -225,14 +227,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
 
   const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
-  wmm<32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
+  wmmp<kFast, 32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
   {
     float mrow[32];
     ld_gmem_row(mrow, rec + r * r, lane, r, r, im2);
     st_row(T0, lane, mrow);                                               // T0 = Mn
   }
   __syncwarp();
-  wmm<32, 32, false, false, false>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
+  wmmp<kFast, 32, 32, false, false, false>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
   __syncwarp();
   {
     float a[32];
@@ -255,16 +257,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   }
   for (int s = 1; s < d.K; ++s) {
     float* out = (AK == T0) ? T2 : T0;
-    wmm<32, 32, false, false, false>(out, AK, kTile, T3, 1.f);
+    wmmp<kFast, 32, 32, false, false, false>(out, AK, kTile, T3, 1.f);
     __syncwarp();
     AK = out;
   }
   __syncwarp();
   float* TU = (AK == T0) ? T2 : T0;
   float* TV = (d.K == 1) ? T2 : T3;
-  wmm<32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
+  wmmp<kFast, 32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
   __syncwarp();
-  wmm<32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
+  wmmp<kFast, 32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
 #pragma unroll
   for (int pb = 0; pb < NPB; ++pb) {
     float crow[32];
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     st_row(TC + pb * kTile, lane, crow);                                  // Cn rows
   }
   __syncwarp();
-  wmm<32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
+  wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
   __syncwarp();
 
   // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     __syncwarp();
 #pragma unroll
     for (int pb = 0; pb < NPB; ++pb)   // bf16 zq is exact in tf32: split only W / m
-      wmm2<32, 32, false, true, false, !kIoExact<IO>, true>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
+      wmmp<kFast, 32, 32, false, true, false>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
     __syncwarp();
 #pragma unroll
     for (int pb = 0; pb < NPB; ++pb) {
@@ -313,6 +315,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
                                                                 float* __restrict__ dstats,
                                                                 float* __restrict__ dmpart,
                                                                 float* __restrict__ dgpart) {
+  constexpr bool kFast = kIoExact<IO>;   // bf16 tensors: TF32 chunk algebra
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
   if (q >= (long long)d.B * d.H * d.C) return;
@@ -340,11 +343,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
 
   // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
   factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
-  wmm<32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  wmmp<kFast, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
   ld_gmem_row(t, rec + r * r, lane, r, r, im2);
   st_row(TX, lane, t);                                                    // TX = Mn
   __syncwarp();
-  wmm<32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  wmmp<kFast, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
   __syncwarp();
   ld_row(t, TA, lane);
 #pragma unroll
@@ -361,15 +364,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     const float* cur = TA;
     for (int s = 1; s < d.K; ++s) {
       float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
-      wmm<32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
+      wmmp<kFast, 32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
       __syncwarp();
       cur = out;
     }
   }
   __syncwarp();
-  wmm<32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  wmmp<kFast, 32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
   __syncwarp();
-  wmm<32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
+  wmmp<kFast, 32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
 #pragma unroll
   for (int pb = 0; pb < NPB; ++pb) {
     ld_gmem_row(t, rec + 2 * r * r, pb * 32 + lane, P, r, im);
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     st_row(TDW + pb * kTile, lane, t);                                    // dW = 0
   }
   __syncwarp();
-  wmm<32 * NPB, 32, false, false, false>(TW, TDY, kTile, TV, 1.f);  // W = Cn V
+  wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TDY, kTile, TV, 1.f);  // W = Cn V
   __syncwarp();
 
   // ---- token pass: dW += dY^T qn, dqn = dY W  (32 tokens at a time) ----
@@ -396,8 +399,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     }
     __syncwarp();
     // bf16 dy and zq are exact in tf32: dW needs one product per tile, dqn two
-    wmm2<32 * NPB, 32, true, false, true, !kIoExact<IO>, !kIoExact<IO>>(TDW, TDY, kTile, TX, im);  // dW += dY^T qn
-    wmm2<32, 32 * NPB, false, false, false, !kIoExact<IO>, true>(TY, TDY, kTile, TW, 1.f);         // dqn = dY W
+    wmmp<kFast, 32 * NPB, 32, true, false, true>(TDW, TDY, kTile, TX, im);  // dW += dY^T qn
+    wmmp<kFast, 32, 32 * NPB, false, false, false>(TY, TDY, kTile, TW, 1.f);         // dqn = dY W
     __syncwarp();
     ld_row(t, TY, lane);
     st_tok_row<IO>(dzq, id.b, tok, id.h, 0, r, live, t, im);             // dzq = dqn / m
@@ -415,8 +418,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     st_row(TDY + pb * kTile, lane, t);                                    // Cn rows again
   }
   __syncwarp();
-  wmm<32, 32 * NPB, true, false, false>(TX, TDY, kTile, TDW, 1.f);  // TX = dV
-  wmm<32 * NPB, 32, false, true, false>(TW, TDW, kTile, TV, 1.f);   // TW = dCn
+  wmmp<kFast, 32, 32 * NPB, true, false, false>(TX, TDY, kTile, TDW, 1.f);  // TX = dV
+  wmmp<kFast, 32 * NPB, 32, false, true, false>(TW, TDW, kTile, TV, 1.f);   // TW = dCn
   __syncwarp();
   float dmc = 0.f;
 #pragma unroll
@@ -441,13 +444,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   float* TdU = TY;
   float* TU = TDW;
   float* TdAK = TDY;
-  wmm<32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
-  wmm<32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  wmmp<kFast, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmmp<kFast, 32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
   __syncwarp();
-  wmm<32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
-  wmm<32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmmp<kFast, 32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmmp<kFast, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
   __syncwarp();
-  wmm<32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  wmmp<kFast, 32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
   __syncwarp();
   // dA from dAK; free: TV, TX, TY, TDW
   const float* TdA;
@@ -467,12 +470,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
       float* En = pool[pi & 3];
       float* Hn = pool[(pi + 1) & 3];
       pi += 2;
-      wmm<32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
+      wmmp<kFast, 32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
       __syncwarp();
       ld_row(t, En, lane);
       st_row(Hn, lane, t);
       __syncwarp();
-      wmm<32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      wmmp<kFast, 32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
       __syncwarp();
       E = En;
       Hc = Hn;
@@ -497,9 +500,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   float* TdMn = fr[1];
   float* TdS = fr[2];
   __syncwarp();
-  wmm<32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
+  wmmp<kFast, 32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
   __syncwarp();
-  wmm<32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  wmmp<kFast, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
   ld_row(t, TdMn, lane);
@@ -516,7 +519,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   }
   st_row(TS, lane, u);                                                    // TS = Mn (S done)
   __syncwarp();
-  wmm<32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  wmmp<kFast, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -524,7 +527,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
   st_row(TdMn, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  wmmp<kFast, 32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
   __syncwarp();
   ld_row(t, TdLi, lane);
 #pragma unroll
@@ -532,7 +535,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmm<32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  wmmp<kFast, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -546,9 +549,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
   st_row(TdS, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  wmmp<kFast, 32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
   __syncwarp();
-  wmm<32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  wmmp<kFast, 32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -632,11 +635,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
 
   // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
   factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
-  wmm<32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  wmmp<true, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
   ld_gmem_row(t, rec + r * r, lane, r, r, im2);
   st_row(TX, lane, t);                                                    // TX = Mn
   __syncwarp();
-  wmm<32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  wmmp<true, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
   __syncwarp();
   ld_row(t, TA, lane);
 #pragma unroll
@@ -653,15 +656,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     const float* cur = TA;
     for (int s = 1; s < d.K; ++s) {
       float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
-      wmm<32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
+      wmmp<true, 32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
       __syncwarp();
       cur = out;
     }
   }
   __syncwarp();
-  wmm<32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  wmmp<true, 32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
   __syncwarp();
-  wmm<32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
+  wmmp<true, 32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
 
   // ---- P blocks: W = Cn V, dW = dW' / m, dV = Cn^T dW, dCn = dW V^T ----
   float dmq = 0.f, dmc = 0.f;
@@ -674,7 +677,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     __syncwarp();
     st_row(TP0, lane, t);                                                 // Cn rows of block pb
     __syncwarp();
-    wmm<32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
+    wmmp<true, 32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
     __syncwarp();
     ld_row(u, TP1, lane);
     ld_gmem_row(t, dwq, p, P, r, 1.f);                                    // dW' rows (raw)
@@ -698,10 +701,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     st_row(TP1, lane, t);                                                 // dW rows
     __syncwarp();
     if (pb == 0)
-      wmm<32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
+      wmmp<true, 32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
     else
-      wmm<32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
-    wmm<32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
+      wmmp<true, 32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
+    wmmp<true, 32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
     __syncwarp();
     ld_row(t, TY, lane);
     ld_row(u, TP0, lane);
@@ -722,13 +725,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   float* TdU = TY;
   float* TU = TP1;
   float* TdAK = TV;
-  wmm<32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
-  wmm<32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  wmmp<true, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmmp<true, 32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
   __syncwarp();
-  wmm<32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
-  wmm<32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmmp<true, 32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmmp<true, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
   __syncwarp();
-  wmm<32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  wmmp<true, 32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
   __syncwarp();
   // dA from dAK; free: TX, TY, TP1, and TAK unless it is A (K = 1)
   const float* TdA;
@@ -748,12 +751,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
       float* En = pool[pi & 3];
       float* Hn = pool[(pi + 1) & 3];
       pi += 2;
-      wmm<32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
+      wmmp<true, 32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
       __syncwarp();
       ld_row(t, En, lane);
       st_row(Hn, lane, t);
       __syncwarp();
-      wmm<32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      wmmp<true, 32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
       __syncwarp();
       E = En;
       Hc = Hn;
@@ -776,9 +779,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   float* TdMn = fr[1];
   float* TdS = fr[2];
   __syncwarp();
-  wmm<32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
+  wmmp<true, 32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
   __syncwarp();
-  wmm<32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  wmmp<true, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
   ld_row(t, TdMn, lane);
@@ -795,7 +798,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   }
   st_row(TS, lane, u);                                                    // TS = Mn (S done)
   __syncwarp();
-  wmm<32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  wmmp<true, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -803,7 +806,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
   st_row(TdMn, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  wmmp<true, 32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
   __syncwarp();
   ld_row(t, TdLi, lane);
 #pragma unroll
@@ -811,7 +814,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmm<32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  wmmp<true, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -825,9 +828,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
   st_row(TdS, lane, t);
   __syncwarp();
-  wmm<32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  wmmp<true, 32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
   __syncwarp();
-  wmm<32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  wmmp<true, 32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);

@@ -244,6 +244,9 @@ __device__ __forceinline__ void mma_tf32_acc(float (&d)[4], const uint32_t (&a)[
 // of lo.  a*b ~= hi_a hi_b + hi_a lo_b + lo_a hi_b has ~2^-20 relative error, i.e.
 // fp32-level products, at two ALU ops per operand value.  SPLIT = false uses hi only.
 // C may not alias A or B.  All 32 lanes must call.
+__device__ __forceinline__ uint32_t tf32_rn(float x) {
+  return (__float_as_uint(x) + 0x1000u) & 0xffffe000u;   // nearest, ties away from zero
+}
 __device__ __forceinline__ void split_trunc(float x, uint32_t& hi, uint32_t& lo) {
   hi = __float_as_uint(x) & 0xffffe000u;
   lo = __float_as_uint(x - __uint_as_float(hi));
@@ -252,9 +255,11 @@ __device__ __forceinline__ void split_trunc(float x, uint32_t& hi, uint32_t& lo)
 // Not inlined: one copy per shape keeps the kernels small enough for the
 // instruction cache (inlining every call site made instruction fetch the main stall).
 // SA_ / SB_: split that operand (an operand holding bf16 values is exact in tf32 and
-// is passed unsplit).  Two 16-row blocks are processed together so that they share
+// is passed unsplit).  RN_: round unsplit operands to the nearest tf32 value
+// (bits + 0x1000, low 13 bits cleared; exact values stay exact) instead of
+// letting the MMA truncate them.  Two 16-row blocks are processed together so that they share
 // the B fragments; M is a multiple of 32.
-template <int M, int K, bool TA, bool TB, bool ACC, bool SA_, bool SB_>
+template <int M, int K, bool TA, bool TB, bool ACC, bool SA_, bool SB_, bool RN_ = false>
 __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict__ A, int SA,
                                   const float* __restrict__ B, float alpha) {
   static_assert(M % 32 == 0 && K % 8 == 0, "tile shape");
@@ -300,7 +305,7 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
           if (SA_) {
             split_trunc(av[u], ah[h][u], al[h][u]);
           } else {
-            ah[h][u] = __float_as_uint(av[u]);
+            ah[h][u] = RN_ ? tf32_rn(av[u]) : __float_as_uint(av[u]);
             al[h][u] = 0u;
           }
         }
@@ -322,8 +327,8 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
           split_trunc(b0, bh0, bl0);
           split_trunc(b1, bh1, bl1);
         } else {
-          bh0 = __float_as_uint(b0);
-          bh1 = __float_as_uint(b1);
+          bh0 = RN_ ? tf32_rn(b0) : __float_as_uint(b0);
+          bh1 = RN_ ? tf32_rn(b1) : __float_as_uint(b1);
           bl0 = bl1 = 0u;
         }
 #pragma unroll
@@ -359,10 +364,18 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
   }
 }
 
-// fp32-level product of two fp32 tiles
-template <int M, int K, bool TA, bool TB, bool ACC>
-__device__ __forceinline__ void wmm(float* C, const float* A, int SA, const float* B, float alpha) {
-  wmm2<M, K, TA, TB, ACC, true, true>(C, A, SA, B, alpha);
+// Product of two fp32 tiles at the precision the I/O type calls for:
+//   FAST = false (fp32 tensors): 3-term split, fp32-level products;
+//   FAST = true  (bf16 tensors): one TF32 product of round-to-nearest operands,
+//     ~2^-11 relative per product -- the results are stored in bf16 (2^-9), and
+//     through the whole chunk algebra the outputs stay within ~1.5e-3 of fp64.
+template <bool FAST, int M, int K, bool TA, bool TB, bool ACC>
+__device__ __forceinline__ void wmmp(float* C, const float* A, int SA, const float* B, float alpha) {
+  if constexpr (FAST) {
+    wmm2<M, K, TA, TB, ACC, false, false, true>(C, A, SA, B, alpha);
+  } else {
+    wmm2<M, K, TA, TB, ACC, true, true>(C, A, SA, B, alpha);
+  }
 }
 
 }  // namespace wpc
