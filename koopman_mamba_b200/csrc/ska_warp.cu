@@ -3,8 +3,7 @@
 // One warp owns one (batch, head, chunk).  The Cholesky factor, the triangular
 // inverse and the power iteration keep one matrix row per lane in registers and
 // run on shuffles; every matrix product is a warp-level tensor-core tile GEMM
-// (wmmp: mma.sync TF32; a 3-term split gives fp32-level products for fp32
-// tensors, one round-to-nearest TF32 product serves bf16 tensors) on the warp's
+// (wmmp: mma.sync TF32 with a 3-term split, fp32-level products) on the warp's
 // swizzled shared-memory tiles.  There are no block barriers.
 //
 // Same algebra as the CTA path in ska_exact.cu, written with
@@ -25,55 +24,10 @@ constexpr int kMaxWarps = 8;   // chunks (warps) per CTA, fewer when the tiles d
 constexpr size_t kSmemBudget = 227 * 1024;
 constexpr int kTile = 1024;    // floats per 32 x 32 tile
 
-__host__ __device__ inline int p_blocks(int P) { return (P + 31) >> 5; }
 // forward tiles per warp: T0..T3, TC (P rows: Cn, then Y), TW (P rows: W / m)
 __host__ __device__ inline int fwd_tiles(int P) { return 4 + 2 * p_blocks(P); }
 // backward tiles per warp: Li, A, AK, V, X, Y, W[NPB], DY[NPB], DW[NPB]
 __host__ __device__ inline int bwd_tiles(int P) { return 6 + 3 * p_blocks(P); }
-
-__device__ __forceinline__ void build_gram_row(float (&g)[32], const float (&grow)[32], const float (&gcol)[32],
-                                               int lane, int r, float im2, float ridge, float jit) {
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float v;
-    if (lane < r && j < r) {
-      v = 0.5f * (grow[j] * im2 + gcol[j] * im2);   // ska.py:119,138
-      if (j == lane) v += ridge + jit;
-    } else {
-      v = (j == lane) ? 1.f : 0.f;
-    }
-    g[j] = v;
-  }
-}
-
-// Global loads are issued unconditionally from clamped (always valid) addresses and
-// masked afterwards, so that a lane's loads are all in flight together.
-
-// row `row` of the nrows x ncols row-major global matrix src, times `scale`, zero padded
-__device__ __forceinline__ void ld_gmem_row(float (&v)[32], const float* src, int row, int nrows, int ncols,
-                                            float scale) {
-  const bool rv = row < nrows;
-  const float* p = src + (size_t)(rv ? row : 0) * ncols;
-  if (ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-    const float4* p4 = reinterpret_cast<const float4*>(p);
-    float4 x[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) x[q] = __ldg(p4 + q);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      v[4 * q] = rv ? x[q].x * scale : 0.f;
-      v[4 * q + 1] = rv ? x[q].y * scale : 0.f;
-      v[4 * q + 2] = rv ? x[q].z * scale : 0.f;
-      v[4 * q + 3] = rv ? x[q].w * scale : 0.f;
-    }
-  } else {
-    float x[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = __ldg(p + (j < ncols ? j : 0));
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (rv && j < ncols) ? x[j] * scale : 0.f;
-  }
-}
 
 // features [f0, f0 + n) of token t (n <= 32), times `scale`; zero when !valid
 template <typename IO>
@@ -127,30 +81,6 @@ __device__ __forceinline__ void st_tok_row(const Out& x, int b, int t, int h, in
     for (int j = 0; j < 32; ++j)
       if (j < n) store_elem<IO>(p + j, v[j] * scale);
   }
-}
-
-struct ChunkId {
-  long long q, bh;
-  int b, h, c;
-};
-__device__ __forceinline__ ChunkId chunk_id(const Dims& d, long long q) {
-  ChunkId id;
-  id.q = q;
-  id.c = (int)(q % d.C);
-  id.bh = q / d.C;
-  id.h = (int)(id.bh % d.H);
-  id.b = (int)(id.bh / d.H);
-  return id;
-}
-
-__device__ __forceinline__ float series_norm(const unsigned long long* cmax, const ChunkId& id, int C, int lane) {
-  unsigned long long key = 0ull;
-  for (int cc = lane; cc < C; cc += 32) {
-    const unsigned long long x = cmax[id.bh * C + cc];
-    key = x > key ? x : key;
-  }
-  key = warp_max_u64(key);
-  return fmaxf(unpack_norm(key), kNormClamp);
 }
 
 // this lane's row of the identity -> tile T
@@ -207,7 +137,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
                                                                 const unsigned long long* __restrict__ cmax,
                                                                 float* __restrict__ invs_out,
                                                                 int* __restrict__ flags_out) {
-  constexpr bool kFast = kIoExact<IO>;   // bf16 tensors: TF32 chunk algebra
+  constexpr bool kFast = false;   // fp32-level products (split operands) for every I/O type
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
   if (q >= (long long)d.B * d.H * d.C) return;   // warp-uniform; no block barriers below
@@ -315,7 +245,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
                                                                 float* __restrict__ dstats,
                                                                 float* __restrict__ dmpart,
                                                                 float* __restrict__ dgpart) {
-  constexpr bool kFast = kIoExact<IO>;   // bf16 tensors: TF32 chunk algebra
+  constexpr bool kFast = false;   // fp32-level products (split operands) for every I/O type
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
   if (q >= (long long)d.B * d.H * d.C) return;
@@ -635,11 +565,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
 
   // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
   factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
-  wmmp<true, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
+  wmmp<false, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
   ld_gmem_row(t, rec + r * r, lane, r, r, im2);
   st_row(TX, lane, t);                                                    // TX = Mn
   __syncwarp();
-  wmmp<true, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
+  wmmp<false, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
   __syncwarp();
   ld_row(t, TA, lane);
 #pragma unroll
@@ -656,15 +586,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     const float* cur = TA;
     for (int s = 1; s < d.K; ++s) {
       float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
-      wmmp<true, 32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
+      wmmp<false, 32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
       __syncwarp();
       cur = out;
     }
   }
   __syncwarp();
-  wmmp<true, 32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
+  wmmp<false, 32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
   __syncwarp();
-  wmmp<true, 32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
+  wmmp<false, 32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
 
   // ---- P blocks: W = Cn V, dW = dW' / m, dV = Cn^T dW, dCn = dW V^T ----
   float dmq = 0.f, dmc = 0.f;
@@ -677,7 +607,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     __syncwarp();
     st_row(TP0, lane, t);                                                 // Cn rows of block pb
     __syncwarp();
-    wmmp<true, 32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
+    wmmp<false, 32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
     __syncwarp();
     ld_row(u, TP1, lane);
     ld_gmem_row(t, dwq, p, P, r, 1.f);                                    // dW' rows (raw)
@@ -701,10 +631,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     st_row(TP1, lane, t);                                                 // dW rows
     __syncwarp();
     if (pb == 0)
-      wmmp<true, 32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
+      wmmp<false, 32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
     else
-      wmmp<true, 32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
-    wmmp<true, 32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
+      wmmp<false, 32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
+    wmmp<false, 32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
     __syncwarp();
     ld_row(t, TY, lane);
     ld_row(u, TP0, lane);
@@ -725,13 +655,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   float* TdU = TY;
   float* TU = TP1;
   float* TdAK = TV;
-  wmmp<true, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
-  wmmp<true, 32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  wmmp<false, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmmp<false, 32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
   __syncwarp();
-  wmmp<true, 32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
-  wmmp<true, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmmp<false, 32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmmp<false, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
   __syncwarp();
-  wmmp<true, 32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
+  wmmp<false, 32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
   __syncwarp();
   // dA from dAK; free: TX, TY, TP1, and TAK unless it is A (K = 1)
   const float* TdA;
@@ -751,12 +681,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
       float* En = pool[pi & 3];
       float* Hn = pool[(pi + 1) & 3];
       pi += 2;
-      wmmp<true, 32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
+      wmmp<false, 32, 32, false, true, false>(En, E, kTile, TA, 1.f);      // E A^T
       __syncwarp();
       ld_row(t, En, lane);
       st_row(Hn, lane, t);
       __syncwarp();
-      wmmp<true, 32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
+      wmmp<false, 32, 32, true, false, true>(Hn, TA, kTile, Hc, 1.f);      // + A^T H
       __syncwarp();
       E = En;
       Hc = Hn;
@@ -779,9 +709,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   float* TdMn = fr[1];
   float* TdS = fr[2];
   __syncwarp();
-  wmmp<true, 32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
+  wmmp<false, 32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
   __syncwarp();
-  wmmp<true, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
+  wmmp<false, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
   ld_row(t, TdMn, lane);
@@ -798,7 +728,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   }
   st_row(TS, lane, u);                                                    // TS = Mn (S done)
   __syncwarp();
-  wmmp<true, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  wmmp<false, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -806,7 +736,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
   st_row(TdMn, lane, t);
   __syncwarp();
-  wmmp<true, 32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  wmmp<false, 32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
   __syncwarp();
   ld_row(t, TdLi, lane);
 #pragma unroll
@@ -814,7 +744,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmmp<true, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  wmmp<false, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -828,9 +758,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
   st_row(TdS, lane, t);
   __syncwarp();
-  wmmp<true, 32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  wmmp<false, 32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
   __syncwarp();
-  wmmp<true, 32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  wmmp<false, 32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);

@@ -218,6 +218,77 @@ __device__ __forceinline__ float power_sigma32(const float (&a)[32], int lane, i
 }
 
 // ---- tensor-core readout helpers (mma.sync m16n8k8 TF32) ----
+// ---- per-chunk record access shared by the chunk kernels ----
+__host__ __device__ inline int p_blocks(int P) { return (P + 31) >> 5; }
+
+__device__ __forceinline__ void build_gram_row(float (&g)[32], const float (&grow)[32], const float (&gcol)[32],
+                                               int lane, int r, float im2, float ridge, float jit) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float v;
+    if (lane < r && j < r) {
+      v = 0.5f * (grow[j] * im2 + gcol[j] * im2);   // ska.py:119,138
+      if (j == lane) v += ridge + jit;
+    } else {
+      v = (j == lane) ? 1.f : 0.f;
+    }
+    g[j] = v;
+  }
+}
+
+// Global loads are issued unconditionally from clamped (always valid) addresses and
+// masked afterwards, so that a lane's loads are all in flight together.
+
+// row `row` of the nrows x ncols row-major global matrix src, times `scale`, zero padded
+__device__ __forceinline__ void ld_gmem_row(float (&v)[32], const float* src, int row, int nrows, int ncols,
+                                            float scale) {
+  const bool rv = row < nrows;
+  const float* p = src + (size_t)(rv ? row : 0) * ncols;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>(p);
+    float4 x[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] = __ldg(p4 + q);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[4 * q] = rv ? x[q].x * scale : 0.f;
+      v[4 * q + 1] = rv ? x[q].y * scale : 0.f;
+      v[4 * q + 2] = rv ? x[q].z * scale : 0.f;
+      v[4 * q + 3] = rv ? x[q].w * scale : 0.f;
+    }
+  } else {
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __ldg(p + (j < ncols ? j : 0));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rv && j < ncols) ? x[j] * scale : 0.f;
+  }
+}
+
+struct ChunkId {
+  long long q, bh;
+  int b, h, c;
+};
+__device__ __forceinline__ ChunkId chunk_id(const Dims& d, long long q) {
+  ChunkId id;
+  id.q = q;
+  id.c = (int)(q % d.C);
+  id.bh = q / d.C;
+  id.h = (int)(id.bh % d.H);
+  id.b = (int)(id.bh / d.H);
+  return id;
+}
+
+__device__ __forceinline__ float series_norm(const unsigned long long* cmax, const ChunkId& id, int C, int lane) {
+  unsigned long long key = 0ull;
+  for (int cc = lane; cc < C; cc += 32) {
+    const unsigned long long x = cmax[id.bh * C + cc];
+    key = x > key ? x : key;
+  }
+  key = warp_max_u64(key);
+  return fmaxf(unpack_norm(key), kNormClamp);
+}
+
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -364,11 +435,12 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
   }
 }
 
-// Product of two fp32 tiles at the precision the I/O type calls for:
-//   FAST = false (fp32 tensors): 3-term split, fp32-level products;
-//   FAST = true  (bf16 tensors): one TF32 product of round-to-nearest operands,
-//     ~2^-11 relative per product -- the results are stored in bf16 (2^-9), and
-//     through the whole chunk algebra the outputs stay within ~1.5e-3 of fp64.
+// Product of two fp32 tiles:
+//   FAST = false: 3-term split, fp32-level products (what the kernels use);
+//   FAST = true:  one TF32 product of round-to-nearest operands, ~2^-11 relative
+//     per product.  Through the chunk algebra that is ~1.5e-3 at config-2
+//     numerics, but with power_K = 3 and 32-token chunks the backward reached the
+//     2e-2 bf16 bar, so it is not used.
 template <bool FAST, int M, int K, bool TA, bool TB, bool ACC>
 __device__ __forceinline__ void wmmp(float* C, const float* A, int SA, const float* B, float alpha) {
   if constexpr (FAST) {

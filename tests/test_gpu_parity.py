@@ -175,6 +175,20 @@ def test_config2_takes_the_tensor_core_statistics_kernel():
                                    _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD)
 
 
+@pytest.mark.parametrize("K", [0, 1, 3])
+def test_bf16_r32_short_chunks_each_power(K):
+    """bf16, r = 32 with 32-token chunks (early prefixes barely above rank), a
+    partial P block (P = 48), a ragged tail, 21 chunks and each A^K branch,
+    forward and backward, against the oracle: the harder conditioning that pins
+    the chunk algebra's precision."""
+    z, zq, v, dy = _inputs(1, 200, 3, 32, 48, 11 + K)
+    got = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16, chunk_size=32, power_K=K)
+    zb, zqb, vb, dyb = (bf16_round(a) for a in (z, zq, v, dy))
+    ref = ska_core_fwd_bwd(zb, zqb, vb, 1.2, dyb, SkaParams(chunk_size=32, power_K=K))
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
 def test_deterministic_bitwise():
     z, zq, v, dy = _inputs(2, 700, 3, 32, 64, 9)
     a = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16)
