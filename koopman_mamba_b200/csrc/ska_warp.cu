@@ -97,11 +97,7 @@ __device__ __forceinline__ void st_identity(float* T, int lane) {
 __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec, int lane, float im2,
                                                  bool force_jitter, float* Tg, float* TLi) {
   const int r = d.r;
-  {
-    float graw[32];
-    ld_gmem_row(graw, rec, lane, r, r, 1.f);
-    st_row(Tg, lane, graw);
-  }
+  load_mat(Tg, rec, r, r, 1.f, lane);
   __syncwarp();
   float g[32], x[32];
   int flag = 0;
@@ -158,11 +154,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
   wmmp<kFast, 32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
-  {
-    float mrow[32];
-    ld_gmem_row(mrow, rec + r * r, lane, r, r, im2);
-    st_row(T0, lane, mrow);                                               // T0 = Mn
-  }
+  __syncwarp();
+  load_mat(T0, rec + r * r, r, r, im2, lane);                             // T0 = Mn
   __syncwarp();
   wmmp<kFast, 32, 32, false, false, false>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
   __syncwarp();
@@ -198,11 +191,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   __syncwarp();
   wmmp<kFast, 32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
 #pragma unroll
-  for (int pb = 0; pb < NPB; ++pb) {
-    float crow[32];
-    ld_gmem_row(crow, rec + 2 * r * r, pb * 32 + lane, P, r, im);
-    st_row(TC + pb * kTile, lane, crow);                                  // Cn rows
-  }
+  for (int pb = 0; pb < NPB; ++pb)
+    load_mat(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, im, lane);   // Cn rows
   __syncwarp();
   wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
   __syncwarp();
@@ -566,8 +556,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
   factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
   wmmp<false, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
-  ld_gmem_row(t, rec + r * r, lane, r, r, im2);
-  st_row(TX, lane, t);                                                    // TX = Mn
+  __syncwarp();
+  load_mat(TX, rec + r * r, r, r, im2, lane);                             // TX = Mn
   __syncwarp();
   wmmp<false, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
   __syncwarp();
@@ -603,14 +593,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
 #pragma unroll 1
   for (int pb = 0; pb < p_blocks(P); ++pb) {
     const int p = pb * 32 + lane;
-    ld_gmem_row(t, rec + 2 * r * r, p, P, r, im);
     __syncwarp();
-    st_row(TP0, lane, t);                                                 // Cn rows of block pb
+    load_mat(TP0, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, im, lane);   // Cn rows of block pb
     __syncwarp();
     wmmp<false, 32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
     __syncwarp();
     ld_row(u, TP1, lane);
-    ld_gmem_row(t, dwq, p, P, r, 1.f);                                    // dW' rows (raw)
+    load_mat(TY, dwq + pb * 32 * r, P - pb * 32, r, 1.f, lane);           // dW' rows (raw)
+    __syncwarp();
+    ld_row(t, TY, lane);
 #pragma unroll
     for (int j = 0; j < 32; ++j) dmq = fmaf(u[j], t[j], dmq);
     if (p < P) {
@@ -639,15 +630,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     ld_row(t, TY, lane);
     ld_row(u, TP0, lane);
     if (p < P) {
-      float* out = dstats + q * d.SW + 2 * r * r + (size_t)p * r;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (j < r) {
-          out[j] = t[j] * im;
-          dmc = fmaf(t[j], u[j], dmc);
-        }
-      }
+      for (int j = 0; j < 32; ++j)
+        if (j < r) dmc = fmaf(t[j], u[j], dmc);
     }
+    store_mat(dstats + q * d.SW + 2 * r * r + pb * 32 * r, TY, P - pb * 32, r, im, lane);   // dCn / m
     __syncwarp();
   }
   // live: TLi, TA, AK, TX (dV); free: TV, TY, TP0, TP1
@@ -714,20 +701,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   wmmp<false, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
-  ld_row(t, TdMn, lane);
-  ld_gmem_row(u, rec + r * r, lane, r, r, im2);                           // Mn row
-  if (lane < r) {
-    float* out = dstats + q * d.SW + r * r + (size_t)lane * r;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < r) {
-        out[j] = t[j] * im2;
-        dmm = fmaf(t[j], u[j], dmm);
-      }
-    }
-  }
-  st_row(TS, lane, u);                                                    // TS = Mn (S done)
+  load_mat(TS, rec + r * r, r, r, im2, lane);                             // TS = Mn (S done)
+  store_mat(dstats + q * d.SW + r * r, TdMn, r, r, im2, lane);            // dMn / m^2
   __syncwarp();
+  ld_row(t, TdMn, lane);
+  ld_row(u, TS, lane);
+  if (lane < r) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < r) dmm = fmaf(t[j], u[j], dmm);
+  }
   wmmp<false, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
@@ -764,25 +747,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
-  float grow[32];
-  ld_gmem_row(grow, rec, lane, r, r, 1.f);
   __syncwarp();
-  st_row(TS, lane, grow);
+  load_mat(TS, rec, r, r, 1.f, lane);                                     // TS = G (raw)
   __syncwarp();
-  float gcol[32];
+  float grow[32], gcol[32];
+  ld_row(grow, TS, lane);
   ld_col<32>(gcol, TS, lane);
   float dmg = 0.f;
-  if (lane < r) {
-    float* out = dstats + q * d.SW + (size_t)lane * r;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < r) {
-        const float gsym = 0.5f * (t[j] + u[j]);
-        out[j] = gsym * im2;
-        dmg = fmaf(gsym, 0.5f * (grow[j] + gcol[j]) * im2, dmg);
-      }
-    }
+  for (int j = 0; j < 32; ++j) {
+    const float gsym = 0.5f * (t[j] + u[j]);
+    if (lane < r && j < r) dmg = fmaf(gsym, 0.5f * (grow[j] + gcol[j]) * im2, dmg);
+    t[j] = gsym;
   }
+  st_row(TdMn, lane, t);                                                  // T1 is dead: sym(dGn)
+  __syncwarp();
+  store_mat(dstats + q * d.SW, TdMn, r, r, im2, lane);                    // dGn / m^2
   const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq * im);
   const float dgs = warp_sum32(dg);
   if (lane == 0) {

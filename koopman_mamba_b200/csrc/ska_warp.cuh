@@ -265,6 +265,59 @@ __device__ __forceinline__ void ld_gmem_row(float (&v)[32], const float* src, in
   }
 }
 
+// Tile T <- rows [0, nrows) of a row-major nrows x ncols fp32 matrix in global
+// memory, times scale (rows and columns past it zero).  With ncols == 32 and a
+// 16-byte aligned source the warp reads 512 contiguous bytes per instruction
+// (lane-per-row loads touch 32 cache lines per instruction instead).  Rows of T
+// are written by other lanes: synchronise the warp before and after.
+__device__ __forceinline__ void load_mat(float* T, const float* src, int nrows, int ncols, float scale, int lane) {
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int f = 32 * k + lane;
+      v[k] = __ldg(s4 + ((f >> 3) < nrows ? f : 0));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int f = 32 * k + lane, row = f >> 3, q = f & 7;
+      const bool ok = row < nrows;
+      const float4 x = make_float4(ok ? v[k].x * scale : 0.f, ok ? v[k].y * scale : 0.f, ok ? v[k].z * scale : 0.f,
+                                   ok ? v[k].w * scale : 0.f);
+      reinterpret_cast<float4*>(T + row * 32)[q ^ (row & 7)] = x;
+    }
+  } else {
+    float v[32];
+    ld_gmem_row(v, src, lane, nrows, ncols, scale);
+    st_row(T, lane, v);
+  }
+}
+
+// rows [0, nrows) x columns [0, ncols) of tile T, times scale -> row-major global
+// matrix (coalesced when ncols == 32, as load_mat).  Synchronise the warp before.
+__device__ __forceinline__ void store_mat(float* dst, const float* T, int nrows, int ncols, float scale,
+                                          int lane) {
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int f = 32 * k + lane, row = f >> 3, q = f & 7;
+      if (row < nrows) {
+        const float4 x = reinterpret_cast<const float4*>(T + row * 32)[q ^ (row & 7)];
+        reinterpret_cast<float4*>(dst)[f] = make_float4(x.x * scale, x.y * scale, x.z * scale, x.w * scale);
+      }
+    }
+  } else {
+    float v[32];
+    ld_row(v, T, lane);
+    if (lane < nrows) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) dst[(size_t)lane * ncols + j] = v[j] * scale;
+    }
+  }
+}
+
 struct ChunkId {
   long long q, bh;
   int b, h, c;
@@ -382,6 +435,8 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
         }
       }
 #pragma unroll
+      uint32_t bh[4][2], bl[4][2];
+#pragma unroll
       for (int n = 0; n < 4; ++n) {
         float b0, b1;
         if (TB) {
@@ -393,22 +448,33 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
           b0 = B[(k0 + t4) * 32 + ((cc ^ t4) << 2) + g3];
           b1 = B[(k0 + t4 + 4) * 32 + ((cc ^ (t4 + 4)) << 2) + g3];
         }
-        uint32_t bh0, bl0, bh1, bl1;
         if (SB_) {
-          split_trunc(b0, bh0, bl0);
-          split_trunc(b1, bh1, bl1);
+          split_trunc(b0, bh[n][0], bl[n][0]);
+          split_trunc(b1, bh[n][1], bl[n][1]);
         } else {
-          bh0 = RN_ ? tf32_rn(b0) : __float_as_uint(b0);
-          bh1 = RN_ ? tf32_rn(b1) : __float_as_uint(b1);
-          bl0 = bl1 = 0u;
-        }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (SA_) mma_tf32_acc(d[h][n], al[h], bh0, bh1);
-          if (SB_) mma_tf32_acc(d[h][n], ah[h], bl0, bl1);
-          mma_tf32_acc(d[h][n], ah[h], bh0, bh1);
+          bh[n][0] = RN_ ? tf32_rn(b0) : __float_as_uint(b0);
+          bh[n][1] = RN_ ? tf32_rn(b1) : __float_as_uint(b1);
+          bl[n][0] = bl[n][1] = 0u;
         }
       }
+      // term-major issue order: consecutive MMAs update different accumulators, so
+      // the three terms of one accumulator never wait on each other back to back
+      if (SA_) {
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) mma_tf32_acc(d[h][n], al[h], bh[n][0], bh[n][1]);
+      }
+      if (SB_) {
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) mma_tf32_acc(d[h][n], ah[h], bl[n][0], bl[n][1]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) mma_tf32_acc(d[h][n], ah[h], bh[n][0], bh[n][1]);
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
