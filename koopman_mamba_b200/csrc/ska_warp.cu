@@ -124,6 +124,99 @@ __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec
   return flag;
 }
 
+// ---- 32-token blocks of a [B, T, H, D] tensor <-> a 32 x 32 tile, coalesced ----
+// A token row of 32 features is 64 (bf16) or 128 (fp32) contiguous bytes; lanes
+// take consecutive 16-byte pieces of consecutive rows, so one warp instruction
+// touches 8 (bf16) or 4 (fp32) token rows instead of 32.  Used when every row
+// start is 16-byte aligned; otherwise each lane moves its own row.
+template <typename IO>
+__device__ __forceinline__ bool tok_rows_aligned(const void* p, long long sb, long long st, long long sh, int f0,
+                                                 int n) {
+  constexpr int kVec = 16 / sizeof(IO);
+  return n == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && sb % kVec == 0 && st % kVec == 0 &&
+         sh % kVec == 0 && f0 % kVec == 0;
+}
+
+// tile rows [0, 32) <- tokens tok0 + row (rows >= nvalid zero), features [f0, f0 + n)
+template <typename IO>
+__device__ __forceinline__ void load_tok_block(float* Tl, const In& x, int b, int tok0, int h, int f0, int n,
+                                               int nvalid, int lane) {
+  constexpr int kVec = 16 / sizeof(IO);          // elements per 16-byte piece
+  constexpr int kPer = 32 / kVec;                // pieces per token row
+  if (nvalid <= 0) {                             // block past the series end: no loads
+    float v[32];
+    zero(v);
+    st_row(Tl, lane, v);
+  } else if (tok_rows_aligned<IO>(x.p, x.sb, x.st, x.sh, f0, n)) {
+    const IO* base = static_cast<const IO*>(x.p) + (long long)b * x.sb + (long long)h * x.sh + f0;
+    uint4 raw[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
+      raw[k] = __ldg(reinterpret_cast<const uint4*>(base + (long long)(tok0 + (row < nvalid ? row : 0)) * x.st) + pc);
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
+      const bool ok = row < nvalid;
+      const IO* e = reinterpret_cast<const IO*>(&raw[k]);   // registers: plain reads only
+      float v[kVec];
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) v[u] = ok ? to_float(e[u]) : 0.f;
+      float4* rowp = reinterpret_cast<float4*>(Tl + row * 32);
+#pragma unroll
+      for (int c = 0; c < kVec / 4; ++c) {
+        const int q = pc * (kVec / 4) + c;       // 16-byte fp32 chunk of the tile row
+        rowp[q ^ (row & 7)] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      }
+    }
+  } else {
+    float v[32];
+    ld_tok_row<IO>(v, x, b, tok0 + lane, h, f0, n, lane < nvalid, 1.f);
+    st_row(Tl, lane, v);
+  }
+}
+
+// tokens tok0 + row (rows < nvalid), features [f0, f0 + n) <- tile rows
+template <typename IO>
+__device__ __forceinline__ void store_tok_block(const Out& x, int b, int tok0, int h, int f0, int n, int nvalid,
+                                                const float* Tl, int lane) {
+  constexpr int kVec = 16 / sizeof(IO);
+  constexpr int kPer = 32 / kVec;
+  if (tok_rows_aligned<IO>(x.p, x.sb, x.st, x.sh, f0, 32)) {
+    IO* base = static_cast<IO*>(x.p) + (long long)b * x.sb + (long long)h * x.sh + f0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
+      if (row < nvalid && pc * kVec < n) {
+        const float4* rowp = reinterpret_cast<const float4*>(Tl + row * 32);
+        float v[kVec];
+#pragma unroll
+        for (int c = 0; c < kVec / 4; ++c) {
+          const float4 t = rowp[(pc * (kVec / 4) + c) ^ (row & 7)];
+          v[4 * c] = t.x;
+          v[4 * c + 1] = t.y;
+          v[4 * c + 2] = t.z;
+          v[4 * c + 3] = t.w;
+        }
+        IO* dst = base + (long long)(tok0 + row) * x.st + pc * kVec;
+        if constexpr (kVec == 8) {
+          __nv_bfloat162 pr[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) pr[u] = __floats2bfloat162_rn(v[2 * u], v[2 * u + 1]);
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(pr);
+        } else {
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+    }
+  } else {
+    float v[32];
+    ld_row(v, Tl, lane);
+    st_tok_row<IO>(x, b, tok0 + lane, h, f0, n, lane < nvalid, v, 1.f);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
@@ -200,24 +293,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T
   const int tchunk = id.c * CS;
   for (int t0 = 0; t0 < CS; t0 += 32) {
-    const int tl = t0 + lane, tok = tchunk + tl;
-    const bool live = tl < CS && tok < T;
-    {
-      float qr[32];
-      ld_tok_row<IO>(qr, zq, id.b, tok, id.h, 0, r, live, 1.f);
-      st_row(T0, lane, qr);
-    }
+    const int nvalid = min(32, min(CS - t0, T - (tchunk + t0)));
+    load_tok_block<IO>(T0, zq, id.b, tchunk + t0, id.h, 0, r, nvalid, lane);
     __syncwarp();
 #pragma unroll
-    for (int pb = 0; pb < NPB; ++pb)   // bf16 zq is exact in tf32: split only W / m
+    for (int pb = 0; pb < NPB; ++pb)
       wmmp<kFast, 32, 32, false, true, false>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
     __syncwarp();
 #pragma unroll
-    for (int pb = 0; pb < NPB; ++pb) {
-      float yr[32];
-      ld_row(yr, TC + pb * kTile, lane);
-      st_tok_row<IO>(y, id.b, tok, id.h, pb * 32, min(32, P - pb * 32), live, yr, 1.f);
-    }
+    for (int pb = 0; pb < NPB; ++pb)
+      store_tok_block<IO>(y, id.b, tchunk + t0, id.h, pb * 32, min(32, P - pb * 32), nvalid, TC + pb * kTile, lane);
     __syncwarp();
   }
 }
