@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   const ChunkId id = chunk_id(d, q);
   const int r = d.r, P = d.P, CS = d.CS, T = d.T;
   extern __shared__ float4 sm4[];
-  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * (4 + 2 * NPB) * kTile;
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * fwd_tiles(P) * kTile;
   float* T0 = base;
   float* T1 = T0 + kTile;
   float* T2 = T1 + kTile;
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
   const ChunkId id = chunk_id(d, q);
   const int r = d.r, P = d.P, CS = d.CS, T = d.T;
   extern __shared__ float4 sm4[];
-  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * (6 + 3 * NPB) * kTile;
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * bwd_tiles(P) * kTile;
   float* TLi = base;
   float* TA = TLi + kTile;
   float* TAK = TA + kTile;
@@ -862,9 +862,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
 // ---------------------------------------------------------------------------
 bool warp_path_ok(const Dims& d) { return d.r <= 32 && d.P <= 128; }
 
+// Warps (chunks) per CTA: the count that fits the most warps on one SM, given
+// 228 KB of shared memory per SM and 1 KB reserved per resident CTA (ties go to
+// the larger CTA).  0 when one warp's tiles do not fit.
 static int warps_for(size_t per_warp) {
-  const int n = (int)(wpc::kSmemBudget / per_warp);
-  return n < wpc::kMaxWarps ? n : wpc::kMaxWarps;
+  constexpr size_t kSmPerSm = 228 * 1024, kReserve = 1024;
+  int best = 0, best_total = 0;
+  for (int nw = wpc::kMaxWarps; nw >= 1; --nw) {
+    const size_t cta = (size_t)nw * per_warp;
+    if (cta > wpc::kSmemBudget) continue;
+    const int total = (int)(kSmPerSm / (cta + kReserve)) * nw;
+    if (total > best_total) {
+      best_total = total;
+      best = nw;
+    }
+  }
+  return best;
 }
 static size_t fwd_warp_bytes(const Dims& d) { return (size_t)wpc::fwd_tiles(d.P) * wpc::kTile * sizeof(float); }
 static size_t bwd_warp_bytes(const Dims& d) { return (size_t)wpc::bwd_tiles(d.P) * wpc::kTile * sizeof(float); }
