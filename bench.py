@@ -134,9 +134,8 @@ def run_reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "compute": "bf16 token tensors and tensor-core operands (fp32 values as bf16 hi+lo pairs), "
-                       "fp32 accumulation; fp32 Cholesky, inverse and power iteration",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "compute": "numpy fp32 on the host cores (the reference's fp32 upcast of the bf16 tensors)",
         "data": "synthetic (seeded N(0,1)/8 inputs, bf16-rounded)",
         "config": {"workload": WORKLOAD, "path": "reference CPU path: numpy oracle port of "
                    "koopman_lm/ska.py (PyTorch backend) fwd+bwd, fp32", "io_dtype": "bf16-rounded"},
@@ -456,8 +455,9 @@ def main(argv=None):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "compute": "bf16 token tensors and tensor-core operands (fp32 values as bf16 hi+lo pairs), "
-                       "fp32 accumulation; fp32 Cholesky, inverse and power iteration",
+            "compute": "bf16 token tensors; token-level tcgen05 products (fp32 operands as bf16 hi+lo "
+                       "pairs); chunk algebra as 3-term-split TF32 mma.sync (fp32-level); fp32 accumulation, "
+                       "Cholesky, inverse and power iteration",
             "data": "synthetic (seeded N(0,1)/8 inputs, N(0,1) upstream grad)",
             "config": {"workload": WORKLOAD, "B_per_gpu": B_PER_GPU, "H": H, "L": L, "P": P, "r": R, "chunk": CS,
                        "power_K": K, "io_dtype": "bf16", "parallelism": f"dp{world} (batch shards, no collective)",
