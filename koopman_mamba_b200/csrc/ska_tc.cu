@@ -28,10 +28,16 @@ namespace tc {
 constexpr int kStatsThreads = 128;     // 4 warps: TMEM lanes 0-127, one row each
 constexpr uint32_t kTmemCols = 512;    // TMEM columns per SM
 
+// Two tile layouts.  sw = 0: 16-byte feature groups, no swizzle (ska_tc.cuh).
+// sw = 1 (r and P multiples of 32): TMA boxes of 32 features (64-byte token rows)
+// in the 64-byte swizzle, one "atom column" of CS rows x 64 B per 32 features; the
+// MN-major operand then has LBO = CS * 64 (next 32 features) and SBO = 512 (next
+// 8 tokens).  Wider rows halve the L2 -> SM sectors of 16-byte rows.
 struct StatsGeom {
   int nb;              // 128-row MMA blocks covering the 2r + P statistic rows
   uint32_t ncols;      // TMEM columns allocated (power of two >= 32)
-  uint32_t grp;        // bytes of one feature group: CS tokens x 16 B
+  uint32_t grp;        // bytes of one feature group (CS x 16 B), or of one atom column (CS x 64 B)
+  int sw;              // 1: 64-byte swizzled atom columns
   size_t smem;         // dynamic shared memory
 };
 
@@ -41,8 +47,9 @@ __host__ __device__ inline StatsGeom stats_geom(int r, int P, int CS) {
   uint32_t need = (uint32_t)(g.nb * r), c = 32;
   while (c < need) c <<= 1;
   g.ncols = c;
-  g.grp = (uint32_t)CS * 16u;
-  g.smem = (size_t)g.nb * 16 * g.grp + 128;    // + alignment slack
+  g.sw = (r % 32 == 0 && P % 32 == 0) ? 1 : 0;
+  g.grp = (uint32_t)CS * (g.sw ? 64u : 16u);
+  g.smem = (size_t)g.nb * (g.sw ? 4 : 16) * g.grp + 1024;    // + alignment slack (swizzle atoms)
   return g;
 }
 
@@ -62,7 +69,7 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
   __shared__ uint32_t tmem_slot;
   __shared__ unsigned long long red[kStatsThreads / 32];
   unsigned char* tile =
-      smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);   // TMA destinations: 128-B aligned
+      smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // TMA destinations: 1024-B aligned
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long q = blockIdx.x;                                  // (b, h, c), c fastest
   const int c = (int)(q % d.C);
@@ -70,9 +77,10 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
   const int h = (int)(bh % d.H), b = (int)(bh / d.H);
   const int r = d.r, P = d.P, CS = d.CS, T = d.T;
   const int rows = 2 * r + P;
-  unsigned char* tz = tile;                            // Z   : r/8 groups
-  unsigned char* tzp = tile + (size_t)(r / 8) * g.grp; // Z+  : r/8 groups (tokens shifted by one)
-  unsigned char* tv = tile + (size_t)(r / 4) * g.grp;  // V   : P/8 groups
+  const int fpg = g.sw ? 32 : 8;                       // features per group / atom column
+  unsigned char* tz = tile;                            // Z   : r/fpg groups
+  unsigned char* tzp = tile + (size_t)(r / fpg) * g.grp;     // Z+  : tokens shifted by one
+  unsigned char* tv = tile + (size_t)(2 * r / fpg) * g.grp;  // V   : P/fpg groups
 
   if (tid == 0) {
     mbar_init(&bar_load, 1);
@@ -90,11 +98,11 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 
   if (tid == 0) {
     mbar_expect_tx(&bar_load, (uint32_t)rows * (uint32_t)CS * 2u);
-    for (int k = 0; k < r / 8; ++k) {
-      tma_load_4d(tz + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0, b);
-      tma_load_4d(tzp + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 + 1, b);
+    for (int k = 0; k < r / fpg; ++k) {
+      tma_load_4d(tz + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0, b);
+      tma_load_4d(tzp + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0 + 1, b);
     }
-    for (int k = 0; k < P / 8; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, &bar_load, 8 * k, h, t0, b);
+    for (int k = 0; k < P / fpg; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, &bar_load, fpg * k, h, t0, b);
   }
   int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
@@ -107,9 +115,15 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
     const uint32_t id = idesc_bf16(128, r, true, true);
     const uint32_t a0 = smem_u32(tile), b0 = smem_u32(tz);
     for (int mb = 0; mb < g.nb; ++mb)
-      for (int ks = 0; ks < CS / 16; ++ks)
-        mma_bf16(tbase + (uint32_t)(mb * r), sdesc(a0 + (uint32_t)mb * 16u * g.grp + 256u * ks, 128u, g.grp),
-                 sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+      for (int ks = 0; ks < CS / 16; ++ks) {
+        if (g.sw)   // 16 tokens = two 8-row groups of 512 B; 32 features per atom column
+          mma_bf16(tbase + (uint32_t)(mb * r), sdesc_sw(a0 + (uint32_t)mb * 4u * g.grp + 1024u * ks, g.grp, 512u,
+                                                        kSwizzle64),
+                   sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
+        else
+          mma_bf16(tbase + (uint32_t)(mb * r), sdesc(a0 + (uint32_t)mb * 16u * g.grp + 256u * ks, 128u, g.grp),
+                   sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+      }
     mma_commit(&bar_mma);
   }
 
@@ -120,13 +134,18 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
       const int t = t0 + k;
       if (t >= T) break;
       float s = 0.f;
-      for (int gi = 0; gi < r / 8; ++gi) {
-        const uint4 u = *reinterpret_cast<const uint4*>(tz + (size_t)gi * g.grp + (size_t)k * 16);
-        s = sq2(u.x, s);
-        s = sq2(u.y, s);
-        s = sq2(u.z, s);
-        s = sq2(u.w, s);
-      }
+      // no swizzle: token row k is 16 B in each group; 64-byte swizzle: 64 B in each
+      // atom column at (k/8)*512 + (k%8)*64, its 16-byte pieces permuted (summed anyway)
+      const int pieces = g.sw ? 4 : 1;
+      const size_t roff = g.sw ? (size_t)(k >> 3) * 512 + (size_t)(k & 7) * 64 : (size_t)k * 16;
+      for (int gi = 0; gi < r / fpg; ++gi)
+        for (int pc = 0; pc < pieces; ++pc) {
+          const uint4 u = *reinterpret_cast<const uint4*>(tz + (size_t)gi * g.grp + roff + 16 * pc);
+          s = sq2(u.x, s);
+          s = sq2(u.y, s);
+          s = sq2(u.z, s);
+          s = sq2(u.w, s);
+        }
       const unsigned long long kk = pack_max(sqrtf(s), t);
       key = kk > key ? kk : key;
     }
@@ -190,15 +209,16 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint64_t bar_load, bar_mma;
   __shared__ uint32_t tmem_slot;
-  unsigned char* tile = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  unsigned char* tile = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long q = blockIdx.x;
   const int c = (int)(q % d.C);
   const long long bh = q / d.C;
   const int h = (int)(bh % d.H), b = (int)(bh / d.H);
   const int r = d.r, P = d.P, CS = d.CS;
-  unsigned char* tq = tile;                            // ZQ : r/8 groups
-  unsigned char* ty = tile + (size_t)(r / 8) * g.grp;  // dY : P/8 groups (+ room for rows P..127)
+  const int fpg = g.sw ? 32 : 8;                       // features per group / atom column
+  unsigned char* tq = tile;                            // ZQ : r/fpg groups
+  unsigned char* ty = tile + (size_t)(r / fpg) * g.grp;     // dY : P/fpg groups (+ room for rows P..127)
 
   if (tid == 0) {
     mbar_init(&bar_load, 1);
@@ -215,8 +235,8 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
   const int t0 = c * CS;
   if (tid == 0) {
     mbar_expect_tx(&bar_load, (uint32_t)(r + P) * (uint32_t)CS * 2u);
-    for (int k = 0; k < r / 8; ++k) tma_load_4d(tq + (size_t)k * g.grp, &mzq, &bar_load, 8 * k, h, t0, b);
-    for (int k = 0; k < P / 8; ++k) tma_load_4d(ty + (size_t)k * g.grp, &mdy, &bar_load, 8 * k, h, t0, b);
+    for (int k = 0; k < r / fpg; ++k) tma_load_4d(tq + (size_t)k * g.grp, &mzq, &bar_load, fpg * k, h, t0, b);
+    for (int k = 0; k < P / fpg; ++k) tma_load_4d(ty + (size_t)k * g.grp, &mdy, &bar_load, fpg * k, h, t0, b);
   }
   int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
@@ -228,7 +248,11 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
     const uint32_t id = idesc_bf16(128, r, true, true);
     const uint32_t a0 = smem_u32(ty), b0 = smem_u32(tq);
     for (int ks = 0; ks < CS / 16; ++ks)
-      mma_bf16(tbase, sdesc(a0 + 256u * ks, 128u, g.grp), sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+      if (g.sw)
+        mma_bf16(tbase, sdesc_sw(a0 + 1024u * ks, g.grp, 512u, kSwizzle64),
+                 sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
+      else
+        mma_bf16(tbase, sdesc(a0 + 256u * ks, 128u, g.grp), sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
     mma_commit(&bar_mma);
   }
   if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
@@ -485,6 +509,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   if (st == 0 && tid == 0) {
     fence_after_sync();
     const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
+    // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
+    const auto tok_adesc = [&](uint32_t a, int ks) -> uint64_t { return sdesc(a + 2u * g.grp * ks, g.grp, 128u); };
     const uint32_t lbo_z = (uint32_t)rg * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
     const uint32_t idz = idesc_bf16(128, r, false, false), idv = idesc_bf16(128, P, false, false);
     const uint32_t idq = idesc_bf16(128, r, false, true);   // B = W / m, MN-major
@@ -493,15 +519,14 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
       const uint32_t bw0 = smem_u32(bw) + (part ? (uint32_t)(P * r * 2) : 0u);
       for (int ks = 0; ks < kz; ++ks)
-        mma_bf16(tbase, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz,
-                 part > 0 || ks > 0);
+        mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
       for (int ks = 0; ks < kv; ++ks)
-        mma_bf16(tbase + (uint32_t)r, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u),
-                 sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv, part > 0 || ks > 0);
+        mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
+                 part > 0 || ks > 0);
       // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
       for (int ks = 0; ks < (dzq_on ? kq : 0); ++ks)
-        mma_bf16(tbase + (uint32_t)(r + P), sdesc(ay + 2u * g.grp * ks, g.grp, 128u),
-                 sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq, part > 0 || ks > 0);
+        mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq,
+                 part > 0 || ks > 0);
     }
     mma_commit(&bar_mma);
   }
@@ -512,7 +537,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     for (int i = warp; i < r; i += kTokThreads / 32) {
       float a = 0.f;
       for (int j = lane; j < r; j += 32)
-        a = fmaf(__ldg(mprev + i * r + j) - __ldg(dM + i * r + j), bf16_at(zm + (size_t)(j / 8) * g.grp, j % 8), a);
+        a = fmaf(__ldg(mprev + i * r + j) - __ldg(dM + i * r + j),
+                 bf16_at(zm + (size_t)(j / 8) * g.grp, j % 8), a);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
       if (lane == 0) corr[i] = a;
@@ -607,7 +633,7 @@ static bool stride_ok(long long s_elems, long long extent) {
 // increasing stride for the usual layouts); box {8, 1, CS, 1}: one feature group
 // of CS tokens of one head (16-byte rows), i.e. one column of canonical core
 // matrices.  Tokens outside [0, T) read as zeros.
-static bool token_map(CUtensorMap* m, const In& x, int B, int T, int H, int D, int CS) {
+static bool token_map(CUtensorMap* m, const In& x, int B, int T, int H, int D, int CS, bool sw64 = false) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (!fn) return false;
   const auto sub = [](long long s, long long extent) -> cuuint64_t {
@@ -615,11 +641,11 @@ static bool token_map(CUtensorMap* m, const In& x, int B, int T, int H, int D, i
   };
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[3] = {sub(x.sh, H), sub(x.st, T), sub(x.sb, B)};
-  cuuint32_t box[4] = {8, 1, (cuuint32_t)CS, 1};
+  cuuint32_t box[4] = {sw64 ? 32u : 8u, 1, (cuuint32_t)CS, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(x.p), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool stats_tc_ok(const Dims& d, const In& z, const In& v) {
@@ -662,11 +688,11 @@ cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In&
                               const Out& dz, const Out& dv, const Out& dzq, bool dzq_on, int* status,
                               cudaStream_t st) {
   CUtensorMap mz, mv, my;
+  const TokGeom g = tok_geom(d.r, d.P, d.CS);
   if (!token_map(&mz, z, d.B, d.T, d.H, d.r, d.CS) || !token_map(&mv, v, d.B, d.T, d.H, d.P, d.CS))
     return cudaErrorInvalidValue;
   if (dzq_on ? !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS) : !token_map(&my, v, d.B, d.T, d.H, d.P, d.CS))
     return cudaErrorInvalidValue;
-  const TokGeom g = tok_geom(d.r, d.P, d.CS);
   const size_t smem = tmem_safe_smem(g.ncols, kTokThreads, g.smem);
   cudaError_t e = cudaFuncSetAttribute(k_tok_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -681,12 +707,13 @@ bool dw_tc_ok(const Dims& d, const In& zq, const In& dy) { return d.P <= 128 && 
 
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st) {
   CUtensorMap mq, my;
-  if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS) || !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS))
-    return cudaErrorInvalidValue;
   StatsGeom g = stats_geom(d.r, d.P, d.CS);
+  if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS, g.sw) || !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS, g.sw))
+    return cudaErrorInvalidValue;
   g.nb = 1;
   g.ncols = d.r < 32 ? 32u : (uint32_t)d.r;
-  g.smem = (size_t)(d.r / 8 + 16) * g.grp + 128;     // ZQ groups + 16 groups of A rows (P real)
+  // ZQ groups + the groups of 128 A rows (P real)
+  g.smem = g.sw ? (size_t)(d.r / 32 + 4) * g.grp + 1024 : (size_t)(d.r / 8 + 16) * g.grp + 1024;
   const size_t smem = tmem_safe_smem(g.ncols, kStatsThreads, g.smem);
   cudaError_t e = cudaFuncSetAttribute(k_dw_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -698,9 +725,9 @@ cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, i
 cudaError_t launch_stats_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
                             int* status, cudaStream_t st) {
   CUtensorMap mz, mv;
-  if (!token_map(&mz, z, d.B, d.T, d.H, d.r, d.CS) || !token_map(&mv, v, d.B, d.T, d.H, d.P, d.CS))
-    return cudaErrorInvalidValue;
   const StatsGeom g = stats_geom(d.r, d.P, d.CS);
+  if (!token_map(&mz, z, d.B, d.T, d.H, d.r, d.CS, g.sw) || !token_map(&mv, v, d.B, d.T, d.H, d.P, d.CS, g.sw))
+    return cudaErrorInvalidValue;
   const size_t smem = tmem_safe_smem(g.ncols, kStatsThreads, g.smem);
   cudaError_t e = cudaFuncSetAttribute(k_stats_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

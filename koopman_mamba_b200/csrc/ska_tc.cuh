@@ -77,6 +77,11 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46);
 }
+// the same with a swizzle layout code in bits 61-63 (SWIZZLE_64B = 4; checked on B200)
+__device__ __forceinline__ uint64_t sdesc_sw(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return sdesc(saddr, lbo, sbo) | ((uint64_t)layout << 61);
+}
+constexpr uint32_t kSwizzle64 = 4;
 // instruction descriptor: bf16 x bf16 -> f32, A/B major-ness (1 = MN-major), M x N
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
