@@ -96,13 +96,16 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
   const uint32_t tbase = tmem_slot;
   const int t0 = c * CS;
 
-  if (tid == 0) {
-    mbar_expect_tx(&bar_load, (uint32_t)rows * (uint32_t)CS * 2u);
-    for (int k = 0; k < r / fpg; ++k) {
-      tma_load_4d(tz + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0, b);
-      tma_load_4d(tzp + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0 + 1, b);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (lane == 0) {
+      mbar_expect_tx(&bar_load, (uint32_t)rows * (uint32_t)CS * 2u);
+      for (int k = 0; k < r / fpg; ++k) {
+        tma_load_4d(tz + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0, b);
+        tma_load_4d(tzp + (size_t)k * g.grp, &mz, &bar_load, fpg * k, h, t0 + 1, b);
+      }
+      for (int k = 0; k < P / fpg; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, &bar_load, fpg * k, h, t0, b);
     }
-    for (int k = 0; k < P / fpg; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, &bar_load, fpg * k, h, t0, b);
+    __syncwarp();
   }
   int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
@@ -110,21 +113,24 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
     mbar_wait(&bar_load, 0);                           // let copies in flight land
   }
 
-  if (st == 0 && tid == 0) {
-    fence_after_sync();
-    const uint32_t id = idesc_bf16(128, r, true, true);
-    const uint32_t a0 = smem_u32(tile), b0 = smem_u32(tz);
-    for (int mb = 0; mb < g.nb; ++mb)
-      for (int ks = 0; ks < CS / 16; ++ks) {
-        if (g.sw)   // 16 tokens = two 8-row groups of 512 B; 32 features per atom column
-          mma_bf16(tbase + (uint32_t)(mb * r), sdesc_sw(a0 + (uint32_t)mb * 4u * g.grp + 1024u * ks, g.grp, 512u,
-                                                        kSwizzle64),
-                   sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
-        else
-          mma_bf16(tbase + (uint32_t)(mb * r), sdesc(a0 + (uint32_t)mb * 16u * g.grp + 256u * ks, 128u, g.grp),
-                   sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
-      }
-    mma_commit(&bar_mma);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (st == 0 && lane == 0) {
+      fence_after_sync();
+      const uint32_t id = idesc_bf16(128, r, true, true);
+      const uint32_t a0 = smem_u32(tile), b0 = smem_u32(tz);
+      for (int mb = 0; mb < g.nb; ++mb)
+        for (int ks = 0; ks < CS / 16; ++ks) {
+          if (g.sw)   // 16 tokens = two 8-row groups of 512 B; 32 features per atom column
+            mma_bf16(tbase + (uint32_t)(mb * r), sdesc_sw(a0 + (uint32_t)mb * 4u * g.grp + 1024u * ks, g.grp, 512u,
+                                                          kSwizzle64),
+                     sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
+          else
+            mma_bf16(tbase + (uint32_t)(mb * r), sdesc(a0 + (uint32_t)mb * 16u * g.grp + 256u * ks, 128u, g.grp),
+                     sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+        }
+      mma_commit(&bar_mma);
+    }
+    __syncwarp();
   }
 
   // key-norm maximum over the chunk's real tokens, overlapping the MMAs
@@ -233,27 +239,33 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
   fence_after_sync();
   const uint32_t tbase = tmem_slot;
   const int t0 = c * CS;
-  if (tid == 0) {
-    mbar_expect_tx(&bar_load, (uint32_t)(r + P) * (uint32_t)CS * 2u);
-    for (int k = 0; k < r / fpg; ++k) tma_load_4d(tq + (size_t)k * g.grp, &mzq, &bar_load, fpg * k, h, t0, b);
-    for (int k = 0; k < P / fpg; ++k) tma_load_4d(ty + (size_t)k * g.grp, &mdy, &bar_load, fpg * k, h, t0, b);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (lane == 0) {
+      mbar_expect_tx(&bar_load, (uint32_t)(r + P) * (uint32_t)CS * 2u);
+      for (int k = 0; k < r / fpg; ++k) tma_load_4d(tq + (size_t)k * g.grp, &mzq, &bar_load, fpg * k, h, t0, b);
+      for (int k = 0; k < P / fpg; ++k) tma_load_4d(ty + (size_t)k * g.grp, &mdy, &bar_load, fpg * k, h, t0, b);
+    }
+    __syncwarp();
   }
   int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
     st = 1;
     mbar_wait(&bar_load, 0);
   }
-  if (st == 0 && tid == 0) {
-    fence_after_sync();
-    const uint32_t id = idesc_bf16(128, r, true, true);
-    const uint32_t a0 = smem_u32(ty), b0 = smem_u32(tq);
-    for (int ks = 0; ks < CS / 16; ++ks)
-      if (g.sw)
-        mma_bf16(tbase, sdesc_sw(a0 + 1024u * ks, g.grp, 512u, kSwizzle64),
-                 sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
-      else
-        mma_bf16(tbase, sdesc(a0 + 256u * ks, 128u, g.grp), sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
-    mma_commit(&bar_mma);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (st == 0 && lane == 0) {
+      fence_after_sync();
+      const uint32_t id = idesc_bf16(128, r, true, true);
+      const uint32_t a0 = smem_u32(ty), b0 = smem_u32(tq);
+      for (int ks = 0; ks < CS / 16; ++ks)
+        if (g.sw)
+          mma_bf16(tbase, sdesc_sw(a0 + 1024u * ks, g.grp, 512u, kSwizzle64),
+                   sdesc_sw(b0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
+        else
+          mma_bf16(tbase, sdesc(a0 + 256u * ks, 128u, g.grp), sdesc(b0 + 256u * ks, 128u, g.grp), id, ks > 0);
+      mma_commit(&bar_mma);
+    }
+    __syncwarp();
   }
   if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
     st = 2;
@@ -429,19 +441,22 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   fence_after_sync();
   const uint32_t tbase = tmem_slot;
 
-  if (tid == 0) {
-    const uint32_t tok_bytes = (uint32_t)(3 * r + (dzq_on ? 2 : 1) * P) * (uint32_t)CS * 2u;
-    mbar_expect_tx(&bar_load, tok_bytes + (dzq_on ? g.wbytes : 0u));
-    for (int k = 0; k < rg; ++k) {
-      tma_load_4d(tile + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0, b);
-      tma_load_4d(tile + zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 + 1, b);
-      tma_load_4d(tile + 2 * zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 - 1, b);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (lane == 0) {
+      const uint32_t tok_bytes = (uint32_t)(3 * r + (dzq_on ? 2 : 1) * P) * (uint32_t)CS * 2u;
+      mbar_expect_tx(&bar_load, tok_bytes + (dzq_on ? g.wbytes : 0u));
+      for (int k = 0; k < rg; ++k) {
+        tma_load_4d(tile + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0, b);
+        tma_load_4d(tile + zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 + 1, b);
+        tma_load_4d(tile + 2 * zg + (size_t)k * g.grp, &mz, &bar_load, 8 * k, h, t0 - 1, b);
+      }
+      for (int k = 0; k < P / 8; ++k) {
+        tma_load_4d(tile + 3 * zg + (size_t)k * g.grp, &mv, &bar_load, 8 * k, h, t0, b);
+        if (dzq_on) tma_load_4d(tile + dyg + (size_t)k * g.grp, &mdy, &bar_load, 8 * k, h, t0, b);
+      }
+      if (dzq_on) bulk_load(bw, wm + (size_t)q * g.wbytes, g.wbytes, &bar_load);
     }
-    for (int k = 0; k < P / 8; ++k) {
-      tma_load_4d(tile + 3 * zg + (size_t)k * g.grp, &mv, &bar_load, 8 * k, h, t0, b);
-      if (dzq_on) tma_load_4d(tile + dyg + (size_t)k * g.grp, &mdy, &bar_load, 8 * k, h, t0, b);
-    }
-    if (dzq_on) bulk_load(bw, wm + (size_t)q * g.wbytes, g.wbytes, &bar_load);
+    __syncwarp();
   }
 
   // Bz = [(dG + dG^T); dM; dM^T; dC] and Bv = dC^T as K-major operands (overlapping
@@ -506,29 +521,32 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     mbar_wait(&bar_load, 0);
   }
 
-  if (st == 0 && tid == 0) {
-    fence_after_sync();
-    const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
-    // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
-    const auto tok_adesc = [&](uint32_t a, int ks) -> uint64_t { return sdesc(a + 2u * g.grp * ks, g.grp, 128u); };
-    const uint32_t lbo_z = (uint32_t)rg * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
-    const uint32_t idz = idesc_bf16(128, r, false, false), idv = idesc_bf16(128, P, false, false);
-    const uint32_t idq = idesc_bf16(128, r, false, true);   // B = W / m, MN-major
-    const int kz = (3 * r + P) / 16, kv = r / 16, kq = P / 16;
-    for (int part = 0; part < 2; ++part) {
-      const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
-      const uint32_t bw0 = smem_u32(bw) + (part ? (uint32_t)(P * r * 2) : 0u);
-      for (int ks = 0; ks < kz; ++ks)
-        mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
-      for (int ks = 0; ks < kv; ++ks)
-        mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
-                 part > 0 || ks > 0);
-      // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
-      for (int ks = 0; ks < (dzq_on ? kq : 0); ++ks)
-        mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq,
-                 part > 0 || ks > 0);
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (st == 0 && lane == 0) {
+      fence_after_sync();
+      const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
+      // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
+      const auto tok_adesc = [&](uint32_t a, int ks) -> uint64_t { return sdesc(a + 2u * g.grp * ks, g.grp, 128u); };
+      const uint32_t lbo_z = (uint32_t)rg * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
+      const uint32_t idz = idesc_bf16(128, r, false, false), idv = idesc_bf16(128, P, false, false);
+      const uint32_t idq = idesc_bf16(128, r, false, true);   // B = W / m, MN-major
+      const int kz = (3 * r + P) / 16, kv = r / 16, kq = P / 16;
+      for (int part = 0; part < 2; ++part) {
+        const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
+        const uint32_t bw0 = smem_u32(bw) + (part ? (uint32_t)(P * r * 2) : 0u);
+        for (int ks = 0; ks < kz; ++ks)
+          mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
+        for (int ks = 0; ks < kv; ++ks)
+          mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
+                   part > 0 || ks > 0);
+        // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
+        for (int ks = 0; ks < (dzq_on ? kq : 0); ++ks)
+          mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq,
+                   part > 0 || ks > 0);
+      }
+      mma_commit(&bar_mma);
     }
-    mma_commit(&bar_mma);
+    __syncwarp();
   }
   // first token of a chunk: (dM_prev - dM) z_{t-1}, z_{t-1} = row 0 of Z-; one warp per row
   if (st == 0 && c > 0) {
