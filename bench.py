@@ -263,6 +263,7 @@ def _kernel_algo_bytes(tokens_heads):
     wrec = P * R * 4                       # dW' record / W planes
     return {
         "k_fwd_stats": tokens_heads * (R + P) * es + chunks * rec,          # z, v -> records
+        "k_stats_scan": tokens_heads * (R + P) * es + chunks * rec,         # z, v -> scanned records
         "k_scan_fwd": 2 * chunks * rec,                                      # records in place
         "k_fwd_chunk": tokens_heads * (R + P) * es + chunks * rec,          # records, zq -> y
         "k_dw": tokens_heads * (R + P) * es + chunks * wrec,                # zq, dy -> dW'
@@ -360,7 +361,12 @@ def main(argv=None):
     # ---- timed region: K steps, device-timed per step, L2 flushed in between ----
     ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    per_kernel = {k: [] for k in KERNELS}
+    # statistics and scan are one kernel where the layout takes the fused path
+    fused_scan = lib.ska_kernel_path(byref(shape), BF16, byref(D["z"]), byref(D["v"])) & _lib.SKA_PATH_FUSED_SCAN
+    names = ("k_stats_scan",) + KERNELS[2:] if fused_scan else KERNELS
+    # profile-event pairs bounding each forward kernel
+    fwd_pairs = ((0, 2), (2, 3)) if fused_scan else ((0, 1), (1, 2), (2, 3))
+    per_kernel = {k: [] for k in names}
     clocks = ClockSampler()
     clocks.start(local)
     barrier()
@@ -372,9 +378,9 @@ def main(argv=None):
         step()
         ev1[i].record(stream)
         kev[-1].synchronize()
-        spans = [kev[j].elapsed_time(kev[j + 1]) for j in (0, 1, 2)] + \
+        spans = [kev[a].elapsed_time(kev[b]) for a, b in fwd_pairs] + \
                 [kev[j].elapsed_time(kev[j + 1]) for j in (4, 5, 6, 7)]
-        for k, ms in zip(KERNELS, spans):
+        for k, ms in zip(names, spans):
             per_kernel[k].append(ms)
     torch.cuda.synchronize()
     barrier()
@@ -416,7 +422,8 @@ def main(argv=None):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     lib.ska_set_profile_events(None, 0)
-    launches_per_step = 7   # stats, scan, chunk operators; dW', chunk backward, scan, token backward
+    # stats (+ scan), chunk operators; dW', chunk backward, scan, token backward
+    launches_per_step = 6 if fused_scan else 7
 
     # ---- roofline of the dominant kernel ----
     peak, peak_kind = _measured_peaks()

@@ -153,11 +153,15 @@ int ska_set_profile_events(void* const* events, int count);
  *                        too, and the chunk operators' backward without a token
  *                        pass (TC_TOKEN_BWD and WARP_CHUNK, with zq, dy and dzq
  *                        laid out like z and v); otherwise inside the chunk
- *                        kernel */
+ *                        kernel
+ *   SKA_PATH_FUSED_SCAN  the forward statistics and their prefix scan in one
+ *                        kernel, one CTA per (batch, head) series (TC_STATS,
+ *                        r = 32, P <= 64 and B * H >= 64); otherwise two */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
 #define SKA_PATH_TC_READOUT_BWD 8
+#define SKA_PATH_FUSED_SCAN 16
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Forward with no allocation anywhere (no counterpart in the reference, whose

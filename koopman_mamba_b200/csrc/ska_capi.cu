@@ -22,6 +22,7 @@ size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
 namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
+bool stats_scan_tc_ok(const Dims& d, const In& z, const In& v);
 }
 template <typename IO>
 void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
@@ -136,6 +137,7 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   if ((rc = check_tensor(z, es, true, &iz)) || (rc = check_tensor(v, es, true, &iv))) return rc;
   int mask = 0;
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
+  if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_scan_tc_ok(d, iz, iv)) mask |= SKA_PATH_FUSED_SCAN;
   if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
   if (io_dtype == SKA_DTYPE_BF16) {   // gradients and zq, dy assumed laid out like z and v
     const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};

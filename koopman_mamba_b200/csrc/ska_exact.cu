@@ -936,6 +936,9 @@ cudaError_t launch_bwd_chunk_w(const Dims&, const In&, const In&, const float*, 
 
 namespace tc {
 bool stats_tc_ok(const Dims& d, const In& z, const In& v);
+bool stats_scan_tc_ok(const Dims& d, const In& z, const In& v);
+cudaError_t launch_stats_scan_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
+                                 int* status, cudaStream_t st);
 cudaError_t launch_stats_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
                             int* status, cudaStream_t st);
 bool tok_bwd_tc_ok(const Dims& d, const In& z, const In& v, const In& dy, const Out& dz, const Out& dv,
@@ -998,14 +1001,18 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if ((e = set_smem(k_fwd_stats<IO>, s1)) != cudaSuccess) return e;
   if ((e = set_smem(k_fwd_chunk<IO>, s3)) != cudaSuccess) return e;
   prof_record(0, st);
+  bool fused = false;   // statistics and scan in one kernel
   if (tc_stats_path<IO>(d, z, v)) {
     int* status = reinterpret_cast<int*>(saved + L.status);
-    if ((e = tc::launch_stats_tc(d, z, v, stats, cmax, status, st)) != cudaSuccess) return e;
+    fused = tc::stats_scan_tc_ok(d, z, v);
+    e = fused ? tc::launch_stats_scan_tc(d, z, v, stats, cmax, status, st)
+              : tc::launch_stats_tc(d, z, v, stats, cmax, status, st);
+    if (e != cudaSuccess) return e;
   } else {
     k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
   }
   prof_record(1, st);
-  k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
+  if (!fused) k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   prof_record(2, st);
   if (warp_path_ok(d)) {
     if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, y, stats, cmax, invs, flags, st)) != cudaSuccess) return e;

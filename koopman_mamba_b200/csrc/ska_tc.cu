@@ -15,12 +15,14 @@
 // (1: TMA, 2: MMA), waits once more (bounded) for the copies or MMAs in flight,
 // poisons the chunk's record with NaN so that it cannot pass silently, frees its
 // TMEM and returns.
+#include <algorithm>
 #include <mutex>
 
 #include <cudaTypedefs.h>
 
 #include "ska_common.cuh"
 #include "ska_tc.cuh"
+#include "ska_warp.cuh"
 
 namespace ska {
 namespace tc {
@@ -195,6 +197,221 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
   }
   fence_before_sync();
   __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, g.ncols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_stats_scan_tc: the statistics and their exclusive (decayed) scan in one pass,
+// one CTA per (batch, head) series, walking the series' chunks in order
+// (ska.py:114-133, adaptive_chunking.py:225-238).  Warp-specialised:
+//   warp 0             TMA copies of chunk c into shared stage c % ns and the
+//                      product of chunk c into TMEM buffer c % kScanBufs (the
+//                      warp waits together, one lane issues);
+//   warps 1-4          record rows: warp w reads TMEM lane quarter w % 4 (rows
+//                      32 (w % 4) ..), keeps those rows' running prefix in
+//                      registers and writes
+//                        record c = prefix;  prefix = alpha prefix + chunk c
+//                      (alpha = 1: standard) through a per-warp shared tile as
+//                      512-byte warp stores;
+//   warps 5, 6         the key-norm maximum of the even / odd chunks from the
+//                      shared stage (one token per lane).
+// The roles meet only at mbarriers: copy landed, product done, TMEM buffer read,
+// stage read (by the product and by the key norms).  This replaces k_stats_tc + k_scan_fwd (the scan's read and rewrite
+// of every record) when there are enough series to occupy the SMs (r = 32,
+// 2r + P <= 128: one 128-row product per chunk).
+// ---------------------------------------------------------------------------
+constexpr int kScanThreads = 224;
+constexpr int kScanStagesMax = 6;
+constexpr int kScanBufs = 4;
+
+__global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_constant__ CUtensorMap mz,
+                                                                 const __grid_constant__ CUtensorMap mv, Dims d,
+                                                                 StatsGeom g, int ns, float* __restrict__ stats,
+                                                                 unsigned long long* __restrict__ cmax,
+                                                                 int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t bar_load[kScanStagesMax], bar_free[kScanStagesMax], bar_mma[kScanBufs], bar_read[kScanBufs];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int err;
+  unsigned char* tiles = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long bh = blockIdx.x;
+  const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T, C = d.C;
+  const int rows = 2 * r + P;
+  const int fpg = g.sw ? 32 : 8;
+  const size_t tile_bytes = (size_t)g.nb * (g.sw ? 4 : 16) * g.grp;
+  const uint32_t bufcols = (uint32_t)(g.nb * r);      // TMEM columns of one chunk's product
+  float* recs = stats + bh * (long long)C * d.SW;
+
+  if (tid == 0) {
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(&bar_load[i], 1);
+      mbar_init(&bar_free[i], 2);   // product done + key norms read
+    }
+    for (int i = 0; i < kScanBufs; ++i) {
+      mbar_init(&bar_mma[i], 1);
+      mbar_init(&bar_read[i], 4);
+    }
+    err = 0;
+    mbar_fence_init();
+    tma_prefetch_map(&mz);
+    tma_prefetch_map(&mv);
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, g.ncols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {
+    // ---- copies and products: the warp waits together, one lane issues ----
+    const auto load_chunk = [&](int c) {
+      unsigned char* tz = tiles + (size_t)(c % ns) * tile_bytes;
+      unsigned char* tzp = tz + (size_t)(r / fpg) * g.grp;
+      unsigned char* tv = tz + (size_t)(2 * r / fpg) * g.grp;
+      uint64_t* bar = &bar_load[c % ns];
+      const int t0 = c * CS;
+      mbar_expect_tx(bar, (uint32_t)rows * (uint32_t)CS * 2u);
+      for (int k = 0; k < r / fpg; ++k) {
+        tma_load_4d(tz + (size_t)k * g.grp, &mz, bar, fpg * k, h, t0, b);
+        tma_load_4d(tzp + (size_t)k * g.grp, &mz, bar, fpg * k, h, t0 + 1, b);
+      }
+      for (int k = 0; k < P / fpg; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, bar, fpg * k, h, t0, b);
+    };
+    const uint32_t id = idesc_bf16(128, r, true, true);
+    int nload = min(ns, C), nmma = 0;   // chunks copied / multiplied so far
+    bool ok = true;
+    if (lane == 0)
+      for (int c = 0; c < nload; ++c) load_chunk(c);
+    __syncwarp();
+    for (int c = 0; c < C; ++c) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u));
+      if (ok && c >= kScanBufs)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[c % kScanBufs], (uint32_t)(c / kScanBufs - 1) & 1u));
+      if (!ok) break;
+      if (lane == 0) {
+        fence_after_sync();
+        const uint32_t a0 = smem_u32(tiles + (size_t)(c % ns) * tile_bytes);
+        const uint32_t acc = tbase + (uint32_t)(c % kScanBufs) * bufcols;
+        for (int mb = 0; mb < g.nb; ++mb)
+          for (int ks = 0; ks < CS / 16; ++ks) {
+            if (g.sw)
+              mma_bf16(acc + (uint32_t)(mb * r),
+                       sdesc_sw(a0 + (uint32_t)mb * 4u * g.grp + 1024u * ks, g.grp, 512u, kSwizzle64),
+                       sdesc_sw(a0 + 1024u * ks, g.grp, 512u, kSwizzle64), id, ks > 0);
+            else
+              mma_bf16(acc + (uint32_t)(mb * r), sdesc(a0 + (uint32_t)mb * 16u * g.grp + 256u * ks, 128u, g.grp),
+                       sdesc(a0 + 256u * ks, 128u, g.grp), id, ks > 0);
+          }
+        mma_commit(&bar_mma[c % kScanBufs]);
+      }
+      __syncwarp();
+      nmma = c + 1;
+      // chunk c - 1's stage is free once its product is done and its norms are read
+      if (c >= 1 && c - 1 + ns < C) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[(c - 1) % ns], (uint32_t)((c - 1) / ns) & 1u));
+        if (!ok) break;
+        if (lane == 0) load_chunk(c - 1 + ns);
+        __syncwarp();
+        nload = c + ns;
+      }
+    }
+    if (!ok) {   // a wait ran out: flag it and let the copies and products in flight finish
+      if (lane == 0) {
+        atomicExch(&err, 1);
+        for (int s = 0; s < ns; ++s) {
+          int last = -1;
+          for (int c = s; c < nload; c += ns) last = c;
+          if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
+        }
+        for (int s = 0; s < kScanBufs; ++s) {
+          int last = -1;
+          for (int c = s; c < nmma; c += kScanBufs) last = c;
+          if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kScanBufs) & 1u);
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp <= 4) {
+    // ---- record rows ----
+    const int q = warp & 3;   // TMEM lane quarter this warp may read
+    const int row0 = 32 * q, nrow = min(32, rows - row0);
+    float* wtile = reinterpret_cast<float*>(tiles + (size_t)ns * tile_bytes) + (warp - 1) * 1024;
+    const float alpha = d.decay ? d.alpha : 1.f;
+    float pre[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pre[j] = 0.f;
+    for (int c = 0; c < C; ++c) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[c % kScanBufs], (uint32_t)(c / kScanBufs) & 1u))) {
+        if (lane == 0) atomicExch(&err, 1);
+        break;
+      }
+      fence_after_sync();
+      if (warp == 1 && lane == 0) mbar_arrive(&bar_free[c % ns]);   // the product has read the stage
+      float v[32], out[32];
+      tmem_ld32(tbase + (uint32_t)(c % kScanBufs) * bufcols + ((uint32_t)row0 << 16), v);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_read[c % kScanBufs]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        out[j] = pre[j];
+        pre[j] = fmaf(alpha, pre[j], v[j]);
+      }
+      if (nrow > 0) {
+        __syncwarp();
+        wpc::st_row(wtile, lane, out);
+        __syncwarp();
+        wpc::store_mat(recs + (long long)c * d.SW + (size_t)row0 * 32, wtile, nrow, 32, 1.f, lane);
+      }
+    }
+  } else {
+    // ---- key norms: warp 5 takes the even chunks, warp 6 the odd ones ----
+    for (int c = warp - 5; c < C; c += 2) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u))) {
+        if (lane == 0) atomicExch(&err, 1);
+        break;
+      }
+      const unsigned char* tz = tiles + (size_t)(c % ns) * tile_bytes;
+      const int t0 = c * CS;
+      unsigned long long key = 0ull;
+      for (int k = lane; k < CS; k += 32) {   // the token's 64-byte row: four 16-byte units
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const size_t off = g.sw ? (size_t)(k >> 3) * 512 + (size_t)(k & 7) * 64 + 16 * u
+                                  : (size_t)u * g.grp + (size_t)k * 16;
+          const uint4 x = *reinterpret_cast<const uint4*>(tz + off);
+          s0 = sq2(x.x, s0);
+          s1 = sq2(x.y, s1);
+          s2 = sq2(x.z, s2);
+          s3 = sq2(x.w, s3);
+        }
+        const unsigned long long kk = t0 + k < T ? pack_max(sqrtf((s0 + s1) + (s2 + s3)), t0 + k) : 0ull;
+        key = kk > key ? kk : key;
+      }
+      // warp arg-max: largest norm (its bits order like the value), then smallest token
+      const uint32_t nb = (uint32_t)(key >> 32), nt = (uint32_t)key;
+      const uint32_t mb = __reduce_max_sync(0xffffffffu, nb);
+      const uint32_t mt = __reduce_max_sync(0xffffffffu, nb == mb ? nt : 0u);
+      if (lane == 0) {
+        cmax[bh * C + c] = ((unsigned long long)mb << 32) | mt;
+        status[bh * C + c] = 0;
+        mbar_arrive(&bar_free[c % ns]);
+      }
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (err) {   // poison the series
+    const float nan = __int_as_float(0x7fc00000);
+    for (long long i = tid; i < (long long)C * d.SW; i += kScanThreads) recs[i] = nan;
+    for (int c = tid; c < C; c += kScanThreads) status[bh * C + c] = 1;
+  }
   if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tbase, g.ncols);
@@ -737,6 +954,32 @@ cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, i
   if (e != cudaSuccess) return e;
   const long long n = (long long)d.B * d.H * d.C;
   k_dw_tc<<<(unsigned)n, kStatsThreads, smem, st>>>(mq, my, d, g, dw, status);
+  return cudaGetLastError();
+}
+
+bool stats_scan_tc_ok(const Dims& d, const In& z, const In& v) {
+  // r = 32 and 2r + P <= 128: one 128-row product, one 32-float record row per thread
+  return (long long)d.B * d.H >= 64 && d.r == 32 && 2 * d.r + d.P <= 128 && stats_tc_ok(d, z, v);
+}
+
+cudaError_t launch_stats_scan_tc(const Dims& d, const In& z, const In& v, float* stats, unsigned long long* cmax,
+                                 int* status, cudaStream_t st) {
+  CUtensorMap mz, mv;
+  StatsGeom g = stats_geom(d.r, d.P, d.CS);
+  if (!token_map(&mz, z, d.B, d.T, d.H, d.r, d.CS, g.sw) || !token_map(&mv, v, d.B, d.T, d.H, d.P, d.CS, g.sw))
+    return cudaErrorInvalidValue;
+  // as many copy stages as fit next to the record warps' tiles (2 .. kScanStagesMax)
+  const size_t tile_bytes = (size_t)g.nb * (g.sw ? 4 : 16) * g.grp, fixed = 4 * 4096 + 1024;
+  const int ns = (int)std::min<size_t>(kScanStagesMax, (200u * 1024u - fixed) / tile_bytes);
+  if (ns < 2) return cudaErrorInvalidValue;
+  g.smem = (size_t)ns * tile_bytes + fixed;
+  uint32_t c = 32;
+  while (c < (uint32_t)(kScanBufs * g.nb * d.r)) c <<= 1;   // the product buffers
+  g.ncols = c;
+  cudaError_t e = cudaFuncSetAttribute(k_stats_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+  if (e != cudaSuccess) return e;
+  k_stats_scan_tc<<<(unsigned)((long long)d.B * d.H), kScanThreads, g.smem, st>>>(mz, mv, d, g, ns, stats, cmax,
+                                                                                 status);
   return cudaGetLastError();
 }
 

@@ -434,7 +434,6 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
           }
         }
       }
-#pragma unroll
       uint32_t bh[4][2], bl[4][2];
 #pragma unroll
       for (int n = 0; n < 4; ++n) {

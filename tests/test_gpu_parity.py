@@ -172,7 +172,26 @@ def test_config2_takes_the_tensor_core_statistics_kernel():
     z = torch.empty(8, 2048, 12, 32, dtype=torch.bfloat16, device=DEV)
     v = torch.empty(8, 2048, 12, 64, dtype=torch.bfloat16, device=DEV)
     assert _path(z, v, 32, 64) == (_lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD |
-                                   _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD)
+                                   _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD |
+                                   _lib.SKA_PATH_FUSED_SCAN)
+
+
+@pytest.mark.parametrize("alpha", [None, 0.9])
+def test_fused_statistics_scan_ragged(alpha):
+    """64 series (enough for the one-CTA-per-series statistics + scan kernel), a
+    ragged tail chunk, the standard and the decayed scan, forward and backward,
+    against the oracle."""
+    from koopman_mamba_b200 import _lib
+    zt = torch.empty(4, 300, 16, 32, dtype=torch.bfloat16, device=DEV)
+    vt = torch.empty(4, 300, 16, 64, dtype=torch.bfloat16, device=DEV)
+    assert _path(zt, vt, 32, 64) & _lib.SKA_PATH_FUSED_SCAN
+    z, zq, v, dy = _inputs(4, 300, 16, 32, 64, 21)
+    kw = {} if alpha is None else dict(chunk_strategy="decay", decay_alpha=alpha)
+    got = run_cuda(z, zq, v, 1.1, dy, torch.bfloat16, **kw)
+    zb, zqb, vb, dyb = (bf16_round(a) for a in (z, zq, v, dy))
+    ref = ska_core_fwd_bwd(zb, zqb, vb, 1.1, dyb, SkaParams(decay_alpha=alpha))
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
 
 
 @pytest.mark.parametrize("K", [0, 1, 3])
