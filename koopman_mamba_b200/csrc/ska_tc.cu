@@ -219,9 +219,9 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 //   warps 5, 6         the key-norm maximum of the even / odd chunks from the
 //                      shared stage (one token per lane).
 // The roles meet only at mbarriers: copy landed, product done, TMEM buffer read,
-// stage read (by the product and by the key norms).  This replaces k_stats_tc + k_scan_fwd (the scan's read and rewrite
-// of every record) when there are enough series to occupy the SMs (r = 32,
-// 2r + P <= 128: one 128-row product per chunk).
+// stage read (by the product and by the key norms).  This replaces k_stats_tc +
+// k_scan_fwd (the scan's read and rewrite of every record) when there are enough
+// series to occupy the SMs (r = 32, 2r + P <= 128: one 128-row product per chunk).
 // ---------------------------------------------------------------------------
 constexpr int kScanThreads = 224;
 constexpr int kScanStagesMax = 6;
@@ -683,44 +683,83 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   const float* dG = dstats + q * d.SW;
   const float* dM = dG + r * r;
   const float* dC = dG + 2 * r * r;
-  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups 0 .. r/8: dG + dG^T
-    const int n = it / rg, kg = it % rg;
-    float x[8];
-    load_row8(dG + n * r + kg * 8, x);
+  // series arg-max key: warp 0's first load goes out with the operand loads
+  unsigned long long kmx = 0ull;
+  if (warp == 0 && lane < d.C) kmx = cmax[bh * d.C + lane];
+  if (r == 32 && P <= 64) {
+    // every global load of this thread's operand values first, then the splits
+    // and stores: one round trip to L2 instead of one per operand block
+    const int n1 = tid >> 2, k1 = tid & 3;   // dG + dG^T and dM^T items: n, k-group
+    const int k2 = tid >> 5, n2 = tid & 31;  // dM items: k-group, n
+    float a[8], at[8], bm[8], cm[8], c4[2][8], c5[2][8];
+    load_row8(dG + n1 * 32 + k1 * 8, a);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] += __ldg(dG + (kg * 8 + e) * r + n);
-    store_split(bzh, bzl, kg * r + n, x);
-  }
-  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/8 .. r/4: dM
-    const int kg = it / r, n = it % r;
-    float x[8];
+    for (int e = 0; e < 8; ++e) at[e] = __ldg(dG + (k1 * 8 + e) * 32 + n1);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = __ldg(dM + (kg * 8 + e) * r + n);
-    store_split(bzh, bzl, (rg + kg) * r + n, x);
-  }
-  for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/4 .. 3r/8: dM^T
-    const int n = it / rg, kg = it % rg;
-    float x[8];
-    load_row8(dM + n * r + kg * 8, x);
-    store_split(bzh, bzl, (2 * rg + kg) * r + n, x);
-  }
-  for (int it = tid; it < (P / 8) * r; it += kTokThreads) {        // k-groups 3r/8 ..: dC
-    const int kg = it / r, n = it % r;
-    float x[8];
+    for (int e = 0; e < 8; ++e) bm[e] = __ldg(dM + (k2 * 8 + e) * 32 + n2);
+    load_row8(dM + n1 * 32 + k1 * 8, cm);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = __ldg(dC + (kg * 8 + e) * r + n);
-    store_split(bzh, bzl, (3 * rg + kg) * r + n, x);
+    for (int i = 0; i < 2; ++i) {
+      const int it = tid + kTokThreads * i;  // < 4P: dC item (k-group it / 32, n it % 32), Bv item (p it / 4, i-group it % 4)
+      if (it < 4 * P) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) c4[i][e] = __ldg(dC + ((it >> 5) * 8 + e) * 32 + (it & 31));
+        load_row8(dC + (it >> 2) * 32 + (it & 3) * 8, c5[i]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[e] += at[e];
+    store_split(bzh, bzl, k1 * 32 + n1, a);             // k-groups 0 .. 3: dG + dG^T
+    store_split(bzh, bzl, (4 + k2) * 32 + n2, bm);      // k-groups 4 .. 7: dM
+    store_split(bzh, bzl, (8 + k1) * 32 + n1, cm);      // k-groups 8 .. 11: dM^T
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int it = tid + kTokThreads * i;
+      if (it < 4 * P) {
+        store_split(bzh, bzl, (12 + (it >> 5)) * 32 + (it & 31), c4[i]);   // k-groups 12 ..: dC
+        store_split(bvh, bvl, (it & 3) * P + (it >> 2), c5[i]);            // Bv[p][i] = dC[p][i]
+      }
+    }
+  } else {
+    for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups 0 .. r/8: dG + dG^T
+      const int n = it / rg, kg = it % rg;
+      float x[8];
+      load_row8(dG + n * r + kg * 8, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] += __ldg(dG + (kg * 8 + e) * r + n);
+      store_split(bzh, bzl, kg * r + n, x);
+    }
+    for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/8 .. r/4: dM
+      const int kg = it / r, n = it % r;
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __ldg(dM + (kg * 8 + e) * r + n);
+      store_split(bzh, bzl, (rg + kg) * r + n, x);
+    }
+    for (int it = tid; it < rg * r; it += kTokThreads) {             // k-groups r/4 .. 3r/8: dM^T
+      const int n = it / rg, kg = it % rg;
+      float x[8];
+      load_row8(dM + n * r + kg * 8, x);
+      store_split(bzh, bzl, (2 * rg + kg) * r + n, x);
+    }
+    for (int it = tid; it < (P / 8) * r; it += kTokThreads) {        // k-groups 3r/8 ..: dC
+      const int kg = it / r, n = it % r;
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __ldg(dC + (kg * 8 + e) * r + n);
+      store_split(bzh, bzl, (3 * rg + kg) * r + n, x);
+    }
+    for (int it = tid; it < rg * P; it += kTokThreads) {             // Bv[p][i] = dC[p][i]
+      const int p = it / rg, ig = it % rg;
+      float x[8];
+      load_row8(dC + p * r + ig * 8, x);
+      store_split(bvh, bvl, ig * P + p, x);
+    }
   }
-  for (int it = tid; it < rg * P; it += kTokThreads) {             // Bv[p][i] = dC[p][i]
-    const int p = it / rg, ig = it % rg;
-    float x[8];
-    load_row8(dC + p * r + ig * 8, x);
-    store_split(bvh, bvl, ig * P + p, x);
-  }
-  // series arg-max key
+  // series arg-max key (the first 32 chunks' keys were loaded above)
   if (warp == 0) {
-    unsigned long long k = 0ull;
-    for (int i = lane; i < d.C; i += 32) {
+    unsigned long long k = kmx;
+    for (int i = lane + 32; i < d.C; i += 32) {
       const unsigned long long x = cmax[bh * d.C + i];
       k = x > k ? x : k;
     }
