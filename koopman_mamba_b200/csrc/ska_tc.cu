@@ -533,8 +533,10 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
 // already split, in the layout the backward chunk kernel wrote.  Each product
 // runs once per half on the tensor cores, accumulating in fp32 in TMEM.  The
 // first token's dM fix-up, the arg-max term and the bf16 stores are the
-// epilogue.  Requires CS <= 128 (one 128-row MMA block; rows past CS are
-// ignored), r in {32, 64}, P % 16 == 0.
+// epilogue.  Requires CS <= 128 (one 64-row MMA block for CS <= 64, else one
+// 128-row block; rows past CS are ignored), r in {32, 64}, P % 16 == 0.  An
+// M = 64 accumulator puts row i in TMEM lane 32 (i / 16) + i % 16 (checked on
+// B200), so each warp's epilogue takes 16 tokens.
 // ---------------------------------------------------------------------------
 constexpr int kTokThreads = 128;
 
@@ -592,6 +594,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 // bf16 element e of a 16-byte token row -> float
+__device__ __forceinline__ void ld_row8_s(const float* src, float (&x)[8]) {   // shared memory
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  const float4 b = *reinterpret_cast<const float4*>(src + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
 __device__ __forceinline__ float bf16_at(const unsigned char* row, int e) {
   const uint16_t u = *reinterpret_cast<const uint16_t*>(row + 2 * e);
   return __uint_as_float((uint32_t)u << 16);
@@ -622,7 +630,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
                                                                const float* __restrict__ dm, Out dz, Out dv,
                                                                Out dzq, bool dzq_on, int* __restrict__ status) {
   extern __shared__ unsigned char smem_raw[];
-  __shared__ uint64_t bar_load, bar_mma;
+  __shared__ uint64_t bar_load, bar_mma, bar_rec;
   __shared__ uint32_t tmem_slot;
   __shared__ unsigned long long s_max;
   unsigned char* base = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -634,6 +642,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   const int r = d.r, P = d.P, CS = d.CS, T = d.T;
   const int t0 = c * CS;
   const int rg = r / 8;
+  const int mrows = CS <= 64 ? 64 : 128;               // MMA rows: the chunk's tokens, rounded up
+  // r = 32, 32 <= P <= 64: the chunk's gradient record (dG, dM: 8 KB; dC: P r 4 B)
+  // arrives by bulk copy in the bz-lo and bv regions, and the operands are built
+  // from shared memory
+  const bool staged = r == 32 && P >= 32 && P <= 64;
   unsigned char* tile = base;                          // [Z | Z+ | Z- | V | dY] feature groups
   unsigned char* bzh = base + g.o_bzh;
   unsigned char* bzl = base + g.o_bzl;
@@ -647,6 +660,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   if (tid == 0) {
     mbar_init(&bar_load, 1);
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_rec, 1);
     mbar_fence_init();
     tma_prefetch_map(&mz);
     tma_prefetch_map(&mv);
@@ -660,6 +674,12 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
 
   if (warp == 0) {   // one lane issues; the rest of the warp waits converged
     if (lane == 0) {
+      if (staged) {   // the gradient record first: it is what the operand build waits for
+        const float* rec = dstats + q * d.SW;
+        mbar_expect_tx(&bar_rec, (uint32_t)(2 * r * r + P * r) * 4u);
+        bulk_load(bzl, rec, (uint32_t)(2 * r * r) * 4u, &bar_rec);
+        bulk_load(bvh, rec + 2 * r * r, (uint32_t)(P * r) * 4u, &bar_rec);
+      }
       const uint32_t tok_bytes = (uint32_t)(3 * r + (dzq_on ? 2 : 1) * P) * (uint32_t)CS * 2u;
       mbar_expect_tx(&bar_load, tok_bytes + (dzq_on ? g.wbytes : 0u));
       for (int k = 0; k < rg; ++k) {
@@ -686,29 +706,36 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   // series arg-max key: warp 0's first load goes out with the operand loads
   unsigned long long kmx = 0ull;
   if (warp == 0 && lane < d.C) kmx = cmax[bh * d.C + lane];
-  if (r == 32 && P <= 64) {
-    // every global load of this thread's operand values first, then the splits
-    // and stores: one round trip to L2 instead of one per operand block
+  int st = 0;
+  if (staged) {
+    if (!__syncthreads_and(mbar_wait(&bar_rec, 0))) {
+      st = 1;
+      mbar_wait(&bar_rec, 0);
+    }
+    // every value this thread builds, read from the staged record before any
+    // operand row overwrites it
+    const float* sG = reinterpret_cast<const float*>(bzl);   // dG [32][32], then dM
+    const float* sM = sG + 32 * 32;
+    const float* sC = reinterpret_cast<const float*>(bvh);   // dC [P][32]
     const int n1 = tid >> 2, k1 = tid & 3;   // dG + dG^T and dM^T items: n, k-group
     const int k2 = tid >> 5, n2 = tid & 31;  // dM items: k-group, n
-    float a[8], at[8], bm[8], cm[8], c4[2][8], c5[2][8];
-    load_row8(dG + n1 * 32 + k1 * 8, a);
+    float a[8], bm[8], cm[8], c4[2][8], c5[2][8];
+    ld_row8_s(sG + n1 * 32 + k1 * 8, a);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) at[e] = __ldg(dG + (k1 * 8 + e) * 32 + n1);
+    for (int e = 0; e < 8; ++e) a[e] += sG[(k1 * 8 + e) * 32 + n1];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) bm[e] = __ldg(dM + (k2 * 8 + e) * 32 + n2);
-    load_row8(dM + n1 * 32 + k1 * 8, cm);
+    for (int e = 0; e < 8; ++e) bm[e] = sM[(k2 * 8 + e) * 32 + n2];
+    ld_row8_s(sM + n1 * 32 + k1 * 8, cm);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int it = tid + kTokThreads * i;  // < 4P: dC item (k-group it / 32, n it % 32), Bv item (p it / 4, i-group it % 4)
       if (it < 4 * P) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) c4[i][e] = __ldg(dC + ((it >> 5) * 8 + e) * 32 + (it & 31));
-        load_row8(dC + (it >> 2) * 32 + (it & 3) * 8, c5[i]);
+        for (int e = 0; e < 8; ++e) c4[i][e] = sC[((it >> 5) * 8 + e) * 32 + (it & 31)];
+        ld_row8_s(sC + (it >> 2) * 32 + (it & 3) * 8, c5[i]);
       }
     }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) a[e] += at[e];
+    __syncthreads();
     store_split(bzh, bzl, k1 * 32 + n1, a);             // k-groups 0 .. 3: dG + dG^T
     store_split(bzh, bzl, (4 + k2) * 32 + n2, bm);      // k-groups 4 .. 7: dM
     store_split(bzh, bzl, (8 + k1) * 32 + n1, cm);      // k-groups 8 .. 11: dM^T
@@ -771,7 +798,6 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     if (lane == 0) s_max = k;
   }
   fence_async_smem();                                  // B operands -> tensor-core proxy
-  int st = 0;
   if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
     st = 1;
     mbar_wait(&bar_load, 0);
@@ -784,8 +810,8 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
       const auto tok_adesc = [&](uint32_t a, int ks) -> uint64_t { return sdesc(a + 2u * g.grp * ks, g.grp, 128u); };
       const uint32_t lbo_z = (uint32_t)rg * 128u, lbo_v = (uint32_t)(P / 8) * 128u;
-      const uint32_t idz = idesc_bf16(128, r, false, false), idv = idesc_bf16(128, P, false, false);
-      const uint32_t idq = idesc_bf16(128, r, false, true);   // B = W / m, MN-major
+      const uint32_t idz = idesc_bf16(mrows, r, false, false), idv = idesc_bf16(mrows, P, false, false);
+      const uint32_t idq = idesc_bf16(mrows, r, false, true);   // B = W / m, MN-major
       const int kz = (3 * r + P) / 16, kv = r / 16, kq = P / 16;
       for (int part = 0; part < 2; ++part) {
         const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
@@ -805,7 +831,24 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     __syncwarp();
   }
   // first token of a chunk: (dM_prev - dM) z_{t-1}, z_{t-1} = row 0 of Z-; one warp per row
-  if (st == 0 && c > 0) {
+  if (st == 0 && c > 0 && r == 32) {
+    // r = 32: lane j holds column j of rows warp + 4u; all 16 loads go out together
+    const float* mprev = dM - d.SW;
+    const float zj = bf16_at(tile + 2 * zg + (size_t)(lane / 8) * g.grp, lane % 8);
+    float dd[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = warp + 4 * u;
+      dd[u] = __ldg(mprev + i * 32 + lane) - __ldg(dM + i * 32 + lane);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      float a = dd[u] * zj;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) corr[warp + 4 * u] = a;
+    }
+  } else if (st == 0 && c > 0) {
     const unsigned char* zm = tile + 2 * zg;
     const float* mprev = dM - d.SW;
     for (int i = warp; i < r; i += kTokThreads / 32) {
@@ -825,9 +868,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   __syncthreads();
   fence_after_sync();
 
-  // epilogue: thread (warp, lane) owns token row m = 32 warp + lane
-  const int m = 32 * warp + lane, t = t0 + m;
-  const bool live = m < CS && t < T;
+  // epilogue: token row m sits in TMEM lane 32 warp + lane (M = 128: m = 32 warp + lane)
+  // or 32 warp + (m % 16) (M = 64: m = 16 warp + lane for lanes 0-15)
+  const int m = mrows == 64 ? 16 * warp + lane : 32 * warp + lane, t = t0 + m;
+  const bool live = (mrows == 128 || lane < 16) && m < CS && t < T;
   const unsigned long long kmax = s_max;
   const float raw = unpack_norm(kmax);
   const int tstar = unpack_t(kmax);
