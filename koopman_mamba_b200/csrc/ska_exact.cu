@@ -342,7 +342,10 @@ __global__ void __launch_bounds__(kThreads) k_fwd_stats(Dims d, In z, In v, floa
 // ----------------------------------------------------------------------------
 // exclusive scan over chunks (forward) and exclusive suffix scan (backward)
 // ----------------------------------------------------------------------------
-constexpr int kScanBatch = 8;
+// Chunks whose loads go out together before any is added and stored: 16 float4
+// per thread (64 registers) keeps every scan CTA of a 96-series problem resident
+// while the 32 chunks of a 2048-token series take two L2/DRAM round trips.
+constexpr int kScanBatch = 16;
 
 // One thread scans 4 consecutive record floats (a float4 when SW % 4 == 0).
 __device__ __forceinline__ void scan_lanes4(float* base, int n4, size_t s, int C, bool reverse, int decay,

@@ -208,6 +208,19 @@ def test_bf16_r32_short_chunks_each_power(K):
     assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
 
 
+@pytest.mark.parametrize("P", [32, 128])
+def test_bf16_r32_value_widths(P):
+    """r = 32 with P = 32 (operands staged in shared memory, 64-byte dY rows) and
+    P = 128 (dY in two 128-byte swizzled atom columns, a 128-row dW' product),
+    a ragged tail, forward and backward against the oracle."""
+    z, zq, v, dy = _inputs(2, 333, 4, 32, P, 30 + P)
+    got = run_cuda(z, zq, v, 1.1, dy, torch.bfloat16)
+    zb, zqb, vb, dyb = (bf16_round(a) for a in (z, zq, v, dy))
+    ref = ska_core_fwd_bwd(zb, zqb, vb, 1.1, dyb, SkaParams())
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
 def test_deterministic_bitwise():
     z, zq, v, dy = _inputs(2, 700, 3, 32, 64, 9)
     a = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16)
