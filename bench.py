@@ -14,7 +14,10 @@ Prints ONE JSON line (rank 0):
           max over ranks
   e2e     the same metric through the C ABI with pinned HOST buffers: each step
           copies z, zq, v, dy host->device, runs fwd+bwd, copies y, dz, dzq, dv
-          back; copies inside the timed region
+          back; copies inside the timed region.  `value` streams the steps with
+          double-buffered device tensors (each step's copies overlap its
+          neighbours' compute and copies); `serial_value` runs them one after
+          another on one stream
   roofline  the dominant kernel: algorithmic bytes per launch / its average
           CUDA-event duration against MEASURED_PEAKS.json HBM bandwidth
   cpu_baseline  the numpy oracle (port of the reference's CPU path) on the
@@ -336,14 +339,14 @@ def main(argv=None):
     savp, scrp = ctypes.c_void_p(saved.data_ptr()), ctypes.c_void_p(scratch.data_ptr())
     byref = ctypes.byref
 
-    def step():
-        rc = lib.ska_fwd(byref(shape), BF16, byref(D["z"]), byref(D["zq"]), byref(D["v"]), gp, byref(D["y"]),
+    def step(Dx=D):
+        rc = lib.ska_fwd(byref(shape), BF16, byref(Dx["z"]), byref(Dx["zq"]), byref(Dx["v"]), gp, byref(Dx["y"]),
                          savp, saved_bytes, sp)
         if rc:
             _lib.check("ska_fwd", rc)
-        rc = lib.ska_bwd(byref(shape), BF16, byref(D["z"]), byref(D["zq"]), byref(D["v"]), gp, byref(D["dy"]),
-                         savp, saved_bytes, scrp, scratch_bytes, byref(D["dz"]), byref(D["dzq"]), byref(D["dv"]),
-                         dgp, sp)
+        rc = lib.ska_bwd(byref(shape), BF16, byref(Dx["z"]), byref(Dx["zq"]), byref(Dx["v"]), gp, byref(Dx["dy"]),
+                         savp, saved_bytes, scrp, scratch_bytes, byref(Dx["dz"]), byref(Dx["dzq"]),
+                         byref(Dx["dv"]), dgp, sp)
         if rc:
             _lib.check("ska_bwd", rc)
 
@@ -418,8 +421,56 @@ def main(argv=None):
             eb[i].record(stream)
         torch.cuda.synchronize()
         e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ea, eb)), dev)
-        e2e = {"value": tokens_per_step * args.steps / (e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        serial = tokens_per_step * args.steps / (e_ms / 1e3)
+
+        # The same steps as a stream of batches: two device buffer sets; step i copies its
+        # inputs host->device on one stream and its results device->host on another,
+        # overlapping step i - 1's compute and copies (the link is full duplex).  Every
+        # step's copies stay inside the timed region, which spans all K steps.
+        din = [(z, zq, v, dy), tuple(torch.empty_like(t) for t in (z, zq, v, dy))]
+        dout = [(y, dz, dzq, dv), tuple(torch.empty_like(t) for t in (y, dz, dzq, dv))]
+        Dset = [{n: desc(t) for n, t in zip(("z", "zq", "v", "dy", "y", "dz", "dzq", "dv"), din[k] + dout[k])}
+                for k in range(2)]
+        outs = [out_host, [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (y, dz, dzq, dv)]]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_in, ev_comp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+
+        def piped_step(i):
+            k = i % 2
+            s_in.wait_event(ev_comp[k])          # step i - 2's compute has read this input set
+            with torch.cuda.stream(s_in):
+                for src, dst in zip(host, din[k]):
+                    dst.copy_(src, non_blocking=True)
+            ev_in[k].record(s_in)
+            stream.wait_event(ev_in[k])
+            stream.wait_event(ev_out[k])         # step i - 2's results have left this output set
+            step(Dset[k])
+            ev_comp[k].record(stream)
+            s_out.wait_event(ev_comp[k])
+            with torch.cuda.stream(s_out):
+                for src, dst in zip(dout[k], outs[k]):
+                    dst.copy_(src, non_blocking=True)
+            ev_out[k].record(s_out)
+
+        for i in range(2):
+            piped_step(i)
+        torch.cuda.synchronize()
+        barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        s_in.wait_event(p0)
+        for i in range(args.steps):
+            piped_step(i)
+        for k in range(2):
+            stream.wait_event(ev_out[k])
+        p1.record(stream)
+        torch.cuda.synchronize()
+        p_ms = max_over_ranks(p0.elapsed_time(p1), dev)
+        e2e = {"value": tokens_per_step * args.steps / (p_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "copies": "double-buffered: host->device and device->host on two copy streams, overlapping "
+                         "the neighbouring steps' compute and copies",
+               "serial_value": serial}
 
     lib.ska_set_profile_events(None, 0)
     # stats (+ scan), chunk operators; dW', chunk backward, scan, token backward
