@@ -95,9 +95,9 @@ __device__ __forceinline__ void st_identity(float* T, int lane) {
 // it (jitter retry as ska.py:140-145, or jitter forced), and writes Li rows into TLi.
 // Returns the jitter flags.
 __device__ __forceinline__ int factor_and_invert(const Dims& d, const float* rec, int lane, float im2,
-                                                 bool force_jitter, float* Tg, float* TLi) {
+                                                 bool force_jitter, float* Tg, float* TLi, bool preloaded = false) {
   const int r = d.r;
-  load_mat(Tg, rec, r, r, 1.f, lane);
+  if (!preloaded) load_mat(Tg, rec, r, r, 1.f, lane);   // else Tg already holds G
   __syncwarp();
   float g[32], x[32];
   int flag = 0;
@@ -138,42 +138,77 @@ __device__ __forceinline__ bool tok_rows_aligned(const void* p, long long sb, lo
 }
 
 // tile rows [0, 32) <- tokens tok0 + row (rows >= nvalid zero), features [f0, f0 + n)
+// the aligned path of load_tok_block in two halves, so that several blocks' loads
+// can be in flight together: this lane's 16-byte pieces, then their tile rows
+template <typename IO>
+struct TokRaw {
+  uint4 v[32 / (16 / sizeof(IO))];
+};
+template <typename IO>
+__device__ __forceinline__ void tok_raw_load(TokRaw<IO>& raw, const In& x, int b, int tok0, int h, int f0,
+                                             int nvalid, int lane) {
+  constexpr int kVec = 16 / sizeof(IO);          // elements per 16-byte piece
+  constexpr int kPer = 32 / kVec;                // pieces per token row
+  const IO* base = static_cast<const IO*>(x.p) + (long long)b * x.sb + (long long)h * x.sh + f0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
+    raw.v[k] = __ldg(reinterpret_cast<const uint4*>(base + (long long)(tok0 + (row < nvalid ? row : 0)) * x.st) + pc);
+  }
+}
+template <typename IO>
+__device__ __forceinline__ void tok_raw_store(float* Tl, const TokRaw<IO>& raw, int nvalid, int lane) {
+  constexpr int kVec = 16 / sizeof(IO);
+  constexpr int kPer = 32 / kVec;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
+    const bool ok = row < nvalid;
+    const IO* e = reinterpret_cast<const IO*>(&raw.v[k]);   // registers: plain reads only
+    float v[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) v[u] = ok ? to_float(e[u]) : 0.f;
+    float4* rowp = reinterpret_cast<float4*>(Tl + row * 32);
+#pragma unroll
+    for (int c = 0; c < kVec / 4; ++c) {
+      const int q = pc * (kVec / 4) + c;       // 16-byte fp32 chunk of the tile row
+      rowp[q ^ (row & 7)] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+  }
+}
+
 template <typename IO>
 __device__ __forceinline__ void load_tok_block(float* Tl, const In& x, int b, int tok0, int h, int f0, int n,
                                                int nvalid, int lane) {
-  constexpr int kVec = 16 / sizeof(IO);          // elements per 16-byte piece
-  constexpr int kPer = 32 / kVec;                // pieces per token row
   if (nvalid <= 0) {                             // block past the series end: no loads
     float v[32];
     zero(v);
     st_row(Tl, lane, v);
   } else if (tok_rows_aligned<IO>(x.p, x.sb, x.st, x.sh, f0, n)) {
-    const IO* base = static_cast<const IO*>(x.p) + (long long)b * x.sb + (long long)h * x.sh + f0;
-    uint4 raw[kPer];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
-      raw[k] = __ldg(reinterpret_cast<const uint4*>(base + (long long)(tok0 + (row < nvalid ? row : 0)) * x.st) + pc);
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int f = 32 * k + lane, row = f / kPer, pc = f % kPer;
-      const bool ok = row < nvalid;
-      const IO* e = reinterpret_cast<const IO*>(&raw[k]);   // registers: plain reads only
-      float v[kVec];
-#pragma unroll
-      for (int u = 0; u < kVec; ++u) v[u] = ok ? to_float(e[u]) : 0.f;
-      float4* rowp = reinterpret_cast<float4*>(Tl + row * 32);
-#pragma unroll
-      for (int c = 0; c < kVec / 4; ++c) {
-        const int q = pc * (kVec / 4) + c;       // 16-byte fp32 chunk of the tile row
-        rowp[q ^ (row & 7)] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      }
-    }
+    TokRaw<IO> raw;
+    tok_raw_load<IO>(raw, x, b, tok0, h, f0, nvalid, lane);
+    tok_raw_store<IO>(Tl, raw, nvalid, lane);
   } else {
     float v[32];
     ld_tok_row<IO>(v, x, b, tok0 + lane, h, f0, n, lane < nvalid, 1.f);
     st_row(Tl, lane, v);
+  }
+}
+
+// two consecutive 32-token blocks (tok0, tok0 + 32) into Ta, Tb with both blocks'
+// loads in flight together when both are live and aligned
+template <typename IO>
+__device__ __forceinline__ void load_tok_blocks2(float* Ta, float* Tb, const In& x, int b, int tok0, int h, int f0,
+                                                 int n, int nva, int nvb, int lane) {
+  if (nva > 0 && nvb > 0 && tok_rows_aligned<IO>(x.p, x.sb, x.st, x.sh, f0, n)) {
+    TokRaw<IO> ra, rb;
+    tok_raw_load<IO>(ra, x, b, tok0, h, f0, nva, lane);
+    tok_raw_load<IO>(rb, x, b, tok0 + 32, h, f0, nvb, lane);
+    tok_raw_store<IO>(Ta, ra, nva, lane);
+    tok_raw_store<IO>(Tb, rb, nvb, lane);
+  } else {
+    load_tok_block<IO>(Ta, x, b, tok0, h, f0, n, nva, lane);
+    load_tok_block<IO>(Tb, x, b, tok0 + 32, h, f0, n, nvb, lane);
   }
 }
 
@@ -241,16 +276,32 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   float* TC = T3 + kTile;                   // NPB tiles: Cn rows, later Y blocks
   float* TW = TC + NPB * kTile;             // NPB tiles: (W / m) rows
   const float* rec = stats + q * d.SW;
+  // The record's G, M and C rows go out as asynchronous copies into the tiles that
+  // hold them first (G -> T0, M -> TW, C -> TC, unscaled), overlapping the series
+  // norm and the Cholesky; the 1/m scales move into the products that use them.
+  const bool pre = cp_tile_async(T0, rec, r, r, lane);
+  cp_async_commit();
+  bool pre_mc = pre && cp_tile_async(TW, rec + r * r, r, r, lane);
+#pragma unroll
+  for (int pb = 0; pb < NPB; ++pb)
+    pre_mc = pre_mc && cp_tile_async(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, lane);
+  cp_async_commit();
   const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
   const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
+  cp_async_wait<1>();                                                     // G has landed
 
-  const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1);   // T1 = Li
+  const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1, pre);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
   wmmp<kFast, 32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
+  cp_async_wait<0>();                                                     // M and C have landed
   __syncwarp();
-  load_mat(T0, rec + r * r, r, r, im2, lane);                             // T0 = Mn
+  const float* TM = TW;                                                   // M (raw): A0 = (M / m^2) S
+  if (!pre_mc) {
+    load_mat(T0, rec + r * r, r, r, 1.f, lane);
+    TM = T0;
+  }
   __syncwarp();
-  wmmp<kFast, 32, 32, false, false, false>(T3, T0, kTile, T2, 1.f);       // T3 = A0 = Mn S
+  wmmp<kFast, 32, 32, false, false, false>(T3, TM, kTile, T2, im2);       // T3 = A0 = Mn S
   __syncwarp();
   {
     float a[32];
@@ -283,27 +334,36 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   wmmp<kFast, 32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
   __syncwarp();
   wmmp<kFast, 32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
+  if (!pre_mc) {
 #pragma unroll
-  for (int pb = 0; pb < NPB; ++pb)
-    load_mat(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, im, lane);   // Cn rows
+    for (int pb = 0; pb < NPB; ++pb)
+      load_mat(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, 1.f, lane);   // C rows
+  }
   __syncwarp();
-  wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im);  // W / m = Cn V / m
+  wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im2);  // W / m = (C / m) V / m
   __syncwarp();
 
-  // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T
+  // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T.
+  // Two token blocks at a time (T0, T1; Li is dead), both blocks' loads together.
   const int tchunk = id.c * CS;
-  for (int t0 = 0; t0 < CS; t0 += 32) {
-    const int nvalid = min(32, min(CS - t0, T - (tchunk + t0)));
-    load_tok_block<IO>(T0, zq, id.b, tchunk + t0, id.h, 0, r, nvalid, lane);
+  for (int t0 = 0; t0 < CS; t0 += 64) {
+    const int nva = min(32, min(CS - t0, T - (tchunk + t0)));
+    const int nvb = min(32, min(CS - t0 - 32, T - (tchunk + t0 + 32)));
+    load_tok_blocks2<IO>(T0, T1, zq, id.b, tchunk + t0, id.h, 0, r, nva, nvb, lane);
     __syncwarp();
+    for (int hb = 0; hb < 2 && t0 + 32 * hb < CS; ++hb) {
+      const float* TQ = hb ? T1 : T0;
+      const int nvalid = hb ? nvb : nva;
 #pragma unroll
-    for (int pb = 0; pb < NPB; ++pb)
-      wmmp<kFast, 32, 32, false, true, false>(TC + pb * kTile, T0, kTile, TW + pb * kTile, 1.f);
-    __syncwarp();
+      for (int pb = 0; pb < NPB; ++pb)
+        wmmp<kFast, 32, 32, false, true, false>(TC + pb * kTile, TQ, kTile, TW + pb * kTile, 1.f);
+      __syncwarp();
 #pragma unroll
-    for (int pb = 0; pb < NPB; ++pb)
-      store_tok_block<IO>(y, id.b, tchunk + t0, id.h, pb * 32, min(32, P - pb * 32), nvalid, TC + pb * kTile, lane);
-    __syncwarp();
+      for (int pb = 0; pb < NPB; ++pb)
+        store_tok_block<IO>(y, id.b, tchunk + t0 + 32 * hb, id.h, pb * 32, min(32, P - pb * 32), nvalid,
+                            TC + pb * kTile, lane);
+      __syncwarp();
+    }
   }
 }
 

@@ -294,6 +294,30 @@ __device__ __forceinline__ void load_mat(float* T, const float* src, int nrows, 
   }
 }
 
+// rows [0, nrows) x columns [0, ncols) of a row-major global matrix -> tile T by
+// asynchronous 16-byte copies (cp.async, L2 only); the rest of the tile is zeroed by
+// zero-length sources.  Returns false, and copies nothing, unless ncols % 4 == 0
+// and src is 16-byte aligned (then call load_mat instead).  The copies belong to
+// the lane's next cp_async_commit group; wait for it and synchronise the warp
+// before reading the tile.
+__device__ __forceinline__ bool cp_tile_async(float* T, const float* src, int nrows, int ncols, int lane) {
+  if ((ncols & 3) != 0 || (reinterpret_cast<uintptr_t>(src) & 15) != 0) return false;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int f = 32 * k + lane, row = f >> 3, q = f & 7;
+    const bool ok = row < nrows && 4 * q < ncols;
+    const float* s = src + (ok ? row * ncols + 4 * q : 0);
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(T + row * 32 + ((q ^ (row & 7)) << 2)));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(s), "r"(ok ? 16 : 0) : "memory");
+  }
+  return true;
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {   // at most N of this lane's groups still in flight
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // rows [0, nrows) x columns [0, ncols) of tile T, times scale -> row-major global
 // matrix (coalesced when ncols == 32, as load_mat).  Synchronise the warp before.
 __device__ __forceinline__ void store_mat(float* dst, const float* T, int nrows, int ncols, float scale,
