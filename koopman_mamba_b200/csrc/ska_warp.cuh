@@ -422,8 +422,9 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
 #pragma unroll
       for (int n = 0; n < 4; ++n) d[h][n][0] = d[h][n][1] = d[h][n][2] = d[h][n][3] = 0.f;
     // not unrolled: each product shape is its own function and the chunk kernels
-    // stall on instruction fetch, so the smallest copies run fastest (full unroll
-    // 0.2105 ms, by 2 0.2035 ms, none 0.2012 ms for the config-2 backward)
+    // stall on instruction fetch, so the smallest copies run fastest (backward at
+    // B=8, H=12, L=2048, P=64, r=32: full unroll 0.2105 ms, by 2 0.2035 ms, none
+    // 0.2012 ms)
 #pragma unroll 1
     for (int k0 = 0; k0 < K; k0 += 8) {
       if ((k0 & 15) == 0) sched_fence();
