@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
                                                                const float* __restrict__ dm, Out dz, Out dv,
                                                                Out dzq, bool dzq_on, int* __restrict__ status) {
   extern __shared__ unsigned char smem_raw[];
-  __shared__ uint64_t bar_load, bar_mma, bar_rec;
+  __shared__ uint64_t bar_load, bar_mma, bar_mmq, bar_rec;
   __shared__ uint32_t tmem_slot;
   __shared__ unsigned long long s_max;
   unsigned char* base = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -661,6 +661,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     mbar_init(&bar_load, 1);
     mbar_init(&bar_mma, 1);
     mbar_init(&bar_rec, 1);
+    mbar_init(&bar_mmq, 1);
     mbar_fence_init();
     tma_prefetch_map(&mz);
     tma_prefetch_map(&mv);
@@ -803,8 +804,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     mbar_wait(&bar_load, 0);
   }
 
-  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
-    if (st == 0 && lane == 0) {
+  // warp 0 issues the dZ and dV products, warp 1 (at the same time) the dZQ product
+  // into its own TMEM columns; each commits to its own barrier
+  if (warp < 2) {   // one lane issues; the rest of the warp waits converged
+    if (st == 0 && lane == 0 && (warp == 0 || dzq_on)) {
       fence_after_sync();
       const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
       // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
@@ -816,17 +819,20 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       for (int part = 0; part < 2; ++part) {
         const uint32_t bz0 = smem_u32(part ? bzl : bzh), bv0 = smem_u32(part ? bvl : bvh);
         const uint32_t bw0 = smem_u32(bw) + (part ? (uint32_t)(P * r * 2) : 0u);
-        for (int ks = 0; ks < kz; ++ks)
-          mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
-        for (int ks = 0; ks < kv; ++ks)
-          mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
-                   part > 0 || ks > 0);
-        // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
-        for (int ks = 0; ks < (dzq_on ? kq : 0); ++ks)
-          mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u), idq,
-                   part > 0 || ks > 0);
+        if (warp == 0) {
+          for (int ks = 0; ks < kz; ++ks)
+            mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
+          for (int ks = 0; ks < kv; ++ks)
+            mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
+                     part > 0 || ks > 0);
+        } else {
+          // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
+          for (int ks = 0; ks < kq; ++ks)
+            mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u),
+                     idq, part > 0 || ks > 0);
+        }
       }
-      mma_commit(&bar_mma);
+      mma_commit(warp == 0 ? &bar_mma : &bar_mmq);
     }
     __syncwarp();
   }
@@ -861,9 +867,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       if (lane == 0) corr[i] = a;
     }
   }
-  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0) && (!dzq_on || mbar_wait(&bar_mmq, 0)))) {
     st = 2;
     mbar_wait(&bar_mma, 0);
+    if (dzq_on) mbar_wait(&bar_mmq, 0);
   }
   __syncthreads();
   fence_after_sync();
