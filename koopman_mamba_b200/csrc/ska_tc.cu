@@ -207,9 +207,10 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 // k_stats_scan_tc: the statistics and their exclusive (decayed) scan in one pass,
 // one CTA per (batch, head) series, walking the series' chunks in order
 // (ska.py:114-133, adaptive_chunking.py:225-238).  Warp-specialised:
-//   warp 0             TMA copies of chunk c into shared stage c % ns and the
-//                      product of chunk c into TMEM buffer c % kScanBufs (the
-//                      warp waits together, one lane issues);
+//   warp 0             TMA copies of chunk c into shared stage c % ns;
+//   warp 7             the product of chunk c into TMEM buffer c % kScanBufs
+//                      (each warp waits together, one lane issues: copies and
+//                      products pipeline instead of alternating in one thread);
 //   warps 1-4          record rows: warp w reads TMEM lane quarter w % 4 (rows
 //                      32 (w % 4) ..), keeps those rows' running prefix in
 //                      registers and writes
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
 // k_scan_fwd (the scan's read and rewrite of every record) when there are enough
 // series to occupy the SMs (r = 32, 2r + P <= 128: one 128-row product per chunk).
 // ---------------------------------------------------------------------------
-constexpr int kScanThreads = 224;
+constexpr int kScanThreads = 256;
 constexpr int kScanStagesMax = 6;
 constexpr int kScanBufs = 4;
 
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
   const uint32_t tbase = tmem_slot;
 
   if (warp == 0) {
-    // ---- copies and products: the warp waits together, one lane issues ----
+    // ---- copies: the warp waits together, one lane issues ----
     const auto load_chunk = [&](int c) {
       unsigned char* tz = tiles + (size_t)(c % ns) * tile_bytes;
       unsigned char* tzp = tz + (size_t)(r / fpg) * g.grp;
@@ -282,12 +283,31 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
       }
       for (int k = 0; k < P / fpg; ++k) tma_load_4d(tv + (size_t)k * g.grp, &mv, bar, fpg * k, h, t0, b);
     };
-    const uint32_t id = idesc_bf16(128, r, true, true);
-    int nload = min(ns, C), nmma = 0;   // chunks copied / multiplied so far
+    int nload = 0;   // chunks copied so far
     bool ok = true;
-    if (lane == 0)
-      for (int c = 0; c < nload; ++c) load_chunk(c);
+    for (int c = 0; c < C; ++c) {
+      if (c >= ns) {   // chunk c - ns has left the stage (its product is done, its norms read)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[c % ns], (uint32_t)(c / ns - 1) & 1u));
+        if (!ok) break;
+      }
+      if (lane == 0) load_chunk(c);
+      __syncwarp();
+      nload = c + 1;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every copy has landed before the CTA leaves (bounded; at once when all went well)
+      for (int s = 0; s < ns; ++s) {
+        int last = -1;
+        for (int c = s; c < nload; c += ns) last = c;
+        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
+      }
+    }
     __syncwarp();
+  } else if (warp == 7) {
+    // ---- products: the warp waits together, one lane issues ----
+    const uint32_t id = idesc_bf16(128, r, true, true);
+    int nmma = 0;   // chunks multiplied so far
+    bool ok = true;
     for (int c = 0; c < C; ++c) {
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u));
       if (ok && c >= kScanBufs)
@@ -311,31 +331,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
       }
       __syncwarp();
       nmma = c + 1;
-      // chunk c - 1's stage is free once its product is done and its norms are read
-      if (c >= 1 && c - 1 + ns < C) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[(c - 1) % ns], (uint32_t)((c - 1) / ns) & 1u));
-        if (!ok) break;
-        if (lane == 0) load_chunk(c - 1 + ns);
-        __syncwarp();
-        nload = c + ns;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every product has completed before the CTA leaves (bounded)
+      for (int s = 0; s < kScanBufs; ++s) {
+        int last = -1;
+        for (int c = s; c < nmma; c += kScanBufs) last = c;
+        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kScanBufs) & 1u);
       }
     }
-    if (!ok) {   // a wait ran out: flag it and let the copies and products in flight finish
-      if (lane == 0) {
-        atomicExch(&err, 1);
-        for (int s = 0; s < ns; ++s) {
-          int last = -1;
-          for (int c = s; c < nload; c += ns) last = c;
-          if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
-        }
-        for (int s = 0; s < kScanBufs; ++s) {
-          int last = -1;
-          for (int c = s; c < nmma; c += kScanBufs) last = c;
-          if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kScanBufs) & 1u);
-        }
-      }
-      __syncwarp();
-    }
+    __syncwarp();
   } else if (warp <= 4) {
     // ---- record rows ----
     const int q = warp & 3;   // TMEM lane quarter this warp may read
@@ -369,7 +374,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
         wpc::store_mat(recs + (long long)c * d.SW + (size_t)row0 * 32, wtile, nrow, 32, 1.f, lane);
       }
     }
-  } else {
+  } else if (warp <= 6) {
     // ---- key norms: warp 5 takes the even chunks, warp 6 the odd ones ----
     for (int c = warp - 5; c < C; c += 2) {
       if (!__all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u))) {
