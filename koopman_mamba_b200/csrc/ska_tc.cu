@@ -1033,6 +1033,168 @@ cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In&
 }
 
 // dW' needs the A block (P rows) inside one 128-row MMA
+// ---------------------------------------------------------------------------
+// k_dw_ps: the dW' products of many chunks per CTA (r = 32, P = 64, 64-byte
+// swizzled tiles), so that the one-chunk CTAs of k_dw_tc do not leave a partial
+// second wave and each CTA's set-up is paid once:
+//   warp 0      TMA copies of chunk j's [ZQ | dY] tiles into shared stage j % ns;
+//   warp 1      chunk j's M = 64 product dY^T ZQ into TMEM buffer j % kDwBufs;
+//   warps 2-5   the epilogue: warp w reads TMEM lane quarter w % 4, whose lanes
+//               0-15 hold product rows 16 (w % 4) .. + 15, and writes them as the
+//               chunk's fp32 record.
+// Each warp waits together and one lane issues; the roles meet only at mbarriers.
+// The CTA takes chunks blockIdx.x, blockIdx.x + gridDim.x, ...
+// ---------------------------------------------------------------------------
+constexpr int kDwThreads = 192;
+constexpr int kDwStagesMax = 6;
+constexpr int kDwBufs = 4;
+
+__global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__ CUtensorMap mzq,
+                                                        const __grid_constant__ CUtensorMap mdy, Dims d,
+                                                        uint32_t grp, int ns, float* __restrict__ dw,
+                                                        int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t bar_load[kDwStagesMax], bar_free[kDwStagesMax], bar_mma[kDwBufs], bar_read[kDwBufs];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int err;
+  unsigned char* tiles = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = d.r, P = d.P, CS = d.CS;
+  const long long nq = (long long)d.B * d.H * d.C;
+  const int nj = (int)((nq - (long long)blockIdx.x + gridDim.x - 1) / gridDim.x);   // this CTA's chunks
+  const size_t stage_bytes = (size_t)(r / 32 + P / 32) * grp;   // ZQ atom column, then the dY ones
+  const auto chunk_of = [&](int j) { return (long long)blockIdx.x + (long long)j * gridDim.x; };
+
+  if (tid == 0) {
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(&bar_load[i], 1);
+      mbar_init(&bar_free[i], 1);
+    }
+    for (int i = 0; i < kDwBufs; ++i) {
+      mbar_init(&bar_mma[i], 1);
+      mbar_init(&bar_read[i], 4);
+    }
+    err = 0;
+    mbar_fence_init();
+    tma_prefetch_map(&mzq);
+    tma_prefetch_map(&mdy);
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, kDwBufs * 32);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {
+    // ---- copies ----
+    int nload = 0;
+    bool ok = true;
+    for (int j = 0; j < nj; ++j) {
+      if (j >= ns) {   // chunk j - ns's product has read the stage
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[j % ns], (uint32_t)(j / ns - 1) & 1u));
+        if (!ok) break;
+      }
+      if (lane == 0) {
+        const long long q = chunk_of(j);
+        const int c = (int)(q % d.C);
+        const long long bh = q / d.C;
+        const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+        unsigned char* tq = tiles + (size_t)(j % ns) * stage_bytes;
+        unsigned char* ty = tq + (size_t)(r / 32) * grp;
+        uint64_t* bar = &bar_load[j % ns];
+        mbar_expect_tx(bar, (uint32_t)(r + P) * (uint32_t)CS * 2u);
+        for (int k = 0; k < r / 32; ++k) tma_load_4d(tq + (size_t)k * grp, &mzq, bar, 32 * k, h, c * CS, b);
+        for (int k = 0; k < P / 32; ++k) tma_load_4d(ty + (size_t)k * grp, &mdy, bar, 32 * k, h, c * CS, b);
+      }
+      __syncwarp();
+      nload = j + 1;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every copy has landed before the CTA leaves (bounded)
+      for (int s = 0; s < ns; ++s) {
+        int last = -1;
+        for (int j = s; j < nload; j += ns) last = j;
+        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- products ----
+    const uint32_t id = idesc_bf16(64, r, true, true);
+    int nmma = 0;
+    bool ok = true;
+    for (int j = 0; j < nj; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[j % ns], (uint32_t)(j / ns) & 1u));
+      if (ok && j >= kDwBufs)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[j % kDwBufs], (uint32_t)(j / kDwBufs - 1) & 1u));
+      if (!ok) break;
+      if (lane == 0) {
+        fence_after_sync();
+        const uint32_t b0 = smem_u32(tiles + (size_t)(j % ns) * stage_bytes);
+        const uint32_t a0 = b0 + (uint32_t)(r / 32) * grp;
+        const uint32_t acc = tbase + (uint32_t)(j % kDwBufs) * 32u;
+        for (int ks = 0; ks < CS / 16; ++ks)
+          mma_bf16(acc, sdesc_sw(a0 + 1024u * ks, grp, 512u, kSwizzle64), sdesc_sw(b0 + 1024u * ks, grp, 512u, kSwizzle64),
+                   id, ks > 0);
+        mma_commit(&bar_mma[j % kDwBufs]);
+      }
+      __syncwarp();
+      nmma = j + 1;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every product has completed before the CTA leaves (bounded)
+      for (int s = 0; s < kDwBufs; ++s) {
+        int last = -1;
+        for (int j = s; j < nmma; j += kDwBufs) last = j;
+        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kDwBufs) & 1u);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: rows 16 qd + lane (lanes 0-15) of each product ----
+    const int qd = warp & 3;
+    const int row = 16 * qd + lane;
+    for (int j = 0; j < nj; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[j % kDwBufs], (uint32_t)(j / kDwBufs) & 1u))) {
+        if (lane == 0) atomicExch(&err, 1);
+        break;
+      }
+      fence_after_sync();
+      if (warp == 2 && lane == 0) mbar_arrive(&bar_free[j % ns]);   // the product has read the stage
+      float v0[16], v1[16];
+      const uint32_t ta = tbase + (uint32_t)(j % kDwBufs) * 32u + ((uint32_t)(32 * qd) << 16);
+      tmem_ld16(ta, v0);
+      tmem_ld16(ta + 16u, v1);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_read[j % kDwBufs]);
+      const long long q = chunk_of(j);
+      if (lane < 16 && row < P) {
+        float4* dst = reinterpret_cast<float4*>(dw + q * (long long)P * r + (size_t)row * r);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[e] = make_float4(v0[4 * e], v0[4 * e + 1], v0[4 * e + 2], v0[4 * e + 3]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[4 + e] = make_float4(v1[4 * e], v1[4 * e + 1], v1[4 * e + 2], v1[4 * e + 3]);
+      }
+      if (warp == 2 && lane == 0) status[q] = 0;
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (err) {   // poison this CTA's chunks
+    const float nan = __int_as_float(0x7fc00000);
+    for (int j = 0; j < nj; ++j) {
+      const long long q = chunk_of(j);
+      for (int i = tid; i < P * r; i += kDwThreads) dw[q * (long long)P * r + i] = nan;
+      if (tid == 0) status[q] = 1;
+    }
+  }
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, kDwBufs * 32);
+  }
+}
+
 bool dw_tc_ok(const Dims& d, const In& zq, const In& dy) { return d.P <= 128 && stats_tc_ok(d, zq, dy); }
 
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st) {
@@ -1040,6 +1202,22 @@ cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, i
   StatsGeom g = stats_geom(d.r, d.P, d.CS);
   if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS, g.sw) || !token_map(&my, dy, d.B, d.T, d.H, d.P, d.CS, g.sw))
     return cudaErrorInvalidValue;
+  if (g.sw && d.r == 32 && d.P == 64) {   // persistent CTAs, two per SM
+    const size_t stage = (size_t)(d.r / 32 + d.P / 32) * g.grp;
+    const int ns = (int)std::min<size_t>(kDwStagesMax, (100u * 1024u - 1024u) / stage);
+    if (ns >= 2) {
+      const size_t smem = (size_t)ns * stage + 1024;
+      cudaError_t e = cudaFuncSetAttribute(k_dw_ps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      int dev = 0, sms = 0;
+      if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+      if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+      const long long n = (long long)d.B * d.H * d.C;
+      const unsigned grid = (unsigned)std::min<long long>(n, 2LL * sms);
+      k_dw_ps<<<grid, kDwThreads, smem, st>>>(mq, my, d, g.grp, ns, dw, status);
+      return cudaGetLastError();
+    }
+  }
   g.nb = 1;
   g.ncols = d.r < 32 ? 32u : (uint32_t)d.r;
   // ZQ groups + the groups of 128 A rows (P real)
