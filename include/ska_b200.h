@@ -69,6 +69,8 @@ enum {
   SKA_ERR_ALIGN = -6,       /* misaligned pointer or stride                        */
   SKA_ERR_LAUNCH = -7,      /* a kernel launch failed (cudaGetLastError)           */
   SKA_ERR_STRATEGY = -8,    /* unknown strategy, or decay_alpha not finite         */
+  SKA_ERR_TIMEOUT = -9,     /* ska_check_status: a bounded wait of a tensor-core   */
+                            /* kernel expired (the chunk's outputs are NaN)        */
 };
 
 /* Static problem description (constructor arguments of the reference
@@ -164,6 +166,39 @@ int ska_set_profile_events(void* const* events, int count);
 #define SKA_PATH_FUSED_SCAN 16
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
+/* Bounded waits of the tensor-core kernels (no counterpart in the reference,
+ * whose library calls have no device-side waits; this is the "scan-wait
+ * timeout" error of the drop-in contract).  Every mbarrier wait in the TMA +
+ * tcgen05 kernels gives up after a bounded number of polls.  A wait that gives
+ * up records a status entry for its chunk, waits (with the full limit) for the
+ * copies and products still in flight, writes NaN into that chunk's outputs,
+ * frees its tensor memory and returns: the launch completes and the CUDA
+ * context stays usable.  ska_fwd / ska_bwd cannot report this at return (they
+ * never synchronise); ska_check_status reads it afterwards.
+ *
+ * Status entries: int32 [B][H][C] (chunk c of head h of batch b at
+ * (b * H + h) * C + c), one array in `saved` (forward statistics kernels:
+ * 0 ok, 1 copy wait expired, 2 product wait expired) and one in `scratch`
+ * (backward: bits 0-1 the readout-gradient kernel, bits 2-3 the token kernel,
+ * each coded as in the forward).  Layouts without tensor-core kernels write 0.
+ *
+ * ska_check_status synchronises `stream`, then scans the forward entries of
+ * `saved` and the backward entries of `scratch` (either may be NULL to skip it).
+ * Returns SKA_OK when every entry is 0, SKA_ERR_TIMEOUT at the first non-zero one
+ * with *first_bad = its flat chunk index and *code = the forward entry (1, 2) or
+ * SKA_STATUS_BWD_BASE + the backward entry's bits; other negative codes for bad
+ * arguments.  A diagnostic call: it copies the entries to host memory.
+ *
+ * ska_set_wait_limit sets the poll limit of the first wait of every role in
+ * every later launch (process-wide; 0 = give up at once, without polling;
+ * 0xFFFFFFFF = back to the default of 2^22 polls).  The waits that drain
+ * in-flight work after a failure always keep the default.  It exists so that a
+ * test can make the waits expire on a GPU without a fault. */
+#define SKA_STATUS_BWD_BASE 16
+int ska_set_wait_limit(uint32_t polls);
+int ska_check_status(const SkaShape* shape, const void* saved, size_t saved_bytes, const void* scratch,
+                     size_t scratch_bytes, void* stream, int64_t* first_bad, int* code);
+
 /* Forward with no allocation anywhere (no counterpart in the reference, whose
  * PyTorch path always allocates through the caching allocator).  Same
  * computation and arguments as ska_fwd, minus the `saved` buffer: the
@@ -174,9 +209,15 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
  * allocate between launches (cudaMalloc can synchronise the device).
  *   - Problems whose ska_workspace_size saved_bytes exceed
  *     SKA_NOALLOC_SCRATCH_BYTES return SKA_ERR_WORKSPACE and launch nothing.
+ *     The checks run in this order: the shape (as ska_workspace_size), then
+ *     the size against the array, then everything ska_fwd checks (dtype,
+ *     pointers, alignment); so an over-size problem returns SKA_ERR_WORKSPACE
+ *     whatever its tensors are.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is kept for the life of the
+ *     process, so a device reset (cudaDeviceReset, or destroying the primary
+ *     context) is not supported once the entry point has been called.
  *   - All calls share the one array and it keeps the previous call's contents
  *     (every part of it that is read is rewritten first).  Calls whose work
  *     overlaps on the GPU race on it: serialise them, e.g. on one stream.

@@ -28,7 +28,12 @@ EXPORTED = (
     "ska_set_profile_events",
     "ska_fwd_noalloc",
     "ska_kernel_path",
+    "ska_set_wait_limit",
+    "ska_check_status",
 )
+SKA_ERR_TIMEOUT = -9
+SKA_STATUS_BWD_BASE = 16
+SKA_WAIT_LIMIT_DEFAULT = 0xFFFFFFFF
 SKA_PATH_TC_STATS = 1
 SKA_PATH_WARP_CHUNK = 2
 SKA_PATH_TC_TOKEN_BWD = 4
@@ -97,6 +102,11 @@ def _declare(L: ctypes.CDLL) -> None:
     L.ska_fwd_noalloc.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), P(SkaTensor),
                                   ctypes.c_void_p, P(SkaTensor), ctypes.c_void_p]
     L.ska_fwd_noalloc.restype = ctypes.c_int
+    L.ska_set_wait_limit.argtypes = [ctypes.c_uint32]
+    L.ska_set_wait_limit.restype = ctypes.c_int
+    L.ska_check_status.argtypes = [P(SkaShape), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                   ctypes.c_void_p, P(ctypes.c_int64), P(ctypes.c_int)]
+    L.ska_check_status.restype = ctypes.c_int
 
 
 def lib() -> ctypes.CDLL:

@@ -2,8 +2,11 @@
 // include/ska_b200.h): argument validation, workspace layout, dispatch.
 #include "../../include/ska_b200.h"
 #include "ska_common.cuh"
+#include "ska_tc.cuh"
 
+#include <atomic>
 #include <cmath>
+#include <vector>
 
 namespace ska {
 template <typename T>
@@ -33,6 +36,9 @@ namespace {
 
 using ska::Dims;
 
+// polls before a tensor-core kernel's first wait of a role gives up (ska_set_wait_limit)
+std::atomic<uint32_t> g_wait_limit{ska::tc::kWaitLimit};
+
 int make_dims(const SkaShape* s, Dims* d) {
   if (!s) return SKA_ERR_NULL;
   if (s->B < 0 || s->T < 1 || s->H < 1 || s->r < 1 || s->P < 1 || s->chunk_size < 1 || s->power_K < 0)
@@ -58,6 +64,7 @@ int make_dims(const SkaShape* s, Dims* d) {
   d->ridge = s->ridge_eps;
   d->alpha = d->decay ? s->decay_alpha : 1.f;
   d->SW = 2 * d->r * d->r + d->P * d->r;
+  d->wlim = g_wait_limit.load(std::memory_order_relaxed);
   // every kernel's shared-memory tile set must fit one sm_100a CTA (227 KB opt-in)
   const size_t kMaxSmem = 232448;
   if (ska::smem_fwd_stats(*d) > kMaxSmem || ska::smem_bwd_tok(*d) > kMaxSmem) return SKA_ERR_UNSUPPORTED;
@@ -160,8 +167,48 @@ const char* ska_status_string(int code) {
     case SKA_ERR_ALIGN: return "misaligned pointer";
     case SKA_ERR_LAUNCH: return "CUDA kernel launch failed";
     case SKA_ERR_STRATEGY: return "unknown chunk strategy or non-finite decay_alpha";
+    case SKA_ERR_TIMEOUT: return "a tensor-core kernel's bounded wait expired (its chunks' outputs are NaN)";
     default: return "unknown status";
   }
+}
+
+int ska_set_wait_limit(uint32_t polls) {
+  g_wait_limit.store(polls == 0xFFFFFFFFu ? ska::tc::kWaitLimit : polls, std::memory_order_relaxed);
+  return SKA_OK;
+}
+
+int ska_check_status(const SkaShape* shape, const void* saved, size_t saved_bytes, const void* scratch,
+                     size_t scratch_bytes, void* stream, int64_t* first_bad, int* code) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (first_bad) *first_bad = -1;
+  if (code) *code = 0;
+  const size_t n = (size_t)d.B * d.H * d.C;
+  if (n == 0) return SKA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<int> host(n);
+  // forward entries first, then backward (bits 0-1 readout gradient, 2-3 token kernel)
+  for (int part = 0; part < 2; ++part) {
+    const char* base = static_cast<const char*>(part ? scratch : saved);
+    if (!base) continue;
+    if (reinterpret_cast<uintptr_t>(base) % 256) return SKA_ERR_ALIGN;
+    const size_t off = part ? ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P).status
+                            : ska::saved_layout(d.B, d.H, d.C, d.SW).status;
+    const size_t have = part ? scratch_bytes : saved_bytes;
+    if (have < off + n * sizeof(int)) return SKA_ERR_WORKSPACE;
+    if (cudaMemcpyAsync(host.data(), base + off, n * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return SKA_ERR_LAUNCH;
+    for (size_t i = 0; i < n; ++i) {
+      if (host[i] != 0) {
+        if (first_bad) *first_bad = (int64_t)i;
+        if (code) *code = part ? SKA_STATUS_BWD_BASE + host[i] : host[i];
+        return SKA_ERR_TIMEOUT;
+      }
+    }
+  }
+  return SKA_OK;
 }
 
 int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scratch_bytes) {

@@ -48,6 +48,7 @@ struct Dims {
   float ridge;
   float alpha;      // 1 for standard
   int SW;           // floats per statistics record: 2 r r + P r
+  uint32_t wlim;    // polls before a tensor-core kernel's first wait of a role gives up
 };
 
 struct In {
@@ -111,8 +112,10 @@ struct ScratchLayout {
   size_t dmpart;    // float [B][H][C]      per-chunk partial d(max norm)
   size_t dgpart;    // float [B][H][C]      per-chunk partial d(gamma)
   size_t dm;        // float [B][H]
-  size_t status;    // int   [B][H][C]      tensor-core token kernels: 0 ok,
-                    //                      1 TMA wait expired, 2 MMA wait expired
+  size_t status;    // int   [B][H][C]      tensor-core backward kernels: bits 0-1 the
+                    //                      readout-gradient kernel, bits 2-3 the token
+                    //                      kernel; each 0 ok, 1 copy wait expired,
+                    //                      2 product wait expired
   size_t dw;        // float [B][H][C][P r] raw readout gradient sum_t dy_t zq_t^T
   size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the dzq operand
   size_t total;

@@ -1012,6 +1012,9 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
               : tc::launch_stats_tc(d, z, v, stats, cmax, status, st);
     if (e != cudaSuccess) return e;
   } else {
+    // no tensor-core kernel writes the status entries: they read as "no wait expired"
+    const size_t n = (size_t)d.B * d.H * d.C * sizeof(int);
+    if ((e = cudaMemsetAsync(saved + L.status, 0, n, st)) != cudaSuccess) return e;
     k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
   }
   prof_record(1, st);
@@ -1049,6 +1052,10 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   unsigned char* wm = reinterpret_cast<unsigned char*>(scratch + S.wm);
   int* status = reinterpret_cast<int*>(scratch + S.status);
   prof_record(4, st);
+  // the readout-gradient kernel writes every chunk's status; otherwise start from 0
+  // (the token kernel ORs its own code into bits 2-3)
+  if (!full && (e = cudaMemsetAsync(status, 0, (size_t)d.B * d.H * d.C * sizeof(int), st)) != cudaSuccess)
+    return e;
   if (full && (e = tc::launch_dw_tc(d, zq, dy, dw, status, st)) != cudaSuccess) return e;
   prof_record(5, st);
   if (full) {

@@ -110,9 +110,9 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
     __syncwarp();
   }
   int st = 0;
-  if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
+  if (!__syncthreads_and(mbar_wait(&bar_load, 0, d.wlim))) {
     st = 1;
-    mbar_wait(&bar_load, 0);                           // let copies in flight land
+    mbar_wait(&bar_load, 0, kWaitLimit);                           // let copies in flight land
   }
 
   if (warp == 0) {   // one lane issues; the rest of the warp waits converged
@@ -165,9 +165,9 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_stats_tc(const __grid_cons
   }
   if (lane == 0) red[warp] = key;
 
-  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim))) {
     st = 2;
-    mbar_wait(&bar_mma, 0);                            // let MMAs in flight finish
+    mbar_wait(&bar_mma, 0, kWaitLimit);                            // let MMAs in flight finish
   }
   __syncthreads();
   fence_after_sync();
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
     bool ok = true;
     for (int c = 0; c < C; ++c) {
       if (c >= ns) {   // chunk c - ns has left the stage (its product is done, its norms read)
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[c % ns], (uint32_t)(c / ns - 1) & 1u));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[c % ns], (uint32_t)(c / ns - 1) & 1u, d.wlim));
         if (!ok) break;
       }
       if (lane == 0) load_chunk(c);
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
       for (int s = 0; s < ns; ++s) {
         int last = -1;
         for (int c = s; c < nload; c += ns) last = c;
-        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
+        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u, kWaitLimit);
       }
     }
     __syncwarp();
@@ -309,9 +309,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
     int nmma = 0;   // chunks multiplied so far
     bool ok = true;
     for (int c = 0; c < C; ++c) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u));
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u, d.wlim));
       if (ok && c >= kScanBufs)
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[c % kScanBufs], (uint32_t)(c / kScanBufs - 1) & 1u));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[c % kScanBufs], (uint32_t)(c / kScanBufs - 1) & 1u, d.wlim));
       if (!ok) break;
       if (lane == 0) {
         fence_after_sync();
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
       for (int s = 0; s < kScanBufs; ++s) {
         int last = -1;
         for (int c = s; c < nmma; c += kScanBufs) last = c;
-        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kScanBufs) & 1u);
+        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kScanBufs) & 1u, kWaitLimit);
       }
     }
     __syncwarp();
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
 #pragma unroll
     for (int j = 0; j < 32; ++j) pre[j] = 0.f;
     for (int c = 0; c < C; ++c) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[c % kScanBufs], (uint32_t)(c / kScanBufs) & 1u))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[c % kScanBufs], (uint32_t)(c / kScanBufs) & 1u, d.wlim))) {
         if (lane == 0) atomicExch(&err, 1);
         break;
       }
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
   } else if (warp <= 6) {
     // ---- key norms: warp 5 takes the even chunks, warp 6 the odd ones ----
     for (int c = warp - 5; c < C; c += 2) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_load[c % ns], (uint32_t)(c / ns) & 1u, d.wlim))) {
         if (lane == 0) atomicExch(&err, 1);
         break;
       }
@@ -415,7 +415,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) k_stats_scan_tc(const __grid_
   if (err) {   // poison the series
     const float nan = __int_as_float(0x7fc00000);
     for (long long i = tid; i < (long long)C * d.SW; i += kScanThreads) recs[i] = nan;
-    for (int c = tid; c < C; c += kScanThreads) status[bh * C + c] = 1;
+    for (int c = tid; c < C; c += kScanThreads) {
+      status[bh * C + c] = 1;
+      cmax[bh * C + c] = 0ull;   // defined (if meaningless) key norms for the consumers
+    }
   }
   if (warp == 0) {
     fence_after_sync();
@@ -470,9 +473,9 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
     __syncwarp();
   }
   int st = 0;
-  if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
+  if (!__syncthreads_and(mbar_wait(&bar_load, 0, d.wlim))) {
     st = 1;
-    mbar_wait(&bar_load, 0);
+    mbar_wait(&bar_load, 0, kWaitLimit);
   }
   if (warp == 0) {   // one lane issues; the rest of the warp waits converged
     if (st == 0 && lane == 0) {
@@ -489,9 +492,9 @@ __global__ void __launch_bounds__(kStatsThreads, 8) k_dw_tc(const __grid_constan
     }
     __syncwarp();
   }
-  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0))) {
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim))) {
     st = 2;
-    mbar_wait(&bar_mma, 0);
+    mbar_wait(&bar_mma, 0, kWaitLimit);
   }
   __syncthreads();
   fence_after_sync();
@@ -714,9 +717,9 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
   if (warp == 0 && lane < d.C) kmx = cmax[bh * d.C + lane];
   int st = 0;
   if (staged) {
-    if (!__syncthreads_and(mbar_wait(&bar_rec, 0))) {
+    if (!__syncthreads_and(mbar_wait(&bar_rec, 0, d.wlim))) {
       st = 1;
-      mbar_wait(&bar_rec, 0);
+      mbar_wait(&bar_rec, 0, kWaitLimit);
     }
     // every value this thread builds, read from the staged record before any
     // operand row overwrites it
@@ -804,9 +807,9 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     if (lane == 0) s_max = k;
   }
   fence_async_smem();                                  // B operands -> tensor-core proxy
-  if (!__syncthreads_and(mbar_wait(&bar_load, 0))) {
+  if (!__syncthreads_and(mbar_wait(&bar_load, 0, d.wlim))) {
     st = 1;
-    mbar_wait(&bar_load, 0);
+    mbar_wait(&bar_load, 0, kWaitLimit);
   }
 
   // warp 0 issues the dZ and dV products, warp 1 (at the same time) the dZQ product
@@ -872,10 +875,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       if (lane == 0) corr[i] = a;
     }
   }
-  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0) && (!dzq_on || mbar_wait(&bar_mmq, 0)))) {
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim) && (!dzq_on || mbar_wait(&bar_mmq, 0, d.wlim)))) {
     st = 2;
-    mbar_wait(&bar_mma, 0);
-    if (dzq_on) mbar_wait(&bar_mmq, 0);
+    mbar_wait(&bar_mma, 0, kWaitLimit);
+    if (dzq_on) mbar_wait(&bar_mmq, 0, kWaitLimit);
   }
   __syncthreads();
   fence_after_sync();
@@ -928,7 +931,7 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       store_bf16x16(tok_ptr(dzq, b, t, h) + j0, x);
     }
   }
-  if (tid == 0) status[q] = st;
+  if (tid == 0) status[q] |= st << 2;   // bits 2-3 (bits 0-1: the readout-gradient kernel)
   fence_before_sync();
   __syncthreads();
   if (warp == 0) {
@@ -1091,7 +1094,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__
     bool ok = true;
     for (int j = 0; j < nj; ++j) {
       if (j >= ns) {   // chunk j - ns's product has read the stage
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[j % ns], (uint32_t)(j / ns - 1) & 1u));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[j % ns], (uint32_t)(j / ns - 1) & 1u, d.wlim));
         if (!ok) break;
       }
       if (lane == 0) {
@@ -1114,7 +1117,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__
       for (int s = 0; s < ns; ++s) {
         int last = -1;
         for (int j = s; j < nload; j += ns) last = j;
-        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u);
+        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u, kWaitLimit);
       }
     }
     __syncwarp();
@@ -1124,9 +1127,9 @@ __global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__
     int nmma = 0;
     bool ok = true;
     for (int j = 0; j < nj; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[j % ns], (uint32_t)(j / ns) & 1u));
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[j % ns], (uint32_t)(j / ns) & 1u, d.wlim));
       if (ok && j >= kDwBufs)
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[j % kDwBufs], (uint32_t)(j / kDwBufs - 1) & 1u));
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[j % kDwBufs], (uint32_t)(j / kDwBufs - 1) & 1u, d.wlim));
       if (!ok) break;
       if (lane == 0) {
         fence_after_sync();
@@ -1146,7 +1149,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__
       for (int s = 0; s < kDwBufs; ++s) {
         int last = -1;
         for (int j = s; j < nmma; j += kDwBufs) last = j;
-        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kDwBufs) & 1u);
+        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kDwBufs) & 1u, kWaitLimit);
       }
     }
     __syncwarp();
@@ -1155,7 +1158,7 @@ __global__ void __launch_bounds__(kDwThreads, 1) k_dw_ps(const __grid_constant__
     const int qd = warp & 3;
     const int row = 16 * qd + lane;
     for (int j = 0; j < nj; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[j % kDwBufs], (uint32_t)(j / kDwBufs) & 1u))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[j % kDwBufs], (uint32_t)(j / kDwBufs) & 1u, d.wlim))) {
         if (lane == 0) atomicExch(&err, 1);
         break;
       }

@@ -43,10 +43,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// true when the phase with the given parity has completed; gives up after kWaitLimit polls
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// true when the phase with the given parity has completed; gives up after `limit`
+// polls (0: at once, without polling).  The first wait of each role takes the
+// launch's limit (Dims::wlim, kWaitLimit unless a caller lowered it through
+// ska_set_wait_limit); the drain waits after a failure always take kWaitLimit, so
+// that no CTA leaves with a copy or product still in flight.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+  for (uint32_t it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"

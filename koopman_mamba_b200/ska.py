@@ -158,8 +158,9 @@ class SKAModule(nn.Module):
     Args (same meaning and defaults as upstream ``ska.py:368-371``):
         d_model, n_heads, rank=48, head_dim=None (d_model // n_heads),
         ridge_eps=1e-3, scale=1.5 (initial eta), power_K=2, chunk_size=64,
-        backend='auto' (accepted for compatibility; the core always runs on the
-        sm_100a kernels), chunk_strategy='standard' | 'decay' ('overlap' raises
+        backend='auto' (resolved to 'sm100a'; 'pytorch' / 'triton' are accepted
+        for compatibility, and the core always runs on the sm_100a kernels),
+        chunk_strategy='standard' | 'decay' ('overlap' raises
         NotImplementedError), overlap_fraction=0.5, decay_alpha=0.95.
     """
 
@@ -181,7 +182,11 @@ class SKAModule(nn.Module):
         self.chunk_strategy = chunk_strategy
         self.overlap_fraction = overlap_fraction
         self.decay_alpha = decay_alpha
-        self.backend = backend
+        # the reference resolves 'auto' to the backend that will run (ska.py:383-386);
+        # here that is always the sm_100a kernels.  An explicit 'pytorch' or 'triton'
+        # is kept as given (for extra_repr and checkpoint tooling) but runs the same
+        # kernels.
+        self.backend = "sm100a" if backend == "auto" else backend
 
         # same construction and init order as the reference (ska.py:389-400), so a
         # seeded construction gives identical weights

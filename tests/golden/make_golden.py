@@ -1,8 +1,9 @@
 """Generate golden SKA vectors by running the upstream reference itself.
 
-Run in a container where the upstream project is mounted (read-only) at
-``/root/reference``; writes ``tests/golden/*.npz``.  The GPU machines never run
-this script: they only read the committed ``.npz`` files.
+Run where a checkout of the upstream project is available; its
+``koopman-lm-fast`` directory is given by ``--ref-root`` or the environment
+variable ``SKA_REFERENCE_ROOT``.  Writes ``tests/golden/*.npz``.  The GPU
+machines never run this script: they only read the committed ``.npz`` files.
 
 Every case calls the reference's own code with ``backend='pytorch'`` (its
 ``auto`` backend picks Triton, which cannot run on a CPU), so the gradients
@@ -17,7 +18,7 @@ The ``module_*`` case runs the whole ``SKAModule`` (projections, eta,
 out_proj) with seeded weights and stores its state_dict, so the drop-in
 module can be checked end to end.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py --ref-root <upstream>/koopman-lm-fast
 """
 from __future__ import annotations
 
@@ -28,11 +29,13 @@ import sys
 import numpy as np
 import torch
 
-REF_ROOT = "/root/reference/koopman-lm-fast"
+REF_ROOT = os.environ.get("SKA_REFERENCE_ROOT", "")
 OUT_DIR = os.path.dirname(os.path.abspath(__file__))
 
 
 def _import_reference():
+    if not REF_ROOT or not os.path.isdir(os.path.join(REF_ROOT, "koopman_lm")):
+        raise SystemExit("pass --ref-root (or set SKA_REFERENCE_ROOT) to the upstream koopman-lm-fast directory")
     sys.path.insert(0, REF_ROOT)
     from koopman_lm import ska as ref_ska                     # noqa: E402
     from koopman_lm import adaptive_chunking as ref_ac        # noqa: E402
@@ -186,4 +189,9 @@ def main():
 
 
 if __name__ == "__main__":
+    import argparse
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--ref-root", default=REF_ROOT,
+                    help="the upstream koopman-lm-fast directory (default: $SKA_REFERENCE_ROOT)")
+    REF_ROOT = ap.parse_args().ref_root
     main()

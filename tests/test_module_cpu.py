@@ -63,3 +63,11 @@ def test_cpu_tensors_raise_no_fallback():
     z = torch.randn(1, 16, 2, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ska_core(z, z, torch.randn(1, 16, 2, 64), torch.tensor(1.0))
+
+
+def test_backend_auto_resolves_like_the_reference():
+    """The reference resolves backend='auto' to the backend that runs (ska.py:383-386);
+    here that is always the sm_100a kernels, and explicit values are kept."""
+    assert SKAModule(64, 2, rank=16).backend == "sm100a"
+    assert "backend=sm100a" in SKAModule(64, 2, rank=16).extra_repr()
+    assert SKAModule(64, 2, rank=16, backend="pytorch").backend == "pytorch"
