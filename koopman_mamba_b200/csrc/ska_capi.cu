@@ -194,7 +194,7 @@ int ska_check_status(const SkaShape* shape, const void* saved, size_t saved_byte
     if (!base) continue;
     if (reinterpret_cast<uintptr_t>(base) % 256) return SKA_ERR_ALIGN;
     const size_t off = part ? ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P).status
-                            : ska::saved_layout(d.B, d.H, d.C, d.SW).status;
+                            : ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P).status;
     const size_t have = part ? scratch_bytes : saved_bytes;
     if (have < off + n * sizeof(int)) return SKA_ERR_WORKSPACE;
     if (cudaMemcpyAsync(host.data(), base + off, n * sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
@@ -215,7 +215,7 @@ int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scrat
   Dims d{};
   const int rc = make_dims(shape, &d);
   if (rc) return rc;
-  if (saved_bytes) *saved_bytes = ska::saved_layout(d.B, d.H, d.C, d.SW).total;
+  if (saved_bytes) *saved_bytes = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P).total;
   if (scratch_bytes) *scratch_bytes = ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P).total;
   return SKA_OK;
 }
@@ -236,7 +236,7 @@ int ska_fwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   if (!work) return SKA_OK;
   if (!gamma || !saved) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
-  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW);
+  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
   if (saved_bytes < L.total) return SKA_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
@@ -271,7 +271,7 @@ int ska_bwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   }
   if (!gamma || !saved || !scratch) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256 || reinterpret_cast<uintptr_t>(scratch) % 256) return SKA_ERR_ALIGN;
-  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW);
+  const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
   const ska::ScratchLayout S = ska::scratch_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
   if (saved_bytes < L.total || scratch_bytes < S.total) return SKA_ERR_WORKSPACE;
   cudaError_t e;

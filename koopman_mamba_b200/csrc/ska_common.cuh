@@ -97,6 +97,13 @@ __device__ __forceinline__ void st_tok(const Out& x, int b, int t, int h, int j,
 
 __host__ __device__ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Chunk operators kept by the warp-path forward (r <= 32) for the backward, one
+// 32 x 32 fp32 row-major tile each (rows and columns past r hold the padding the
+// warp kernels use: identity for Li and S, zero elsewhere, identity for A^K when
+// K = 0):
+constexpr int kOpLi = 0, kOpA = 1, kOpAK = 2, kOpU = 3, kOpV = 4, kOpS = 5, kNumOps = 6;
+constexpr int kOpFloats = 32 * 32;
+
 struct SavedLayout {
   size_t stats;     // float [B][H][C][SW]  exclusive-scanned raw statistics
   size_t cmax;      // u64   [B][H][C]      packed (norm bits, ~t) chunk maxima
@@ -104,6 +111,11 @@ struct SavedLayout {
   size_t flags;     // int   [B][H][C]      bit0: jittered, bit1: jitter failed too
   size_t status;    // int   [B][H][C]      tensor-core statistics kernel: 0 ok,
                     //                      1 TMA wait expired, 2 MMA wait expired
+  size_t ops;       // float [B][H][C][kNumOps][32][32]  (r <= 32 only)
+                    //   Li = L^{-1}, A = gamma' A0 / max(sigma, 1), A^K, U = A^K Li,
+                    //   V = Li^T U, S = Li^T Li (bf16 I/O forwards write them)
+  size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the
+                    //   tensor-core operand of the readout products (r <= 32 only)
   size_t total;
 };
 
@@ -117,19 +129,22 @@ struct ScratchLayout {
                     //                      kernel; each 0 ok, 1 copy wait expired,
                     //                      2 product wait expired
   size_t dw;        // float [B][H][C][P r] raw readout gradient sum_t dy_t zq_t^T
-  size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the dzq operand
   size_t total;
 };
 
-__host__ __device__ inline SavedLayout saved_layout(long long B, long long H, long long C, long long SW) {
+__host__ __device__ inline SavedLayout saved_layout(long long B, long long H, long long C, long long SW,
+                                                   long long r, long long P) {
   SavedLayout L{};
   const size_t n = (size_t)B * H * C;
+  const bool warp_ops = r <= 32;
   size_t off = 0;
   L.stats = off; off = align256(off + n * SW * sizeof(float));
   L.cmax = off;  off = align256(off + n * sizeof(unsigned long long));
   L.invs = off;  off = align256(off + n * sizeof(float));
   L.flags = off; off = align256(off + n * sizeof(int));
   L.status = off; off = align256(off + n * sizeof(int));
+  L.ops = off;   off = align256(off + (warp_ops ? n * kNumOps * kOpFloats * sizeof(float) : 0));
+  L.wm = off;    off = align256(off + (warp_ops ? n * (size_t)P * r * 4 : 0));
   L.total = off;
   return L;
 }
@@ -145,7 +160,6 @@ __host__ __device__ inline ScratchLayout scratch_layout(long long B, long long H
   L.dm = off;     off = align256(off + (size_t)B * H * sizeof(float));
   L.status = off; off = align256(off + n * sizeof(int));
   L.dw = off;     off = align256(off + n * (size_t)P * r * sizeof(float));
-  L.wm = off;     off = align256(off + n * (size_t)P * r * 4);
   L.total = off;
   return L;
 }

@@ -931,7 +931,7 @@ size_t smem_bwd_tok(const Dims& d) {
 bool warp_path_ok(const Dims& d);
 template <typename IO>
 cudaError_t launch_fwd_chunk_w(const Dims&, const In&, const float*, const Out&, const float*,
-                               const unsigned long long*, float*, int*, cudaStream_t);
+                               const unsigned long long*, float*, int*, float*, unsigned char*, cudaStream_t);
 template <typename IO>
 cudaError_t launch_bwd_chunk_w(const Dims&, const In&, const In&, const float*, const Out&, const float*,
                                const unsigned long long*, const float*, const int*, float*, float*, float*,
@@ -954,8 +954,8 @@ bool dw_tc_ok(const Dims& d, const In& zq, const In& dy);
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st);
 }  // namespace tc
 cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               const float* invs, const int* flags, const float* dwraw, float* dstats,
-                               float* dmpart, float* dgpart, unsigned char* wm, cudaStream_t st);
+                               const float* invs, const float* ops, const float* dwraw, float* dstats,
+                               float* dmpart, float* dgpart, cudaStream_t st);
 
 // Which backward kernels run (bf16 token tensors with TMA-compatible layouts):
 //   full: dW' and dzq on tcgen05, chunk operators without a token pass (r <= 32)
@@ -1021,7 +1021,12 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if (!fused) k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   prof_record(2, st);
   if (warp_path_ok(d)) {
-    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, y, stats, cmax, invs, flags, st)) != cudaSuccess) return e;
+    // bf16 forwards keep the chunk operators and W / m for the tensor-core backward
+    const bool keep = std::is_same<IO, __nv_bfloat16>::value;
+    float* ops = keep ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
+    unsigned char* wm = keep ? reinterpret_cast<unsigned char*>(saved + L.wm) : nullptr;
+    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, y, stats, cmax, invs, flags, ops, wm, st)) != cudaSuccess)
+      return e;
   } else {
     k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
   }
@@ -1049,7 +1054,10 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   bool full = false, tc_tok = false;
   bwd_tc_paths<IO>(d, z, zq, v, dy, dz, dzq, dv, &full, &tc_tok);
   float* dw = reinterpret_cast<float*>(scratch + S.dw);
-  unsigned char* wm = reinterpret_cast<unsigned char*>(scratch + S.wm);
+  // the bf16 forward on the warp path (which the full tensor-core backward implies)
+  // kept the chunk operators and W / m
+  const float* ops = reinterpret_cast<const float*>(saved + L.ops);
+  const unsigned char* wm = reinterpret_cast<const unsigned char*>(saved + L.wm);
   int* status = reinterpret_cast<int*>(scratch + S.status);
   prof_record(4, st);
   // the readout-gradient kernel writes every chunk's status; otherwise start from 0
@@ -1059,8 +1067,7 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if (full && (e = tc::launch_dw_tc(d, zq, dy, dw, status, st)) != cudaSuccess) return e;
   prof_record(5, st);
   if (full) {
-    if ((e = launch_bwd_chunk_s(d, gamma, stats, cmax, invs, flags, dw, dstats, dmpart, dgpart, wm, st)) !=
-        cudaSuccess)
+    if ((e = launch_bwd_chunk_s(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st)) != cudaSuccess)
       return e;
   } else if (warp_path_ok(d)) {
     if ((e = launch_bwd_chunk_w<IO>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart, dgpart,

@@ -255,12 +255,37 @@ __device__ __forceinline__ void store_tok_block(const Out& x, int b, int tok0, i
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
+// W / m rows of P block pb (tile TW) as bf16 hi and lo planes in the layout of the
+// tensor-core readout operands: the 16-byte row of j-group ng and p sits at byte
+// ng * P * 16 + p * 16 of a plane (the lo plane follows the hi plane)
+__device__ __forceinline__ void store_wm_block(unsigned char* wq, const float* TW, int pb, int P, int r, int lane) {
+  float u[32];
+  ld_row(u, TW, lane);
+  const int p = pb * 32 + lane;
+  if (p >= P) return;
+#pragma unroll
+  for (int ng = 0; ng < 4; ++ng) {
+    if (8 * ng >= r) break;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = u[8 * ng + e];
+    uint4 hi, lo;
+    split_bf16x8(x, hi, lo);
+    *reinterpret_cast<uint4*>(wq + (size_t)ng * P * 16 + (size_t)p * 16) = hi;
+    *reinterpret_cast<uint4*>(wq + (size_t)P * r * 2 + (size_t)ng * P * 16 + (size_t)p * 16) = lo;
+  }
+}
+
+// ops_out / wm_out (both or neither): keep the chunk's operators (kOp* tiles) and
+// W / m for the backward (and the tensor-core readout); nullptr = do not keep them.
 template <typename IO, int NPB>
 __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, const float* __restrict__ gamma_p,
                                                                 Out y, const float* __restrict__ stats,
                                                                 const unsigned long long* __restrict__ cmax,
                                                                 float* __restrict__ invs_out,
-                                                                int* __restrict__ flags_out) {
+                                                                int* __restrict__ flags_out,
+                                                                float* __restrict__ ops_out,
+                                                                unsigned char* __restrict__ wm_out) {
   constexpr bool kFast = false;   // fp32-level products (split operands) for every I/O type
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
@@ -292,9 +317,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
 
   const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1, pre);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
+  float* opq = ops_out ? ops_out + q * (long long)(kNumOps * kOpFloats) : nullptr;
+  if (opq) store_mat(opq + kOpLi * kOpFloats, T1, 32, 32, 1.f, lane);
   wmmp<kFast, 32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
   cp_async_wait<0>();                                                     // M and C have landed
   __syncwarp();
+  if (opq) store_mat(opq + kOpS * kOpFloats, T2, 32, 32, 1.f, lane);
   const float* TM = TW;                                                   // M (raw): A0 = (M / m^2) S
   if (!pre_mc) {
     load_mat(T0, rec + r * r, r, r, 1.f, lane);
@@ -316,6 +344,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     st_row(T3, lane, a);                                                  // T3 = A
   }
   __syncwarp();
+  if (opq) store_mat(opq + kOpA * kOpFloats, T3, 32, 32, 1.f, lane);
   // A^K (K = 0: identity), ping-pong in T0 / T2
   const float* AK = T3;
   if (d.K == 0) {
@@ -329,10 +358,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     AK = out;
   }
   __syncwarp();
+  if (opq) store_mat(opq + kOpAK * kOpFloats, AK, 32, 32, 1.f, lane);
   float* TU = (AK == T0) ? T2 : T0;
   float* TV = (d.K == 1) ? T2 : T3;
   wmmp<kFast, 32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
   __syncwarp();
+  if (opq) store_mat(opq + kOpU * kOpFloats, TU, 32, 32, 1.f, lane);
   wmmp<kFast, 32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
   if (!pre_mc) {
 #pragma unroll
@@ -340,8 +371,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
       load_mat(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, 1.f, lane);   // C rows
   }
   __syncwarp();
+  if (opq) store_mat(opq + kOpV * kOpFloats, TV, 32, 32, 1.f, lane);
   wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im2);  // W / m = (C / m) V / m
   __syncwarp();
+  if (wm_out && (r & 7) == 0) {
+    unsigned char* wq = wm_out + (size_t)q * P * r * 4;
+#pragma unroll
+    for (int pb = 0; pb < NPB; ++pb) store_wm_block(wq, TW + pb * kTile, pb, P, r, lane);
+  }
 
   // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T.
   // Two token blocks at a time (T0, T1; Li is dead), both blocks' loads together.
@@ -649,31 +686,37 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_w(Dims d, In zq, I
 
 
 // ---------------------------------------------------------------------------
-// backward without the token pass (bf16 token tensors on the tensor-core path)
+// backward without the token pass (bf16 token tensors on the tensor-core path),
+// from the operators the forward kept
 //
-// The token-level products leave this kernel: dW' = sum_t dy_t zq_t^T comes from
-// k_dw_tc, and dzq = dy (W / m) is formed by k_tok_bwd_tc from the W / m this
-// kernel writes.  What remains is the chunk operator's chain rule.  The P x r
-// blocks of Cn, W and dW stream through two tiles, so a warp holds 8 tiles
-// whatever P is (7 warps per SM instead of 4 at P = 64).  Also
-//   sum_t dqn_t . zq_t = sum_t dy_t^T W zq_t = <W, dW'>,
-// so the d(max norm) share of the readout needs no tokens either.
-// W / m is stored as bf16 hi and lo planes, each in the MN-major canonical
-// layout of a B operand with N = r and K = P: the 16-byte row of n-group ng and
-// k (= p) sits at byte ng * P * 16 + p * 16.
+// The token-level products live elsewhere: dW' = sum_t dy_t zq_t^T comes from
+// k_dw_ps / k_dw_tc, and dzq = dy (W / m) is formed by k_tok_bwd_tc from the
+// W / m planes the forward wrote.  The forward also kept the chunk's Li, A, A^K,
+// U, V and S (kOp* tiles), so nothing of the forward is recomputed here (no
+// Cholesky, no inverse, no power iteration): what remains is the chain rule.
+//   dW = dW' / m, dV = Cn^T dW = C^T dW' / m^2, dCn = dW V^T = dW' V^T / m;
+// the readout's share of d(max norm) is sum_t dqn_t . zq_t / m = <W, dW> = <V, dV>.
+// The P x r blocks of C and dW' stream through two tiles, so a warp holds 8 tiles
+// whatever P is.
 // ---------------------------------------------------------------------------
 constexpr int kBwdStreamTiles = 8;
+
+// tile T <- rows [0, nrows) x columns [0, ncols) of a row-major global matrix, by
+// cp.async when the source allows it (then it belongs to the lane's next commit
+// group), else by plain loads
+__device__ __forceinline__ void fetch_tile(float* T, const float* src, int nrows, int ncols, int lane) {
+  if (!cp_tile_async(T, src, nrows, ncols, lane)) load_mat(T, src, nrows, ncols, 1.f, lane);
+}
 
 __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const float* __restrict__ gamma_p,
                                                                 const float* __restrict__ stats,
                                                                 const unsigned long long* __restrict__ cmax,
                                                                 const float* __restrict__ invs_in,
-                                                                const int* __restrict__ flags_in,
+                                                                const float* __restrict__ ops,
                                                                 const float* __restrict__ dwraw,
                                                                 float* __restrict__ dstats,
                                                                 float* __restrict__ dmpart,
-                                                                float* __restrict__ dgpart,
-                                                                unsigned char* __restrict__ wm) {
+                                                                float* __restrict__ dgpart) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const long long q = (long long)blockIdx.x * (blockDim.x >> 5) + w;
   if (q >= (long long)d.B * d.H * d.C) return;
@@ -685,117 +728,86 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   float* TA = TLi + kTile;
   float* TAK = TA + kTile;
   float* TV = TAK + kTile;
-  float* TX = TV + kTile;
+  float* TX = TV + kTile;       // dV
   float* TY = TX + kTile;
   float* TP0 = TY + kTile;
   float* TP1 = TP0 + kTile;
   const float* rec = stats + q * d.SW;
+  const float* opq = ops + q * (long long)(kNumOps * kOpFloats);
+  const float* dwq = dwraw + q * (long long)P * r;
+  const float* crec = rec + 2 * r * r;
+  // group 0: V and the first P block of C and dW'; group 1: Li, A, A^K
+  fetch_tile(TV, opq + kOpV * kOpFloats, 32, 32, lane);
+  fetch_tile(TP0, crec, min(32, P), r, lane);
+  fetch_tile(TP1, dwq, min(32, P), r, lane);
+  cp_async_commit();
+  fetch_tile(TLi, opq + kOpLi * kOpFloats, 32, 32, lane);
+  fetch_tile(TA, opq + kOpA * kOpFloats, 32, 32, lane);
+  fetch_tile(TAK, opq + kOpAK * kOpFloats, 32, 32, lane);
+  cp_async_commit();
   const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
   const float gam = *gamma_p;
   const float gs = fminf(fmaxf(gam, 1.f), 1.5f);
-  const bool gpass = gam >= 1.f && gam <= 1.5f;
+  const bool gpass = gam >= 1.f && gam <= 1.5f;       // clamp passes gradients inclusively
   const float kk = gs * invs_in[q];
-  const int flag = flags_in[q];
   float t[32], u[32];
 
-  // ---- recompute the forward operator (same arithmetic as k_fwd_chunk_w) ----
-  factor_and_invert(d, rec, lane, im2, (flag & 1) != 0, TX, TLi);
-  wmmp<false, 32, 32, true, false, false>(TY, TLi, kTile, TLi, 1.f);      // TY = S
-  __syncwarp();
-  load_mat(TX, rec + r * r, r, r, im2, lane);                             // TX = Mn
-  __syncwarp();
-  wmmp<false, 32, 32, false, false, false>(TA, TX, kTile, TY, 1.f);       // TA = A0
-  __syncwarp();
-  ld_row(t, TA, lane);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) t[j] *= kk;
-  __syncwarp();
-  st_row(TA, lane, t);                                                    // TA = A
-  __syncwarp();
-  const float* AK = TAK;
-  if (d.K == 0) {
-    st_identity(TAK, lane);
-  } else if (d.K == 1) {
-    AK = TA;
-  } else {
-    const float* cur = TA;
-    for (int s = 1; s < d.K; ++s) {
-      float* out = (s == d.K - 1) ? TAK : ((s & 1) ? TX : TY);
-      wmmp<false, 32, 32, false, false, false>(out, cur, kTile, TA, 1.f);
-      __syncwarp();
-      cur = out;
-    }
-  }
-  __syncwarp();
-  wmmp<false, 32, 32, false, false, false>(TX, AK, kTile, TLi, 1.f);      // TX = U
-  __syncwarp();
-  wmmp<false, 32, 32, true, false, false>(TV, TLi, kTile, TX, 1.f);       // TV = V
-
-  // ---- P blocks: W = Cn V, dW = dW' / m, dV = Cn^T dW, dCn = dW V^T ----
-  float dmq = 0.f, dmc = 0.f;
-  const float* dwq = dwraw + q * (long long)P * r;
-  unsigned char* wq = wm + (size_t)q * P * r * 4;
+  // ---- P blocks: dV = C^T dW' / m^2,  dCn / m = dW' V^T / m^2 ----
+  float dmc = 0.f;
 #pragma unroll 1
   for (int pb = 0; pb < p_blocks(P); ++pb) {
     const int p = pb * 32 + lane;
-    __syncwarp();
-    load_mat(TP0, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, im, lane);   // Cn rows of block pb
-    __syncwarp();
-    wmmp<false, 32, 32, false, false, false>(TP1, TP0, kTile, TV, 1.f);   // W rows
-    __syncwarp();
-    ld_row(u, TP1, lane);
-    load_mat(TY, dwq + pb * 32 * r, P - pb * 32, r, 1.f, lane);           // dW' rows (raw)
-    __syncwarp();
-    ld_row(t, TY, lane);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) dmq = fmaf(u[j], t[j], dmq);
-    if (p < P) {
-#pragma unroll
-      for (int ng = 0; ng < 4; ++ng) {
-        float x[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = u[8 * ng + e] * im;
-        uint4 hi, lo;
-        split_bf16x8(x, hi, lo);
-        *reinterpret_cast<uint4*>(wq + (size_t)ng * P * 16 + (size_t)p * 16) = hi;
-        *reinterpret_cast<uint4*>(wq + (size_t)P * r * 2 + (size_t)ng * P * 16 + (size_t)p * 16) = lo;
-      }
+    if (pb > 0) {
+      __syncwarp();
+      fetch_tile(TP0, crec + pb * 32 * r, P - pb * 32, r, lane);
+      fetch_tile(TP1, dwq + pb * 32 * r, P - pb * 32, r, lane);
+      cp_async_commit();
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) t[j] *= im;
-    __syncwarp();
-    st_row(TP1, lane, t);                                                 // dW rows
     __syncwarp();
     if (pb == 0)
-      wmmp<false, 32, 32, true, false, false>(TX, TP0, kTile, TP1, 1.f);  // dV  = Cn^T dW
+      wmmp<false, 32, 32, true, false, false>(TX, TP0, kTile, TP1, im2);   // dV  = C^T dW' / m^2
     else
-      wmmp<false, 32, 32, true, false, true>(TX, TP0, kTile, TP1, 1.f);   // dV += Cn^T dW
-    wmmp<false, 32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);     // dCn = dW V^T
+      wmmp<false, 32, 32, true, false, true>(TX, TP0, kTile, TP1, im2);    // dV += C^T dW' / m^2
+    wmmp<false, 32, 32, false, true, false>(TY, TP1, kTile, TV, 1.f);      // TY = dW' V^T = m dCn
     __syncwarp();
     ld_row(t, TY, lane);
     ld_row(u, TP0, lane);
     if (p < P) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (j < r) dmc = fmaf(t[j], u[j], dmc);
+        if (j < r) dmc = fmaf(t[j], u[j], dmc);           // <TY, C> = m^2 <dCn, Cn>
     }
-    store_mat(dstats + q * d.SW + 2 * r * r + pb * 32 * r, TY, P - pb * 32, r, im, lane);   // dCn / m
-    __syncwarp();
+    store_mat(dstats + q * d.SW + 2 * r * r + pb * 32 * r, TY, P - pb * 32, r, im2, lane);   // dCn / m
   }
-  // live: TLi, TA, AK, TX (dV); free: TV, TY, TP0, TP1
+  __syncwarp();
+  float dmq = 0.f;                                        // <V, dV> = <W, dW>
+  ld_row(t, TV, lane);
+  ld_row(u, TX, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) dmq = fmaf(t[j], u[j], dmq);
+  __syncwarp();
+  // V is dead: U -> TY, S -> TP1 (group 2)
+  fetch_tile(TY, opq + kOpU * kOpFloats, 32, 32, lane);
+  fetch_tile(TP1, opq + kOpS * kOpFloats, 32, 32, lane);
+  cp_async_commit();
+  cp_async_wait<1>();                                     // Li, A, A^K have landed
+  __syncwarp();
+  // live: TLi, TA, TAK, TX (dV); U, S in flight
+  float* TdU = TV;
   float* TdLi = TP0;
-  float* TdU = TY;
-  float* TU = TP1;
-  float* TdAK = TV;
   wmmp<false, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
-  wmmp<false, 32, 32, false, false, false>(TU, AK, kTile, TLi, 1.f);       // U = A^K Li
+  cp_async_wait<0>();
   __syncwarp();
-  wmmp<false, 32, 32, false, true, false>(TdLi, TU, kTile, TX, 1.f);       // dLi = U dV^T
+  wmmp<false, 32, 32, false, true, false>(TdLi, TY, kTile, TX, 1.f);       // dLi = U dV^T
+  __syncwarp();
+  float* TdAK = TX;                                                       // dV is dead
   wmmp<false, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmmp<false, 32, 32, true, false, true>(TdLi, TAK, kTile, TdU, 1.f);      // dLi += AK^T dU
   __syncwarp();
-  wmmp<false, 32, 32, true, false, true>(TdLi, AK, kTile, TdU, 1.f);       // dLi += AK^T dU
-  __syncwarp();
-  // dA from dAK; free: TX, TY, TP1, and TAK unless it is A (K = 1)
+  // dA from dAK; free: TY (U), TV (dU), TAK
   const float* TdA;
   if (d.K == 0) {
     zero(t);
@@ -805,7 +817,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     TdA = TdAK;
   } else {
     // Horner over E_s = dAK (A^T)^s:  E <- E A^T,  H <- E + A^T H,  E = H = dAK at start
-    float* pool[4] = {TX, TY, TP1, TAK};
+    float* pool[4] = {TY, TV, TAK, TX};
     const float* E = TdAK;
     const float* Hc = TdAK;
     int pi = 0;
@@ -830,33 +842,33 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   ld_row(u, TA, lane);
 #pragma unroll
   for (int j = 0; j < 32; ++j) dg = fmaf(t[j], u[j], dg);
+  // three scratch tiles among {TY, TV, TAK, TX, TA} not holding dA (A is dead now)
   float* fr[3];
   {
-    float* cand[5] = {TV, TX, TY, TP1, TAK};
+    float* cand[5] = {TY, TV, TAK, TX, TA};
     int nf = 0;
     for (int i = 0; i < 5 && nf < 3; ++i)
       if (cand[i] != TdA) fr[nf++] = cand[i];
   }
-  float* TS = fr[0];
+  float* TS = TP1;
+  float* TMn = fr[0];
   float* TdMn = fr[1];
   float* TdS = fr[2];
-  __syncwarp();
-  wmmp<false, 32, 32, true, false, false>(TS, TLi, kTile, TLi, 1.f);       // S
   __syncwarp();
   wmmp<false, 32, 32, false, false, false>(TdMn, TdA, kTile, TS, kk);      // dMn = kk dA S
   __syncwarp();
   float dmm = 0.f;
-  load_mat(TS, rec + r * r, r, r, im2, lane);                             // TS = Mn (S done)
+  load_mat(TMn, rec + r * r, r, r, im2, lane);                            // Mn
   store_mat(dstats + q * d.SW + r * r, TdMn, r, r, im2, lane);            // dMn / m^2
   __syncwarp();
   ld_row(t, TdMn, lane);
-  ld_row(u, TS, lane);
+  ld_row(u, TMn, lane);
   if (lane < r) {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < r) dmm = fmaf(t[j], u[j], dmm);
   }
-  wmmp<false, 32, 32, true, false, false>(TdS, TS, kTile, TdA, kk);        // dS = kk Mn^T dA
+  wmmp<false, 32, 32, true, false, false>(TdS, TMn, kTile, TdA, kk);       // dS = kk Mn^T dA
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);
@@ -872,7 +884,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmmp<false, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T
+  wmmp<false, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T (S is dead)
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -908,7 +920,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   st_row(TdMn, lane, t);                                                  // T1 is dead: sym(dGn)
   __syncwarp();
   store_mat(dstats + q * d.SW, TdMn, r, r, im2, lane);                    // dGn / m^2
-  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc + dmq * im);
+  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc * im2 + dmq);
   const float dgs = warp_sum32(dg);
   if (lane == 0) {
     dmpart[q] = -tot / m;
@@ -960,11 +972,13 @@ static cudaError_t launch_w(Kern kern, const Dims& d, size_t per_warp, cudaStrea
 
 template <typename IO>
 cudaError_t launch_fwd_chunk_w(const Dims& d, const In& zq, const float* gamma, const Out& y, const float* stats,
-                               const unsigned long long* cmax, float* invs, int* flags, cudaStream_t st) {
+                               const unsigned long long* cmax, float* invs, int* flags, float* ops,
+                               unsigned char* wm, cudaStream_t st) {
   Dims dd = d;
   In zz = zq;
   Out yy = y;
-  void* args[] = {&dd, &zz, (void*)&gamma, &yy, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags};
+  void* args[] = {&dd, &zz, (void*)&gamma, &yy, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags,
+                  (void*)&ops, (void*)&wm};
   const size_t pw = fwd_warp_bytes(d);
   switch (wpc::p_blocks(d.P)) {
     case 1: return launch_w(wpc::k_fwd_chunk_w<IO, 1>, d, pw, st, args);
@@ -993,19 +1007,20 @@ cudaError_t launch_bwd_chunk_w(const Dims& d, const In& zq, const In& dy, const 
 }
 
 cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               const float* invs, const int* flags, const float* dwraw, float* dstats,
-                               float* dmpart, float* dgpart, unsigned char* wm, cudaStream_t st) {
+                               const float* invs, const float* ops, const float* dwraw, float* dstats,
+                               float* dmpart, float* dgpart, cudaStream_t st) {
   Dims dd = d;
-  void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags, (void*)&dwraw,
-                  (void*)&dstats, (void*)&dmpart, (void*)&dgpart, (void*)&wm};
+  void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&ops, (void*)&dwraw,
+                  (void*)&dstats, (void*)&dmpart, (void*)&dgpart};
   return launch_w(wpc::k_bwd_chunk_s, d, (size_t)wpc::kBwdStreamTiles * wpc::kTile * sizeof(float), st, args);
 }
 
 template cudaError_t launch_fwd_chunk_w<float>(const Dims&, const In&, const float*, const Out&, const float*,
-                                               const unsigned long long*, float*, int*, cudaStream_t);
+                                               const unsigned long long*, float*, int*, float*, unsigned char*,
+                                               cudaStream_t);
 template cudaError_t launch_fwd_chunk_w<__nv_bfloat16>(const Dims&, const In&, const float*, const Out&,
                                                        const float*, const unsigned long long*, float*, int*,
-                                                       cudaStream_t);
+                                                       float*, unsigned char*, cudaStream_t);
 template cudaError_t launch_bwd_chunk_w<float>(const Dims&, const In&, const In&, const float*, const Out&,
                                                const float*, const unsigned long long*, const float*, const int*,
                                                float*, float*, float*, cudaStream_t);
