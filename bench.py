@@ -382,6 +382,8 @@ class Runner:
         L, p = self.L, self.path
         names = ["k_stats_scan"] if p & L.SKA_PATH_FUSED_SCAN else ["k_fwd_stats", "k_scan_fwd"]
         names.append("k_fwd_chunk")
+        if p & L.SKA_PATH_TC_READOUT_FWD:
+            names.append("k_readout")
         if self.wl["bwd"]:
             full = bool(p & L.SKA_PATH_TC_READOUT_BWD)
             names += (["k_dw"] if full else []) + ["k_bwd_chunk", "k_scan_bwd", "k_bwd_tok"]
@@ -429,6 +431,8 @@ def per_kernel_ms(run, n, flush):
     names = run.kernel_names()
     fused = bool(run.path & L.SKA_PATH_FUSED_SCAN)
     fwd_pairs = [(0, 2), (2, 3)] if fused else [(0, 1), (1, 2), (2, 3)]
+    if "k_readout" in names:
+        fwd_pairs.append((3, 9))
     bwd_pairs = []
     if run.wl["bwd"]:
         bwd_pairs = ([(4, 5)] if "k_dw" in names else []) + [(5, 6), (6, 7), (7, 8)]
@@ -437,7 +441,7 @@ def per_kernel_ms(run, n, flush):
         for _ in range(n):
             flush.zero_()
             run.step()
-            kev[8 if run.wl["bwd"] else 3].synchronize()
+            kev[8 if run.wl["bwd"] else 9].synchronize()
             spans = [kev[a].elapsed_time(kev[b]) for a, b in fwd_pairs + bwd_pairs]
             for k, ms in zip(names, spans):
                 acc[k].append(ms)

@@ -129,13 +129,14 @@ int ska_bwd(const SkaShape* shape, int io_dtype,
 /* Profiling hook (process-wide, not thread-safe; no counterpart in the
  * reference, which has no per-kernel timing).  With `events` non-NULL and
  * count >= SKA_PROFILE_EVENTS, every later ska_fwd records events[0] on its
- * stream before its first kernel and events[i] after its i-th kernel
- * (i = 1..3: statistics, scan, chunk operators); ska_bwd records events[4]
- * before its first kernel and events[5..8] after the readout-gradient kernel
- * (recorded back to back when that kernel does not run), the chunk operators,
- * the scan and the token kernel.  The handles are cudaEvent_t values created
+ * stream before its first kernel, events[1..3] after the statistics, the scan
+ * and the chunk-operator kernels, and events[9] after the tensor-core readout
+ * kernel; ska_bwd records events[4] before its first kernel and events[5..8]
+ * after the readout-gradient kernel, the chunk operators, the scan and the
+ * token kernel.  An event whose kernel does not run for the layout is recorded
+ * right after the previous one.  The handles are cudaEvent_t values created
  * by the caller.  NULL disables recording. */
-#define SKA_PROFILE_EVENTS 9
+#define SKA_PROFILE_EVENTS 10
 int ska_set_profile_events(void* const* events, int count);
 
 /* Which kernels ska_fwd / ska_bwd launch for these arguments (no counterpart in
@@ -158,12 +159,17 @@ int ska_set_profile_events(void* const* events, int count);
  *                        kernel
  *   SKA_PATH_FUSED_SCAN  the forward statistics and their prefix scan in one
  *                        kernel, one CTA per (batch, head) series (TC_STATS,
- *                        r = 32, P <= 64 and B * H >= 64); otherwise two */
+ *                        r = 32, P <= 64 and B * H >= 64); otherwise two
+ *   SKA_PATH_TC_READOUT_FWD  the forward readout y = (W / m) zq as its own TMA +
+ *                        tcgen05 kernel (bf16, WARP_CHUNK, r % 16 == 0,
+ *                        P % 16 == 0, chunk_size <= 128, y laid out like v);
+ *                        otherwise inside the chunk-operator kernel */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
 #define SKA_PATH_TC_READOUT_BWD 8
 #define SKA_PATH_FUSED_SCAN 16
+#define SKA_PATH_TC_READOUT_FWD 32
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Bounded waits of the tensor-core kernels (no counterpart in the reference,
@@ -177,15 +183,16 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
  * never synchronise); ska_check_status reads it afterwards.
  *
  * Status entries: int32 [B][H][C] (chunk c of head h of batch b at
- * (b * H + h) * C + c), one array in `saved` (forward statistics kernels:
- * 0 ok, 1 copy wait expired, 2 product wait expired) and one in `scratch`
- * (backward: bits 0-1 the readout-gradient kernel, bits 2-3 the token kernel,
- * each coded as in the forward).  Layouts without tensor-core kernels write 0.
+ * (b * H + h) * C + c), one array in `saved` (forward: bits 0-1 the statistics
+ * kernel, bits 2-3 the readout kernel; each 0 ok, 1 copy wait expired,
+ * 2 product wait expired) and one in `scratch` (backward: bits 0-1 the
+ * readout-gradient kernel, bits 2-3 the token kernel, coded the same way).
+ * Layouts without tensor-core kernels write 0.
  *
  * ska_check_status synchronises `stream`, then scans the forward entries of
  * `saved` and the backward entries of `scratch` (either may be NULL to skip it).
  * Returns SKA_OK when every entry is 0, SKA_ERR_TIMEOUT at the first non-zero one
- * with *first_bad = its flat chunk index and *code = the forward entry (1, 2) or
+ * with *first_bad = its flat chunk index and *code = the forward entry's bits or
  * SKA_STATUS_BWD_BASE + the backward entry's bits; other negative codes for bad
  * arguments.  A diagnostic call: it copies the entries to host memory.
  *

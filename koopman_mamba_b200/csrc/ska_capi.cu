@@ -28,6 +28,8 @@ bool stats_tc_ok(const Dims& d, const In& z, const In& v);
 bool stats_scan_tc_ok(const Dims& d, const In& z, const In& v);
 }
 template <typename IO>
+bool fwd_tc_readout(const Dims& d, const In& zq, const Out& y);
+template <typename IO>
 void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
                   const Out& dzq, const Out& dv, bool* full, bool* tok);
 }  // namespace ska
@@ -146,6 +148,10 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_scan_tc_ok(d, iz, iv)) mask |= SKA_PATH_FUSED_SCAN;
   if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
+  if (io_dtype == SKA_DTYPE_BF16) {   // y assumed laid out like v
+    const ska::Out yv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
+    if (ska::fwd_tc_readout<__nv_bfloat16>(d, iz, yv)) mask |= SKA_PATH_TC_READOUT_FWD;
+  }
   if (io_dtype == SKA_DTYPE_BF16) {   // gradients and zq, dy assumed laid out like z and v
     const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
     bool full = false, tok = false;

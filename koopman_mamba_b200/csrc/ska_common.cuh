@@ -194,7 +194,7 @@ __device__ __forceinline__ int unpack_t(unsigned long long k) {
 
 // Caller-provided timing events (ska_set_profile_events); nullptr = off.
 struct ProfileEvents {
-  cudaEvent_t ev[9];
+  cudaEvent_t ev[10];
   bool on;
 };
 ProfileEvents* profile_events();

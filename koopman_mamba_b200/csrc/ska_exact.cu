@@ -952,6 +952,9 @@ cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In&
                               cudaStream_t st);
 bool dw_tc_ok(const Dims& d, const In& zq, const In& dy);
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st);
+bool readout_tc_ok(const Dims& d, const In& zq, const Out& y);
+cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, int* status,
+                              cudaStream_t st);
 }  // namespace tc
 cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                                const float* invs, const float* ops, const float* dwraw, float* dstats,
@@ -991,6 +994,18 @@ bool tc_stats_path(const Dims& d, const In& z, const In& v) {
 template bool tc_stats_path<float>(const Dims&, const In&, const In&);
 template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 
+// bf16 tensors on the warp path whose zq and y the tensor-core readout can take
+template <typename IO>
+bool fwd_tc_readout(const Dims& d, const In& zq, const Out& y) {
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
+    return warp_path_ok(d) && tc::readout_tc_ok(d, zq, y);
+  } else {
+    return false;
+  }
+}
+template bool fwd_tc_readout<float>(const Dims&, const In&, const Out&);
+template bool fwd_tc_readout<__nv_bfloat16>(const Dims&, const In&, const Out&);
+
 template <typename IO>
 cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
                        const SavedLayout& L, char* saved, cudaStream_t st) {
@@ -1020,17 +1035,27 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   prof_record(1, st);
   if (!fused) k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   prof_record(2, st);
+  bool tc_read = false;   // readout as its own tensor-core kernel
   if (warp_path_ok(d)) {
     // bf16 forwards keep the chunk operators and W / m for the tensor-core backward
+    // and readout
     const bool keep = std::is_same<IO, __nv_bfloat16>::value;
     float* ops = keep ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
     unsigned char* wm = keep ? reinterpret_cast<unsigned char*>(saved + L.wm) : nullptr;
-    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, y, stats, cmax, invs, flags, ops, wm, st)) != cudaSuccess)
+    tc_read = fwd_tc_readout<IO>(d, zq, y);
+    const Out ychunk = tc_read ? Out{nullptr, 0, 0, 0} : y;
+    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, ychunk, stats, cmax, invs, flags, ops, wm, st)) != cudaSuccess)
       return e;
   } else {
     k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
   }
   prof_record(3, st);
+  if (tc_read) {
+    const unsigned char* wm = reinterpret_cast<const unsigned char*>(saved + L.wm);
+    if ((e = tc::launch_readout_tc(d, zq, wm, y, reinterpret_cast<int*>(saved + L.status), st)) != cudaSuccess)
+      return e;
+  }
+  prof_record(9, st);
   return cudaGetLastError();
 }
 

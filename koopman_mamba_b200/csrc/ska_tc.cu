@@ -1233,6 +1233,154 @@ cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, i
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// k_readout_tc: the forward readout  y_t = (W / m) zq_t  of one chunk per CTA
+// (KLF/koopman_lm/ska.py:179-186: y = B_v L A^K L^{-1} qn, which is (W / m) zq with
+// W = Cn Li^T A^K Li kept by the chunk-operator kernel).  With tokens as M:
+//   Y (CS x P) = ZQ (CS x r) . (W / m)^T
+// A is the TMA token tile of zq read K-major (features as K); B is W / m as the
+// bf16 hi and lo planes the chunk-operator kernel wrote, whose 16-byte rows (8
+// consecutive j for one p) are exactly a K-major B operand with N = P, K = r.  The
+// bf16 tokens are exact, W / m = hi + lo to ~2^-17, so two products accumulated
+// in fp32 in TMEM give y to fp32 level.  Waits are bounded as in the other kernels;
+// an expired wait ORs its code into bits 2-3 of the chunk's forward status and
+// writes NaN into the chunk's y.
+// ---------------------------------------------------------------------------
+constexpr int kReadThreads = 128;
+
+struct ReadGeom {
+  uint32_t grp;        // bytes of one 8-feature group of the zq tile: CS x 16 B
+  uint32_t o_w;        // offset of the W / m planes (after the tile and the M - CS spare rows)
+  uint32_t wbytes;     // P * r * 4
+  uint32_t ncols;      // TMEM columns: P, rounded up to a power of two >= 32
+  int mrows;           // MMA rows: 64 for CS <= 64, else 128
+  size_t smem;
+};
+
+__host__ __device__ inline ReadGeom read_geom(int r, int P, int CS) {
+  ReadGeom g{};
+  g.mrows = CS <= 64 ? 64 : 128;
+  g.grp = (uint32_t)CS * 16u;
+  const uint32_t tile = (uint32_t)(r / 8) * g.grp + (uint32_t)(g.mrows - CS) * 16u;
+  g.o_w = up128(tile);
+  g.wbytes = (uint32_t)(P * r) * 4u;
+  uint32_t c = 32;
+  while (c < (uint32_t)P) c <<= 1;
+  g.ncols = c;
+  g.smem = (size_t)g.o_w + g.wbytes + 128;
+  return g;
+}
+
+__global__ void __launch_bounds__(kReadThreads) k_readout_tc(const __grid_constant__ CUtensorMap mzq, Dims d,
+                                                             ReadGeom g, const unsigned char* __restrict__ wm,
+                                                             Out y, int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_slot;
+  unsigned char* base = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long q = blockIdx.x;                      // (b, h, c), c fastest
+  const int c = (int)(q % d.C);
+  const long long bh = q / d.C;
+  const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T;
+  const int t0 = c * CS;
+  unsigned char* tile = base;
+  unsigned char* bw = base + g.o_w;
+
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    mbar_fence_init();
+    tma_prefetch_map(&mzq);
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, g.ncols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {   // one lane issues; the rest of the warp waits converged
+    if (lane == 0) {
+      mbar_expect_tx(&bar_load, (uint32_t)r * (uint32_t)CS * 2u + g.wbytes);
+      for (int k = 0; k < r / 8; ++k) tma_load_4d(tile + (size_t)k * g.grp, &mzq, &bar_load, 8 * k, h, t0, b);
+      bulk_load(bw, wm + (size_t)q * g.wbytes, g.wbytes, &bar_load);
+    }
+    __syncwarp();
+  }
+  int st = 0;
+  if (!__syncthreads_and(mbar_wait(&bar_load, 0, d.wlim))) {
+    st = 1;
+    mbar_wait(&bar_load, 0, kWaitLimit);               // let copies in flight land
+  }
+  if (warp == 0) {
+    if (st == 0 && lane == 0) {
+      fence_after_sync();
+      const uint32_t a0 = smem_u32(tile), b0 = smem_u32(bw);
+      const uint32_t id = idesc_bf16(g.mrows, P, false, false);
+      const uint32_t lbo_b = (uint32_t)P * 16u;         // next 8 j of W / m
+      for (int part = 0; part < 2; ++part)
+        for (int ks = 0; ks < r / 16; ++ks)
+          mma_bf16(tbase, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u),
+                   sdesc(b0 + (uint32_t)part * (uint32_t)(P * r * 2) + 2u * lbo_b * ks, lbo_b, 128u), id,
+                   part > 0 || ks > 0);
+      mma_commit(&bar_mma);
+    }
+    __syncwarp();
+  }
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim))) {
+    st = 2;
+    mbar_wait(&bar_mma, 0, kWaitLimit);                // let the products finish
+  }
+  __syncthreads();
+  fence_after_sync();
+  // token row m in TMEM lane 32 warp + lane (M = 128) or 32 warp + m % 16 (M = 64, lanes 0-15)
+  const int m = g.mrows == 64 ? 16 * warp + lane : 32 * warp + lane, t = t0 + m;
+  const bool live = (g.mrows == 128 || lane < 16) && m < CS && t < T;
+  const float nan = __int_as_float(0x7fc00000);
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  for (int j0 = 0; j0 < P; j0 += 16) {
+    float x[16];
+    tmem_ld16(tbase + lane_base + (uint32_t)j0, x);
+    if (live) {
+      if (st) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = nan;
+      }
+      store_bf16x16(tok_ptr(y, b, t, h) + j0, x);
+    }
+  }
+  if (tid == 0 && st) status[q] |= st << 2;            // bits 2-3 (bits 0-1: the statistics kernel)
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, g.ncols);
+  }
+}
+
+bool readout_tc_ok(const Dims& d, const In& zq, const Out& y) {
+  if (d.r % 16 != 0 || d.r > 64 || d.P % 16 != 0 || d.P > 128 || d.CS % 16 != 0 || d.CS > 128) return false;
+  const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(zq.p) || !al(y.p)) return false;
+  if (!stride_ok(zq.st, d.T) || !stride_ok(zq.sh, d.H) || !stride_ok(zq.sb, d.B)) return false;
+  const auto s8 = [](long long s, long long extent) { return extent == 1 || s % 8 == 0; };
+  return s8(y.st, d.T) && s8(y.sh, d.H) && s8(y.sb, d.B) && read_geom(d.r, d.P, d.CS).smem <= 227u * 1024u - 64u;
+}
+
+cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, int* status,
+                              cudaStream_t st) {
+  CUtensorMap mq;
+  const ReadGeom g = read_geom(d.r, d.P, d.CS);
+  if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS)) return cudaErrorInvalidValue;
+  const size_t smem = tmem_safe_smem(g.ncols, kReadThreads, g.smem);
+  cudaError_t e = cudaFuncSetAttribute(k_readout_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const long long n = (long long)d.B * d.H * d.C;
+  k_readout_tc<<<(unsigned)n, kReadThreads, smem, st>>>(mq, d, g, wm, y, status);
+  return cudaGetLastError();
+}
+
 bool stats_scan_tc_ok(const Dims& d, const In& z, const In& v) {
   // r = 32 and 2r + P <= 128: one 128-row product, one 32-float record row per thread
   return (long long)d.B * d.H >= 64 && d.r == 32 && 2 * d.r + d.P <= 128 && stats_tc_ok(d, z, v);

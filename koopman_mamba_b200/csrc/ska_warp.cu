@@ -379,6 +379,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
 #pragma unroll
     for (int pb = 0; pb < NPB; ++pb) store_wm_block(wq, TW + pb * kTile, pb, P, r, lane);
   }
+  if (!y.p) return;   // the readout runs as its own tensor-core kernel (k_readout_tc)
 
   // readout y_t = (W/m) zq_t, 32 tokens per tile: Y block pb = Q (W/m)[pb rows]^T.
   // Two token blocks at a time (T0, T1; Li is dead), both blocks' loads together.

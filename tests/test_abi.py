@@ -96,6 +96,7 @@ def test_fwd_validation_before_any_cuda_call(built_lib):
 
 
 TC = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD
+RD = _lib.SKA_PATH_TC_READOUT_FWD
 
 
 def _contig(base, B, T, H, D):
@@ -105,9 +106,9 @@ def _contig(base, B, T, H, D):
 @pytest.mark.parametrize("kw,dtype,zt,want", [
     # config 2 in bf16, contiguous: every tensor-core kernel + warp chunk operators,
     # statistics and scan fused (96 series)
-    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN),
+    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD),
     # too few series to occupy the SMs one CTA per series: statistics and scan apart
-    (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD),
+    (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
     # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
     # r = 64 (config 3): tensor-core token kernels, one CTA per chunk operator (which
@@ -117,13 +118,13 @@ def _contig(base, B, T, H, D):
     (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
     # P % 16 != 0: tensor-core statistics only
     (dict(P=40), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_FUSED_SCAN),
-    # r = 16: CUDA-core token kernels
-    (dict(r=16), 1, None, _lib.SKA_PATH_WARP_CHUNK),
+    # r = 16: CUDA-core token kernels, tensor-core forward readout
+    (dict(r=16), 1, None, _lib.SKA_PATH_WARP_CHUNK | RD),
     # token stride not a multiple of 16 bytes: CUDA-core token kernels
     (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
     # decay strategy shares the token kernels and the fused statistics + scan
     (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None,
-     TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN),
+     TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD),
 ])
 def test_kernel_path_selection(built_lib, kw, dtype, zt, want):
     s = _shape(**kw)
