@@ -161,15 +161,21 @@ int ska_set_profile_events(void* const* events, int count);
  *                        kernel, one CTA per (batch, head) series (TC_STATS,
  *                        r = 32, P <= 64 and B * H >= 64); otherwise two
  *   SKA_PATH_TC_READOUT_FWD  the forward readout y = (W / m) zq as its own TMA +
- *                        tcgen05 kernel (bf16, WARP_CHUNK, r % 16 == 0,
+ *                        tcgen05 kernel (bf16, WARP_CHUNK or QUAD_CHUNK, r % 16 == 0,
  *                        P % 16 == 0, chunk_size <= 128, y laid out like v);
- *                        otherwise inside the chunk-operator kernel */
+ *                        otherwise inside the chunk-operator kernel
+ *   SKA_PATH_QUAD_CHUNK  forward chunk operators for 32 < r <= 64 (r % 8 == 0,
+ *                        P <= 64, bf16 with a TC_READOUT_FWD layout) on the
+ *                        four-warp kernel (one CTA per chunk, blocked
+ *                        Cholesky); otherwise, for r > 32, on the one-CTA
+ *                        CUDA-core kernel */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
 #define SKA_PATH_TC_READOUT_BWD 8
 #define SKA_PATH_FUSED_SCAN 16
 #define SKA_PATH_TC_READOUT_FWD 32
+#define SKA_PATH_QUAD_CHUNK 64
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Bounded waits of the tensor-core kernels (no counterpart in the reference,

@@ -21,6 +21,7 @@ size_t smem_fwd_chunk(const Dims&);
 size_t smem_bwd_chunk(const Dims&);
 size_t smem_bwd_tok(const Dims&);
 bool warp_path_ok(const Dims&);
+bool quad_path_ok(const Dims&);
 size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
 namespace tc {
@@ -148,6 +149,10 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_tc_ok(d, iz, iv)) mask |= SKA_PATH_TC_STATS;
   if (io_dtype == SKA_DTYPE_BF16 && ska::tc::stats_scan_tc_ok(d, iz, iv)) mask |= SKA_PATH_FUSED_SCAN;
   if (ska::warp_path_ok(d)) mask |= SKA_PATH_WARP_CHUNK;
+  if (io_dtype == SKA_DTYPE_BF16 && ska::quad_path_ok(d)) {   // zq and y assumed laid out like z and v
+    const ska::Out yv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
+    if (ska::fwd_tc_readout<__nv_bfloat16>(d, iz, yv)) mask |= SKA_PATH_QUAD_CHUNK;
+  }
   if (io_dtype == SKA_DTYPE_BF16) {   // y assumed laid out like v
     const ska::Out yv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
     if (ska::fwd_tc_readout<__nv_bfloat16>(d, iz, yv)) mask |= SKA_PATH_TC_READOUT_FWD;

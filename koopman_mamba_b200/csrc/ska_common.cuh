@@ -115,7 +115,7 @@ struct SavedLayout {
                     //   Li = L^{-1}, A = gamma' A0 / max(sigma, 1), A^K, U = A^K Li,
                     //   V = Li^T U, S = Li^T Li (bf16 I/O forwards write them)
   size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the
-                    //   tensor-core operand of the readout products (r <= 32 only)
+                    //   tensor-core operand of the readout products
   size_t total;
 };
 
@@ -144,7 +144,7 @@ __host__ __device__ inline SavedLayout saved_layout(long long B, long long H, lo
   L.flags = off; off = align256(off + n * sizeof(int));
   L.status = off; off = align256(off + n * sizeof(int));
   L.ops = off;   off = align256(off + (warp_ops ? n * kNumOps * kOpFloats * sizeof(float) : 0));
-  L.wm = off;    off = align256(off + (warp_ops ? n * (size_t)P * r * 4 : 0));
+  L.wm = off;    off = align256(off + (r <= 64 ? n * (size_t)P * r * 4 : 0));
   L.total = off;
   return L;
 }

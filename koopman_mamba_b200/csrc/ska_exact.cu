@@ -994,11 +994,16 @@ bool tc_stats_path(const Dims& d, const In& z, const In& v) {
 template bool tc_stats_path<float>(const Dims&, const In&, const In&);
 template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 
-// bf16 tensors on the warp path whose zq and y the tensor-core readout can take
+bool quad_path_ok(const Dims& d);
+cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               float* invs, int* flags, unsigned char* wm, cudaStream_t st);
+
+// bf16 tensors on the warp or four-warp path whose zq and y the tensor-core readout
+// can take
 template <typename IO>
 bool fwd_tc_readout(const Dims& d, const In& zq, const Out& y) {
   if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
-    return warp_path_ok(d) && tc::readout_tc_ok(d, zq, y);
+    return (warp_path_ok(d) || quad_path_ok(d)) && tc::readout_tc_ok(d, zq, y);
   } else {
     return false;
   }
@@ -1045,6 +1050,11 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
     tc_read = fwd_tc_readout<IO>(d, zq, y);
     const Out ychunk = tc_read ? Out{nullptr, 0, 0, 0} : y;
     if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, ychunk, stats, cmax, invs, flags, ops, wm, st)) != cudaSuccess)
+      return e;
+  } else if (fwd_tc_readout<IO>(d, zq, y)) {   // 32 < r <= 64: four-warp operators, tensor-core readout
+    tc_read = true;
+    if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, reinterpret_cast<unsigned char*>(saved + L.wm),
+                                st)) != cudaSuccess)
       return e;
   } else {
     k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);

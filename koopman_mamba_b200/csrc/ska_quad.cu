@@ -1,0 +1,371 @@
+// ska_quad.cu -- chunk-operator forward for ranks 32 < r <= 64: one CTA of four
+// warps per (batch, head, chunk).
+//
+// A 64 x 64 matrix is four of the warp kernels' swizzled 32 x 32 fp32 tiles,
+// stored column-block major: block (bi, bj) (rows 32 bi.., columns 32 bj..) at
+// tile 2 bj + bi.  Then a column block is two consecutive tiles, which the warp
+// tile products (wmmp) read as one "tall" operand of 64 rows, and the two tiles of
+// a row block are 2 tiles apart.  A P x 64 matrix (P <= 64) is NPB row blocks by
+// two column blocks, block (pb, bj) at tile bj * NPB + pb.  Rows and columns past
+// r hold the usual padding (identity on the Gram factor, zero elsewhere).
+//
+// Per chunk (same algebra as the warp kernels, KLF/koopman_lm/ska.py:136-186):
+//   Gn = sym(G) / m^2 + ridge I        blocked Cholesky, by warp 0:
+//     L11 = chol(Gn11), Li11 = L11^{-1}             (chol_inv32)
+//     L21 = Gn21 Li11^T,  Gn22' = Gn22 - L21 L21^T
+//     L22 = chol(Gn22'), Li22 = L22^{-1}            (chol_inv32)
+//     Li21 = -Li22 L21 Li11
+//   (a non-positive pivot in either block refactors the whole Gram matrix with
+//    1e-4 added to its diagonal, ska.py:140-145: the blocked pivots are those of
+//    the unblocked factorisation)
+//   S = Li^T Li, A0 = Mn S                       one output block per warp
+//   sigma: 6 power iterations (ska.py:41-58)     warps 0 and 1, a row per lane
+//   A = clamp(gamma, 1, 1.5) / max(sigma, 1) A0,  A^K,  U = A^K Li,  V = Li^T U
+//   W / m = C V / m^2                            one output block per warp
+// and writes W / m as the bf16 hi / lo planes that k_readout_tc multiplies into
+// the tokens (the readout is not done here).
+#include "ska_warp.cuh"
+
+namespace ska {
+namespace quad {
+
+using namespace wpc;
+
+constexpr int kThreads4 = 128;
+constexpr int kTile = 1024;
+constexpr int kRegion = 4 * kTile;   // one 64 x 64 matrix
+
+__device__ __forceinline__ float* blk(float* M, int bi, int bj) { return M + ((bj << 1) | bi) * kTile; }
+
+// tile T <- rows [0, nrows) x columns [0, ncols) of a global matrix with row stride
+// ld (floats), zero elsewhere; by cp.async (the lane's next commit group) when the
+// source rows are 16-byte aligned pieces, else by plain loads (then synchronise
+// the warp before reading)
+__device__ __forceinline__ void fetch_block(float* T, const float* src, int ld, int nrows, int ncols, int lane) {
+  const bool vec = (ld & 3) == 0 && (ncols & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  if (vec) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int f = 32 * k + lane, row = f >> 3, q = f & 7;
+      const bool ok = row < nrows && 4 * q < ncols;
+      const float* s = src + (ok ? (size_t)row * ld + 4 * q : 0);
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(T + row * 32 + ((q ^ (row & 7)) << 2)));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(s), "r"(ok ? 16 : 0) : "memory");
+    }
+  } else {
+    float v[32];
+    const bool rv = lane < nrows;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rv && j < ncols) ? __ldg(src + (size_t)lane * ld + j) : 0.f;
+    st_row(T, lane, v);
+  }
+}
+
+// the 64 x 64 record block starting at `src` (row stride r) -> region M
+__device__ __forceinline__ void fetch_square(float* M, const float* src, int r, int lane) {
+#pragma unroll
+  for (int bj = 0; bj < 2; ++bj)
+#pragma unroll
+    for (int bi = 0; bi < 2; ++bi)
+      fetch_block(blk(M, bi, bj), src + (size_t)(32 * bi) * r + 32 * bj, r, r - 32 * bi, r - 32 * bj, lane);
+}
+
+// Gn row blocks for the blocked Cholesky (warp 0).  attempt: jitter or not.
+// Returns false (uniformly) when a pivot is not positive.  On success Li holds the
+// inverse factor (block (0, 1) zero).  T0..T3 are scratch tiles.
+__device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, float* T1, float* T2, float* T3,
+                               float im2, float jit, int lane) {
+  const int r = d.r;
+  float g[32], x[32], a[32], b[32];
+  // block 11
+  ld_row(a, blk(G, 0, 0), lane);
+  ld_col<32>(b, blk(G, 0, 0), lane);
+  build_gram_row(g, a, b, lane, 32, im2, d.ridge, jit);
+  if (!chol_inv32(g, x, lane)) return false;
+  st_col<32>(blk(Li, 0, 0), lane, x);                            // Li11 rows
+  // Gn21 (row 32 + lane, column j): (G21 + G12^T) / 2 / m^2
+  ld_row(a, blk(G, 1, 0), lane);
+  ld_col<32>(b, blk(G, 0, 1), lane);
+  const bool row_ok = 32 + lane < r;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) a[j] = row_ok ? 0.5f * (a[j] * im2 + b[j] * im2) : 0.f;
+  st_row(T0, lane, a);
+  // Gn22 (with identity padding past r)
+  ld_row(a, blk(G, 1, 1), lane);
+  ld_col<32>(b, blk(G, 1, 1), lane);
+  build_gram_row(g, a, b, lane, r - 32, im2, d.ridge, jit);
+  st_row(T2, lane, g);
+  __syncwarp();
+  wmmp<false, 32, 32, false, true, false>(T1, T0, kTile, blk(Li, 0, 0), 1.f);   // L21 = Gn21 Li11^T
+  __syncwarp();
+  wmmp<false, 32, 32, false, true, true>(T2, T1, kTile, T1, -1.f);              // Gn22 - L21 L21^T
+  __syncwarp();
+  ld_row(g, T2, lane);
+  if (!chol_inv32(g, x, lane)) return false;
+  st_col<32>(blk(Li, 1, 1), lane, x);                            // Li22 rows
+  __syncwarp();
+  wmmp<false, 32, 32, false, false, false>(T3, T1, kTile, blk(Li, 0, 0), 1.f);  // L21 Li11
+  __syncwarp();
+  wmmp<false, 32, 32, false, false, false>(blk(Li, 1, 0), blk(Li, 1, 1), kTile, T3, -1.f);   // Li21
+  zero(a);
+  st_row(blk(Li, 0, 1), lane, a);
+  __syncwarp();
+  return true;
+}
+
+// A0 = Mn S etc.: out block (bi, bj) = alpha X(bi, :) Y(:, bj) for 64 x 64 X, Y
+__device__ __forceinline__ void mul_block(float* out, float* X, float* Y, int bi, int bj, float alpha) {
+  wmmp<false, 32, 64, false, false, false>(blk(out, bi, bj), blk(X, bi, 0), 2 * kTile, Y + bj * 2 * kTile, alpha);
+}
+
+// sigma_max estimate of ska.py:41-58 for the 64 x 64 matrix A (region), by warps
+// 0 and 1 (lane: row 32 w + lane, held in registers); the same arithmetic as
+// power_sigma32: 6 iterations from v = 1/sqrt(r), x / max(||x||, 1e-8) taken as
+// x * min(rsqrt(||x||^2), 1e8).  vsh: 64 floats; part: 2 x 64 floats; red: 2 floats.
+// Named barrier 1 (64 threads).
+__device__ __forceinline__ void bar64() { asm volatile("bar.sync 1, 64;" ::: "memory"); }
+
+__device__ float power_sigma64(float* A, float* vsh, float* part, float* red, int r, int w, int lane) {
+  float a0[32], a1[32];
+  ld_row(a0, blk(A, w, 0), lane);
+  ld_row(a1, blk(A, w, 1), lane);
+  if (w == 0) {
+    const float v0 = rsqrtf((float)r);
+    vsh[lane] = lane < r ? v0 : 0.f;
+    vsh[32 + lane] = 32 + lane < r ? v0 : 0.f;
+  }
+  bar64();
+  float u = 0.f;
+#pragma unroll 1
+  for (int it = 0; it <= kPowerIters; ++it) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      s0 = fmaf(a0[j], vsh[j], s0);
+      s1 = fmaf(a0[j + 1], vsh[j + 1], s1);
+      s2 = fmaf(a1[j], vsh[32 + j], s2);
+      s3 = fmaf(a1[j + 1], vsh[33 + j], s3);
+    }
+    u = (s0 + s1) + (s2 + s3);
+    const float uu = warp_sum32(u * u);
+    if (lane == 0) red[w] = uu;
+    bar64();
+    const float nu = red[0] + red[1];
+    if (it == kPowerIters) return sqrtf(nu);
+    u *= fminf(rsqrtf(nu), 1.f / kPowerEps);
+    float t[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t[i] = u * a0[i];
+    const float p0 = reduce_scatter32(t, lane);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) t[i] = u * a1[i];
+    const float p1 = reduce_scatter32(t, lane);
+    part[w * 64 + lane] = p0;
+    part[w * 64 + 32 + lane] = p1;
+    bar64();
+    const float w0 = part[lane] + part[64 + lane], w1 = part[32 + lane] + part[96 + lane];
+    const float nw = warp_sum32(w0 * w0 + w1 * w1);
+    const float sc = fminf(rsqrtf(nw), 1.f / kPowerEps);
+    bar64();                                   // every lane has read red and part
+    if (w == 0) {
+      vsh[lane] = w0 * sc;
+      vsh[32 + lane] = w1 * sc;
+    }
+    bar64();
+  }
+  return 0.f;   // not reached
+}
+
+template <int NPB>
+__global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const float* __restrict__ gamma_p,
+                                                              const float* __restrict__ stats,
+                                                              const unsigned long long* __restrict__ cmax,
+                                                              float* __restrict__ invs_out,
+                                                              int* __restrict__ flags_out,
+                                                              unsigned char* __restrict__ wm_out) {
+  extern __shared__ float4 sm4[];
+  float* R0 = reinterpret_cast<float*>(sm4);   // G, then S, then A^K / U / V / spare
+  float* RLi = R0 + kRegion;                   // Li, then W / m
+  float* RA = RLi + kRegion;                   // Cholesky scratch, then A0 / A
+  float* RK = RA + kRegion;                    // Mn, then A^K
+  __shared__ float vsh[64], part[128], red[2];
+  __shared__ float s_sigma;
+  __shared__ int s_flag;
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const long long q = blockIdx.x;
+  const ChunkId id = chunk_id(d, q);
+  const int r = d.r, P = d.P;
+  const float* rec = stats + q * d.SW;
+
+  if (w == 0) fetch_square(R0, rec, r, lane);              // G
+  if (w == 1) fetch_square(RK, rec + r * r, r, lane);      // M
+  cp_async_commit();
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
+
+  // ---- blocked Cholesky + inverse (warp 0), jitter retry ----
+  if (w == 0) {
+    cp_async_wait<0>();
+    __syncwarp();
+    int flag = 0;
+    if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, 0.f, lane)) {
+      flag = 1;
+      if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, kJitter,
+                          lane))
+        flag |= 2;
+    }
+    if (lane == 0) s_flag = flag;
+  }
+  __syncthreads();
+
+  // ---- S = Li^T Li (block (0, 1) of Li is zero) ----
+  {
+    const int bi = w & 1, bj = w >> 1;
+    float* out = blk(R0, bi, bj);
+    if (bi == 0 && bj == 0)
+      wmmp<false, 32, 64, true, false, false>(out, RLi, kTile, RLi, 1.f);
+    else if (bi == 1 && bj == 0)
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 0), 1.f);
+    else if (bi == 0)
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 0), kTile, blk(RLi, 1, 1), 1.f);
+    else
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 1), 1.f);
+  }
+  cp_async_wait<0>();                                      // M (warp 1's copies)
+  __syncthreads();
+  // ---- A0 = Mn S ----
+  mul_block(RA, RK, R0, w & 1, w >> 1, im2);
+  __syncthreads();
+  // ---- spectral norm (warps 0, 1) ----
+  if (w < 2) {
+    const float sg = power_sigma64(RA, vsh, part, red, r, w, lane);
+    if (tid == 0) {
+      s_sigma = sg;
+      const float invs = 1.f / fmaxf(sg, 1.f);
+      invs_out[q] = invs;
+      flags_out[q] = s_flag;
+    }
+  }
+  __syncthreads();
+  const float kk = gs * (1.f / fmaxf(s_sigma, 1.f));     // as the backward forms it from invs
+  {
+    float t[32];
+    float* T = blk(RA, w & 1, w >> 1);
+    ld_row(t, T, lane);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] *= kk;
+    st_row(T, lane, t);                                    // A
+  }
+  __syncthreads();
+  // ---- A^K: K = 0 identity, K = 1 A itself, else ping-pong RK / R0 ----
+  float* AK = RA;
+  if (d.K == 0) {
+    float t[32];
+    const int bi = w & 1, bj = w >> 1;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] = (bi == bj && j == lane) ? 1.f : 0.f;
+    st_row(blk(RK, bi, bj), lane, t);
+    AK = RK;
+  } else {
+    for (int s = 1; s < d.K; ++s) {
+      float* out = (AK == RK) ? R0 : RK;
+      mul_block(out, AK, RA, w & 1, w >> 1, 1.f);
+      __syncthreads();
+      AK = out;
+    }
+  }
+  __syncthreads();
+  // regions now: RLi = Li, AK in one of {RA, RK, R0}; A (RA) dead unless AK is RA
+  float* cand[3] = {R0, RK, RA};
+  float* RU = nullptr;
+  float* RC = nullptr;
+  for (int i = 0; i < 3; ++i) {
+    if (cand[i] == AK) continue;
+    if (!RU) RU = cand[i];
+    else if (!RC) RC = cand[i];
+  }
+  // C rows (P x r, row stride r) into RC, overlapping the U product
+  if (w == 2) {
+#pragma unroll
+    for (int bj = 0; bj < 2; ++bj)
+#pragma unroll
+      for (int pb = 0; pb < NPB; ++pb)
+        fetch_block(RC + (bj * NPB + pb) * kTile, rec + 2 * r * r + (size_t)(32 * pb) * r + 32 * bj, r, P - 32 * pb,
+                    r - 32 * bj, lane);
+    cp_async_commit();
+  }
+  // ---- U = A^K Li (Li block (0, 1) is zero) ----
+  {
+    const int bi = w & 1, bj = w >> 1;
+    if (bj == 0)
+      wmmp<false, 32, 64, false, false, false>(blk(RU, bi, 0), blk(AK, bi, 0), 2 * kTile, RLi, 1.f);
+    else
+      wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), 1.f);
+  }
+  __syncthreads();
+  // ---- V = Li^T U (into the A^K region, dead now) ----
+  float* RV = AK;
+  {
+    const int bi = w & 1, bj = w >> 1;
+    if (bi == 0)
+      wmmp<false, 32, 64, true, false, false>(blk(RV, 0, bj), RLi, kTile, RU + bj * 2 * kTile, 1.f);
+    else
+      wmmp<false, 32, 32, true, false, false>(blk(RV, 1, bj), blk(RLi, 1, 1), kTile, blk(RU, 1, bj), 1.f);
+  }
+  if (w == 2) cp_async_wait<0>();                          // C
+  __syncthreads();
+  // ---- W / m = C V / m^2 (into the Li region, dead now), then its bf16 planes ----
+  float* RW = RLi;
+  for (int t = w; t < 2 * NPB; t += 4) {
+    const int pb = t % NPB, bj = t / NPB;
+    float* out = RW + (bj * NPB + pb) * kTile;
+    wmmp<false, 32, 64, false, false, false>(out, RC + pb * kTile, NPB * kTile, RV + bj * 2 * kTile, im2);
+    __syncwarp();
+    float u[32];
+    ld_row(u, out, lane);
+    const int p = 32 * pb + lane;
+    if (p < P && wm_out) {
+      unsigned char* wq = wm_out + (size_t)q * P * r * 4;
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        const int ng = 4 * bj + g4;
+        if (8 * ng >= r) break;
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = u[8 * g4 + e];
+        uint4 hi, lo;
+        split_bf16x8(x, hi, lo);
+        *reinterpret_cast<uint4*>(wq + (size_t)ng * P * 16 + (size_t)p * 16) = hi;
+        *reinterpret_cast<uint4*>(wq + (size_t)P * r * 2 + (size_t)ng * P * 16 + (size_t)p * 16) = lo;
+      }
+    }
+  }
+}
+
+}  // namespace quad
+
+// 32 < r <= 64, r % 8 == 0, P <= 64: the four-warp chunk operators (readout elsewhere)
+bool quad_path_ok(const Dims& d) { return d.r > 32 && d.r <= 64 && (d.r & 7) == 0 && d.P <= 64; }
+
+size_t smem_fwd_chunk_q(const Dims&) { return (size_t)4 * quad::kRegion * sizeof(float); }
+
+cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               float* invs, int* flags, unsigned char* wm, cudaStream_t st) {
+  const size_t smem = smem_fwd_chunk_q(d);
+  const long long n = (long long)d.B * d.H * d.C;
+  cudaError_t e;
+  if (d.P <= 32) {
+    if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+        cudaSuccess)
+      return e;
+    quad::k_fwd_chunk_q<1><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, wm);
+  } else {
+    if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+        cudaSuccess)
+      return e;
+    quad::k_fwd_chunk_q<2><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, wm);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace ska

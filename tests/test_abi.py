@@ -111,9 +111,12 @@ def _contig(base, B, T, H, D):
     (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
     # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
-    # r = 64 (config 3): tensor-core token kernels, one CTA per chunk operator (which
-    # keeps the readout's token pass)
-    (dict(r=64, chunk_size=128), 1, None, TC),
+    # r = 64 (config 3): tensor-core token kernels and readout, four-warp forward
+    # chunk operators (the backward keeps the one-CTA operator kernel)
+    (dict(r=64, chunk_size=128), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
+    # r = 48 (the module default): four-warp forward operators, tensor-core readout,
+    # CUDA-core statistics and token backward
+    (dict(r=48), 1, None, RD | _lib.SKA_PATH_QUAD_CHUNK),
     # chunk 256: tensor-core statistics only
     (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
     # P % 16 != 0: tensor-core statistics only

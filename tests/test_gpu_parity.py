@@ -103,15 +103,40 @@ def test_config2_bf16_full_size():
     assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
 
 
-def test_config3_bf16_forward_head_subset():
-    """Config 3 (B=1 H=16 L=32768 r=64 chunk 128, seed 2) forward; every (b, h) series is
-    independent, so the oracle checks 3 of the 16 heads at full length."""
+def _oracle_heads_forward(args):
+    z, zq, v, chunk = args
+    return ska_core_forward(z, zq, v, 1.0, SkaParams(chunk_size=chunk), np.float32)[0]
+
+
+def test_config3_bf16_forward_all_heads():
+    """Config 3 (B=1 H=16 L=32768 r=64 chunk 128, seed 2) forward, every head at full
+    length against the oracle, head by head (the four-warp chunk operators and the
+    tensor-core readout)."""
+    from koopman_mamba_b200 import _lib
+    zt = torch.empty(1, 32768, 16, 64, dtype=torch.bfloat16, device=DEV)
+    assert _path(zt, zt, 64, 64, chunk=128) & _lib.SKA_PATH_QUAD_CHUNK
     z, zq, v = _inputs(1, 32768, 16, 64, 64, 2, dy=False)
     (y,) = run_cuda(z, zq, v, 1.0, None, torch.bfloat16, chunk_size=128)
-    heads = [0, 7, 15]
-    ref, _ = ska_core_forward(z[:, :, heads], zq[:, :, heads], v[:, :, heads], 1.0, SkaParams(chunk_size=128))
-    assert rel_fro(y[:, :, heads], ref) <= BF16_TOL
     assert np.all(np.isfinite(y))
+    refs = [_oracle_heads_forward((z[:, :, h:h + 1], zq[:, :, h:h + 1], v[:, :, h:h + 1], 128)) for h in range(16)]
+    ref = np.concatenate(refs, axis=2)
+    assert rel_fro(y, ref) <= BF16_TOL
+    for h in range(16):
+        assert rel_fro(y[:, :, h], ref[:, :, h]) <= BF16_TOL, h
+
+
+def test_config3_bf16_backward_full_size():
+    """Config 3 shape forward + backward through the C ABI (all 16 heads, L=32768,
+    r=64, chunk 128), checked against the oracle on 3 heads at full length (the
+    series are independent; the backward runs the one-CTA chunk operators)."""
+    z, zq, v, dy = _inputs(1, 32768, 16, 64, 64, 2)
+    got = run_cuda(z, zq, v, 1.0, dy, torch.bfloat16, chunk_size=128)
+    heads = [0, 9, 15]
+    sub = [a[:, :, heads] for a in (z, zq, v, dy)]
+    ref = ska_core_fwd_bwd(*sub[:3], 1.0, sub[3], SkaParams(chunk_size=128), np.float32)
+    for g, r_, n in zip(got[:4], ref[:4], ("y", "dz", "dzq", "dv")):
+        assert rel_fro(g[:, :, heads], r_) <= BF16_TOL, n
+    assert all(np.all(np.isfinite(g)) for g in got[:4])
 
 
 def test_fused_projection_strides_bitwise():
