@@ -212,6 +212,42 @@ int ska_set_wait_limit(uint32_t polls);
 int ska_check_status(const SkaShape* shape, const void* saved, size_t saved_bytes, const void* scratch,
                      size_t scratch_bytes, void* stream, int64_t* first_bad, int* code);
 
+/* ---- Recurrent (decode) path --------------------------------------------
+ * Replaces KLF/koopman_lm/recurrent.py for one SKA layer: SKAState (:48-66),
+ * the state extraction of _ska_prefill (:129-189) and _ska_step (:270-375).
+ * The state of one layer is one caller-owned buffer of ska_state_size bytes
+ * (256-byte aligned), fp32 arrays in this order, each 256-byte aligned:
+ *   G [B][H][r][r], M [B][H][r][r], C_v [B][H][P][r], z_last [B][H][r],
+ *   max_norm [B][H], flags [B][H] (int32, bit 0: z_last is set).
+ * G, M and C_v hold the statistics of the keys normalised by max_norm, G with the
+ * ridge on its diagonal, exactly as the reference's SKAState.  Only B, H, r, P
+ * (and for the calls below T, ridge_eps, power_K, chunk_size) of the shape are
+ * used; the standard strategy only (the reference's state is the undecayed sum):
+ * SKA_STRATEGY_DECAY returns SKA_ERR_STRATEGY. */
+int ska_state_size(const SkaShape* shape, size_t* state_bytes);
+
+/* The fresh state of SKAState.__init__: G = ridge I, M = C_v = 0, no z_last,
+ * max_norm = 1e-6. */
+int ska_state_init(const SkaShape* shape, void* state, size_t state_bytes, void* stream);
+
+/* The state after a prompt of shape->T tokens (recurrent.py:150-189), from the
+ * `saved` buffer that ska_fwd wrote for the same shape, z and v: the exclusive
+ * prefix statistics of the last chunk plus that chunk's own tokens (the rest of
+ * the prompt is not read again), scaled by the forward's max key norm, which
+ * becomes the state's max_norm; z_last = z[T-1] / max_norm. */
+int ska_prefill_state(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v,
+                      const void* saved, size_t saved_bytes, void* state, size_t state_bytes, void* stream);
+
+/* shape->T decode tokens in order (z, zq, v: [B, T, H, D]; y: [B, T, H, P]),
+ * each exactly one _ska_step (recurrent.py:306-369): with max_norm frozen,
+ * G += z z^T, M += z z_last^T (when z_last is set), C_v += v z^T, then
+ * y = C_v G^-1 L A^K L^-1 zq with L = chol(sym(G)) (1e-4 jitter where that
+ * fails) and A = clamp(gamma,1,1.5) (M G^-1) / max(sigma, 1) from 6 power
+ * iterations.  Updates the state in place.  r <= 32 (SKA_ERR_UNSUPPORTED
+ * otherwise).  One warp per (batch, head). */
+int ska_step(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+             const float* gamma, const SkaTensor* y, void* state, size_t state_bytes, void* stream);
+
 /* Forward with no allocation anywhere (no counterpart in the reference, whose
  * PyTorch path always allocates through the caching allocator).  Same
  * computation and arguments as ska_fwd, minus the `saved` buffer: the

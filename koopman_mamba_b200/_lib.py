@@ -30,6 +30,10 @@ EXPORTED = (
     "ska_kernel_path",
     "ska_set_wait_limit",
     "ska_check_status",
+    "ska_state_size",
+    "ska_state_init",
+    "ska_prefill_state",
+    "ska_step",
 )
 SKA_ERR_TIMEOUT = -9
 SKA_STATUS_BWD_BASE = 16
@@ -109,6 +113,16 @@ def _declare(L: ctypes.CDLL) -> None:
     L.ska_check_status.argtypes = [P(SkaShape), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
                                    ctypes.c_void_p, P(ctypes.c_int64), P(ctypes.c_int)]
     L.ska_check_status.restype = ctypes.c_int
+    L.ska_state_size.argtypes = [P(SkaShape), P(ctypes.c_size_t)]
+    L.ska_state_size.restype = ctypes.c_int
+    L.ska_state_init.argtypes = [P(SkaShape), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.ska_state_init.restype = ctypes.c_int
+    L.ska_prefill_state.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), ctypes.c_void_p,
+                                    ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.ska_prefill_state.restype = ctypes.c_int
+    L.ska_step.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), P(SkaTensor), ctypes.c_void_p,
+                           P(SkaTensor), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.ska_step.restype = ctypes.c_int
 
 
 def lib() -> ctypes.CDLL:
@@ -144,6 +158,12 @@ def make_shape(B, T, H, r, P, chunk_size, power_K, ridge_eps, strategy=SKA_STRAT
                decay_alpha=1.0) -> SkaShape:
     return SkaShape(int(B), int(T), int(H), int(r), int(P), int(chunk_size), int(power_K),
                     int(strategy), float(ridge_eps), float(decay_alpha))
+
+
+def state_size(shape: SkaShape) -> int:
+    n = ctypes.c_size_t(0)
+    check("ska_state_size", lib().ska_state_size(ctypes.byref(shape), ctypes.byref(n)))
+    return int(n.value)
 
 
 def workspace_size(shape: SkaShape) -> tuple[int, int]:

@@ -33,6 +33,17 @@ bool fwd_tc_readout(const Dims& d, const In& zq, const Out& y);
 template <typename IO>
 void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
                   const Out& dzq, const Out& dv, bool* full, bool* tok);
+struct StateLayout {
+  size_t G, M, C, zlast, maxnorm, flags, total;
+};
+StateLayout state_layout(long long B, long long H, long long r, long long P);
+cudaError_t launch_state_init(const Dims& d, char* state, const StateLayout& L, cudaStream_t st);
+template <typename IO>
+cudaError_t launch_prefill_state(const Dims& d, const In& z, const In& v, const float* stats,
+                                 const unsigned long long* cmax, char* state, const StateLayout& L, cudaStream_t st);
+template <typename IO>
+cudaError_t launch_step(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
+                        char* state, const StateLayout& L, cudaStream_t st);
 }  // namespace ska
 
 namespace {
@@ -292,6 +303,91 @@ int ska_bwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   else
     e = ska::launch_bwd<__nv_bfloat16>(d, iz, izq, iv, gamma, idy, L, static_cast<const char*>(saved), S,
                                        static_cast<char*>(scratch), odz, odzq, odv, dgamma, st);
+  return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
+}
+
+// ---- recurrent (decode) path ----
+
+int ska_state_size(const SkaShape* shape, size_t* state_bytes) {
+  Dims d{};
+  const int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (state_bytes) *state_bytes = ska::state_layout(d.B, d.H, d.r, d.P).total;
+  return SKA_OK;
+}
+
+static int check_state(const Dims& d, const void* state, size_t state_bytes, ska::StateLayout* L) {
+  if (!state) return SKA_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(state) % 256) return SKA_ERR_ALIGN;
+  *L = ska::state_layout(d.B, d.H, d.r, d.P);
+  return state_bytes < L->total ? SKA_ERR_WORKSPACE : SKA_OK;
+}
+
+int ska_state_init(const SkaShape* shape, void* state, size_t state_bytes, void* stream) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (d.B == 0) return SKA_OK;
+  ska::StateLayout L{};
+  if ((rc = check_state(d, state, state_bytes, &L))) return rc;
+  return ska::launch_state_init(d, static_cast<char*>(state), L, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? SKA_OK
+             : SKA_ERR_LAUNCH;
+}
+
+int ska_prefill_state(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v, const void* saved,
+                      size_t saved_bytes, void* state, size_t state_bytes, void* stream) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (d.decay) return SKA_ERR_STRATEGY;   // the reference's state is the plain (undecayed) sum
+  const int es = elem_size(io_dtype);
+  if (!es) return SKA_ERR_DTYPE;
+  const bool work = d.B > 0;
+  ska::In iz{}, iv{};
+  if ((rc = check_tensor(z, es, work, &iz)) || (rc = check_tensor(v, es, work, &iv))) return rc;
+  if (!work) return SKA_OK;
+  ska::StateLayout L{};
+  if ((rc = check_state(d, state, state_bytes, &L))) return rc;
+  if (!saved) return SKA_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
+  const ska::SavedLayout S = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
+  if (saved_bytes < S.total) return SKA_ERR_WORKSPACE;
+  const char* sv = static_cast<const char*>(saved);
+  const float* stats = reinterpret_cast<const float*>(sv + S.stats);
+  const auto* cmax = reinterpret_cast<const unsigned long long*>(sv + S.cmax);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* sp = static_cast<char*>(state);
+  const cudaError_t e = io_dtype == SKA_DTYPE_F32
+                            ? ska::launch_prefill_state<float>(d, iz, iv, stats, cmax, sp, L, st)
+                            : ska::launch_prefill_state<__nv_bfloat16>(d, iz, iv, stats, cmax, sp, L, st);
+  return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
+}
+
+int ska_step(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
+             const float* gamma, const SkaTensor* y, void* state, size_t state_bytes, void* stream) {
+  Dims d{};
+  int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (d.decay) return SKA_ERR_STRATEGY;
+  if (d.r > 32) return SKA_ERR_UNSUPPORTED;
+  const int es = elem_size(io_dtype);
+  if (!es) return SKA_ERR_DTYPE;
+  const bool work = d.B > 0;
+  ska::In iz{}, izq{}, iv{};
+  ska::Out oy{};
+  if ((rc = check_tensor(z, es, work, &iz)) || (rc = check_tensor(zq, es, work, &izq)) ||
+      (rc = check_tensor(v, es, work, &iv)) || (rc = check_out(y, es, work, &oy)))
+    return rc;
+  if (!work) return SKA_OK;
+  if (!gamma) return SKA_ERR_NULL;
+  ska::StateLayout L{};
+  if ((rc = check_state(d, state, state_bytes, &L))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* sp = static_cast<char*>(state);
+  const cudaError_t e = io_dtype == SKA_DTYPE_F32
+                            ? ska::launch_step<float>(d, iz, izq, iv, gamma, oy, sp, L, st)
+                            : ska::launch_step<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, sp, L, st);
   return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
 }
 
