@@ -144,7 +144,7 @@ int ska_set_profile_events(void* const* events, int count);
  * kernels).  Returns a non-negative mask of SKA_PATH_* bits, or a negative
  * SKA_ERR_* code for arguments ska_fwd would reject.  Launches nothing.
  *   SKA_PATH_TC_STATS    chunk statistics on TMA + tcgen05 (bf16 tensors with
- *                        16-byte aligned base and strides, r in {32, 64},
+ *                        16-byte aligned base and strides, r % 16 == 0,
  *                        P % 8 == 0, chunk_size % 16 == 0); otherwise on
  *                        CUDA-core fp32 kernels
  *   SKA_PATH_WARP_CHUNK  chunk operators on the warp-per-chunk register

@@ -982,7 +982,9 @@ static bool token_map(CUtensorMap* m, const In& x, int B, int T, int H, int D, i
 }
 
 bool stats_tc_ok(const Dims& d, const In& z, const In& v) {
-  if (d.r % 32 != 0 || d.r > 64 || d.P % 8 != 0 || d.P > 128 || d.CS % 16 != 0 || d.CS > 256) return false;
+  // r % 16: products of N = r columns and 16-column epilogues (r % 32 also takes the
+  // 64-byte swizzled tiles when P % 32 == 0, else 16-byte feature groups)
+  if (d.r % 16 != 0 || d.r > 64 || d.P % 8 != 0 || d.P > 128 || d.CS % 16 != 0 || d.CS > 256) return false;
   const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!al(z.p) || !al(v.p)) return false;
   return stride_ok(z.st, d.T) && stride_ok(z.sh, d.H) && stride_ok(z.sb, d.B) && stride_ok(v.st, d.T) &&

@@ -114,15 +114,17 @@ def _contig(base, B, T, H, D):
     # r = 64 (config 3): tensor-core token kernels and readout, four-warp forward
     # chunk operators (the backward keeps the one-CTA operator kernel)
     (dict(r=64, chunk_size=128), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
-    # r = 48 (the module default): four-warp forward operators, tensor-core readout,
-    # CUDA-core statistics and token backward
-    (dict(r=48), 1, None, RD | _lib.SKA_PATH_QUAD_CHUNK),
+    # r = 48 (the module default): tensor-core statistics, readout and token backward,
+    # four-warp forward operators (the backward keeps the one-CTA operator kernel)
+    (dict(r=48), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
     # chunk 256: tensor-core statistics only
     (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
     # P % 16 != 0: tensor-core statistics only
     (dict(P=40), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_FUSED_SCAN),
-    # r = 16: CUDA-core token kernels, tensor-core forward readout
-    (dict(r=16), 1, None, _lib.SKA_PATH_WARP_CHUNK | RD),
+    # r = 16 (config 5): every tensor-core kernel but the fused statistics + scan
+    (dict(r=16), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
+    # r = 16, P = 32 (config 5's head): the same
+    (dict(r=16, P=32), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
     # token stride not a multiple of 16 bytes: CUDA-core token kernels
     (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
     # decay strategy shares the token kernels and the fused statistics + scan

@@ -304,3 +304,24 @@ def test_empty_batch_and_errors():
     with pytest.raises(SkaError):
         ska_core(torch.zeros(1, 0, 1, 8, device=DEV), torch.zeros(1, 0, 1, 8, device=DEV),
                  torch.zeros(1, 0, 1, 8, device=DEV), g)
+
+
+@pytest.mark.parametrize("B,T,H,r,P,chunk", [
+    (4, 1024, 4, 16, 32, 64),     # config 5's SKA head (d_model 128, H=4, r=16), 16 series
+    (2, 2048, 7, 48, 64, 64),     # config 4's SKA layer (H=7, r=48, the module default rank)
+])
+def test_bf16_model_config_heads(B, T, H, r, P, chunk):
+    """The SKA shapes of the two full-model configurations, bf16, forward and backward
+    against the oracle: r = 16 takes every tensor-core kernel but the fused
+    statistics + scan; r = 48 the tensor-core statistics, readout and token backward
+    around the four-warp forward operators."""
+    from koopman_mamba_b200 import _lib
+    zt = torch.empty(B, T, H, r, dtype=torch.bfloat16, device=DEV)
+    vt = torch.empty(B, T, H, P, dtype=torch.bfloat16, device=DEV)
+    path = _path(zt, vt, r, P, chunk)
+    assert path & _lib.SKA_PATH_TC_STATS and path & _lib.SKA_PATH_TC_TOKEN_BWD
+    z, zq, v, dy = _inputs(B, T, H, r, P, 70 + r)
+    got = run_cuda(z, zq, v, 1.15, dy, torch.bfloat16, chunk_size=chunk)
+    ref = ska_core_fwd_bwd(z, zq, v, 1.15, dy, SkaParams(chunk_size=chunk), np.float32)
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
