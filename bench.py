@@ -34,11 +34,12 @@ the c3 line alone.  Fields:
             bytes
   sustained ~1 s of back-to-back steps after the timed region with NVML clocks
             (the K-step timed region is short; this shows the clocks under load)
-  cpu_baseline  the numpy oracle (port of the reference's CPU path) on the box's
-            host cores, rank 0 at N=1 only, best of 3 after 1 warm-up
+  cpu_baseline  the reference's CPU path restated in PyTorch (oracle/ska_torch_port.py,
+            which runs at the reference's own CPU speed) on the box's host cores,
+            rank 0 at N=1 only, best of 3 after 1 warm-up
 
---impl reference times the reference's CPU path (the numpy oracle port, all host
-cores) on the same workload; under torchrun only rank 0 runs it.
+--impl reference times that same CPU path (all host cores, one series slice per
+process) on the same workload; under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -117,7 +118,7 @@ def host_inputs(wl, rank, world, dy=True):
 
 
 # ----------------------------------------------------------------------------
-# CPU side: the oracle port of the reference's CPU path, in a spawn pool
+# CPU side: the PyTorch restatement of the reference's CPU path, in a spawn pool
 # ----------------------------------------------------------------------------
 
 _CPU_CACHE = {}
@@ -126,25 +127,29 @@ _CPU_CACHE = {}
 def _cpu_inputs(key):
     if key not in _CPU_CACHE:
         wl = WORKLOADS[key]
-        _CPU_CACHE[key] = [t.numpy() for t in host_inputs(wl, 0, 1)]
+        _CPU_CACHE[key] = host_inputs(wl, 0, 1)
     return _CPU_CACHE[key]
 
 
 def _cpu_task(args):
-    """One slice of the workload through the numpy oracle (fp32, as the reference
-    computes after .float()); returns seconds."""
+    """One slice of the workload through the PyTorch CPU restatement of the
+    reference's path (fp32 after the bf16 rounding, as the reference computes after
+    .float(); autograd backward), one thread; returns seconds."""
     key, b, h_lo, h_hi = args
-    os.environ.setdefault("OMP_NUM_THREADS", "1")
-    import numpy as np
-    from oracle.ska_oracle import SkaParams, ska_core_forward, ska_core_fwd_bwd
+    import torch
+    from oracle.ska_torch_port import ska_core_torch
+    torch.set_num_threads(1)
     wl = WORKLOADS[key]
-    x = [a[b:b + 1, :, h_lo:h_hi] for a in _cpu_inputs(key)]
-    p = SkaParams(chunk_size=wl["CS"], ridge_eps=wl["ridge"], power_K=wl["K"])
+    x = [a[b:b + 1, :, h_lo:h_hi].contiguous() for a in _cpu_inputs(key)]
     t0 = time.perf_counter()
     if wl["bwd"]:
-        ska_core_fwd_bwd(x[0], x[1], x[2], 1.0, x[3], p, np.float32)
+        z, zq, v = (t.clone().requires_grad_(True) for t in x[:3])
+        g = torch.tensor(1.0, requires_grad=True)
+        ska_core_torch(z, zq, v, g, chunk_size=wl["CS"], ridge_eps=wl["ridge"], power_K=wl["K"]).backward(x[3])
     else:
-        ska_core_forward(x[0], x[1], x[2], 1.0, p, np.float32)
+        with torch.no_grad():
+            ska_core_torch(x[0], x[1], x[2], torch.tensor(1.0), chunk_size=wl["CS"], ridge_eps=wl["ridge"],
+                           power_K=wl["K"])
     return time.perf_counter() - t0
 
 
@@ -186,9 +191,9 @@ def cpu_baseline(pool, workers, key, repeats=3):
     ts = [cpu_step(pool, key) for _ in range(repeats)]
     what = "fwd+bwd" if wl["bwd"] else "fwd"
     return {"value": wl["B"] * wl["L"] / min(ts), "unit": UNIT, "cores": workers, "kind": "port",
-            "sample": f"the whole {key} workload ({wl['B']}x{wl['L']} tokens x {wl['H']} heads, {what}), numpy "
-                      f"oracle fp32, {len(cpu_tasks(key))} series slices over {workers} processes, best of "
-                      f"{repeats} after 1 warm-up",
+            "sample": f"the whole {key} workload ({wl['B']}x{wl['L']} tokens x {wl['H']} heads, {what}), PyTorch "
+                      f"CPU restatement of the reference path (fp32, autograd backward), {len(cpu_tasks(key))} "
+                      f"series slices over {workers} single-thread processes, best of {repeats} after 1 warm-up",
             "seconds": [round(t, 4) for t in ts]}
 
 
@@ -215,9 +220,10 @@ def run_reference_arm(args):
         "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
-        "compute": "numpy fp32 on the host cores (the reference's fp32 upcast of the bf16 tensors)",
+        "compute": "PyTorch fp32 on the host cores (the reference's fp32 upcast of the bf16 tensors; batched "
+                   "LAPACK Cholesky and solves, autograd backward)",
         "data": "synthetic (seeded N(0,1)/8 inputs, bf16-rounded)",
-        "config": {"workload": wl["name"], "path": "reference CPU path: numpy oracle port of "
+        "config": {"workload": wl["name"], "path": "reference CPU path: PyTorch restatement of "
                    "koopman_lm/ska.py (PyTorch backend), fp32", "io_dtype": "bf16-rounded"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
                          "sample": f"the whole workload per step, {len(cpu_tasks(key))} series slices over "

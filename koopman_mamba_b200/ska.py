@@ -19,7 +19,7 @@ import torch.nn as nn
 
 from . import _lib
 
-__all__ = ["SKAModule", "ska_core", "SkaCoreFunction"]
+__all__ = ["SKAModule", "ska_core", "SkaCoreFunction", "ProjectedSkaFunction"]
 
 _DTYPES = {torch.float32: _lib.SKA_DTYPE_F32, torch.bfloat16: _lib.SKA_DTYPE_BF16}
 
@@ -76,6 +76,48 @@ def _stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _core_fwd(z, zq, v, g32, params: _Params):
+    """ska_fwd on caller-owned tensors; returns (y, saved, saved_bytes, scratch_bytes)."""
+    dev = z.device
+    shape = _shape(z, v, params)
+    saved_bytes, scratch_bytes = _lib.workspace_size(shape)
+    B, T, H, _ = z.shape
+    y = torch.empty((B, T, H, v.shape[-1]), dtype=z.dtype, device=dev)
+    saved = torch.empty(max(saved_bytes, 1), dtype=torch.uint8, device=dev)
+    dz_, dzq_, dv_, dy_ = (_tensor_desc(t) for t in (z, zq, v, y))
+    with torch.cuda.device(dev):
+        rc = _lib.lib().ska_fwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(dz_),
+                                ctypes.byref(dzq_), ctypes.byref(dv_), ctypes.c_void_p(g32.data_ptr()),
+                                ctypes.byref(dy_), ctypes.c_void_p(saved.data_ptr()), saved_bytes,
+                                ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check("ska_fwd", rc)
+    return y, saved, saved_bytes, scratch_bytes
+
+
+def _core_bwd(z, zq, v, g32, dy, params: _Params, saved, saved_bytes, scratch_bytes, dz, dzq, dv):
+    """ska_bwd writing into the caller's dz, dzq, dv (any feature-contiguous views);
+    returns d(gamma) as a float32 scalar tensor."""
+    dev = z.device
+    shape = _shape(z, v, params)
+    scratch = torch.empty(max(scratch_bytes, 1), dtype=torch.uint8, device=dev)
+    dgamma = torch.empty((), dtype=torch.float32, device=dev)
+    descs = [_tensor_desc(t) for t in (z, zq, v, dy, dz, dzq, dv)]
+    with torch.cuda.device(dev):
+        rc = _lib.lib().ska_bwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(descs[0]),
+                                ctypes.byref(descs[1]), ctypes.byref(descs[2]),
+                                ctypes.c_void_p(g32.data_ptr()), ctypes.byref(descs[3]),
+                                ctypes.c_void_p(saved.data_ptr()), saved_bytes,
+                                ctypes.c_void_p(scratch.data_ptr()), scratch_bytes,
+                                ctypes.byref(descs[4]), ctypes.byref(descs[5]), ctypes.byref(descs[6]),
+                                ctypes.c_void_p(dgamma.data_ptr()), ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check("ska_bwd", rc)
+    return dgamma
+
+
+def _gamma32(gamma, dev):
+    return gamma.detach().reshape(()).to(device=dev, dtype=torch.float32).contiguous()
+
+
 class SkaCoreFunction(torch.autograd.Function):
     """autograd wrapper: forward = ``ska_fwd``, backward = ``ska_bwd``."""
 
@@ -83,52 +125,78 @@ class SkaCoreFunction(torch.autograd.Function):
     def forward(ctx, z, zq, v, gamma, params: _Params):
         _check_inputs(z, zq, v, gamma)
         z, zq, v = (_feature_contiguous(t) for t in (z, zq, v))
-        dev = z.device
-        shape = _shape(z, v, params)
-        saved_bytes, scratch_bytes = _lib.workspace_size(shape)
-        B, T, H, _ = z.shape
-        P = v.shape[-1]
-        y = torch.empty((B, T, H, P), dtype=z.dtype, device=dev)
-        saved = torch.empty(max(saved_bytes, 1), dtype=torch.uint8, device=dev)
-        g32 = gamma.detach().reshape(()).to(device=dev, dtype=torch.float32).contiguous()
-        dz_, dzq_, dv_, dy_ = (_tensor_desc(t) for t in (z, zq, v, y))
-        with torch.cuda.device(dev):
-            rc = _lib.lib().ska_fwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(dz_),
-                                    ctypes.byref(dzq_), ctypes.byref(dv_), ctypes.c_void_p(g32.data_ptr()),
-                                    ctypes.byref(dy_), ctypes.c_void_p(saved.data_ptr()), saved_bytes,
-                                    ctypes.c_void_p(_stream_ptr(dev)))
-        _lib.check("ska_fwd", rc)
+        g32 = _gamma32(gamma, z.device)
+        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params)
         ctx.params = params
         ctx.gamma_dtype = gamma.dtype
         ctx.gamma_shape = gamma.shape
-        ctx.scratch_bytes = scratch_bytes
-        ctx.saved_bytes = saved_bytes
         ctx.save_for_backward(z, zq, v, g32, saved)
         return y
 
     @staticmethod
     def backward(ctx, dy):
         z, zq, v, g32, saved = ctx.saved_tensors
-        dev = z.device
         dy = _feature_contiguous(dy.to(z.dtype))
-        shape = _shape(z, v, ctx.params)
-        scratch = torch.empty(max(ctx.scratch_bytes, 1), dtype=torch.uint8, device=dev)
         dz = torch.empty_like(z, memory_format=torch.contiguous_format)
         dzq = torch.empty_like(zq, memory_format=torch.contiguous_format)
         dv = torch.empty_like(v, memory_format=torch.contiguous_format)
-        dgamma = torch.empty((), dtype=torch.float32, device=dev)
-        descs = [_tensor_desc(t) for t in (z, zq, v, dy, dz, dzq, dv)]
-        with torch.cuda.device(dev):
-            rc = _lib.lib().ska_bwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(descs[0]),
-                                    ctypes.byref(descs[1]), ctypes.byref(descs[2]),
-                                    ctypes.c_void_p(g32.data_ptr()), ctypes.byref(descs[3]),
-                                    ctypes.c_void_p(saved.data_ptr()), ctx.saved_bytes,
-                                    ctypes.c_void_p(scratch.data_ptr()), ctx.scratch_bytes,
-                                    ctypes.byref(descs[4]), ctypes.byref(descs[5]), ctypes.byref(descs[6]),
-                                    ctypes.c_void_p(dgamma.data_ptr()), ctypes.c_void_p(_stream_ptr(dev)))
-        _lib.check("ska_bwd", rc)
+        dgamma = _core_bwd(z, zq, v, g32, dy, ctx.params, saved, ctx.saved_bytes, ctx.scratch_bytes, dz, dzq, dv)
         dg = dgamma.to(ctx.gamma_dtype).reshape(ctx.gamma_shape)
         return dz, dzq, dv, dg, None
+
+
+def _split_proj(proj, H, r, P):
+    """z, zq, v as column slices of the fused projection output [B, T, H(2r + P)]
+    (views: the kernels take the strides as they are)."""
+    Hr = H * r
+    return (proj[..., :Hr].unflatten(-1, (H, r)), proj[..., Hr:2 * Hr].unflatten(-1, (H, r)),
+            proj[..., 2 * Hr:].unflatten(-1, (H, P)))
+
+
+class ProjectedSkaFunction(torch.autograd.Function):
+    """The key/query/value projections as ONE GEMM ``x [Wk; Wq; Wv]^T`` whose column
+    slices feed the SKA core without copies, then the core (upstream
+    ``ska_fast.py:361-364`` fuses the projections the same way; ``ska.py:428-457``
+    is the math).  The backward has the core write dz, dzq, dv straight into one
+    gradient buffer of the fused projection's shape, then forms ``dx = dproj W`` and
+    ``dW = dproj^T x`` as two GEMMs (instead of three projections' six, and without
+    materialising the slices' gradients separately).  Under autocast the GEMMs run
+    in the autocast dtype, as ``nn.Linear`` would."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
+    def forward(ctx, x, w, gamma, H, r, P, params: _Params):
+        proj = torch.nn.functional.linear(x, w)
+        if proj.dtype not in _DTYPES:
+            proj = proj.float()
+        z, zq, v = _split_proj(proj, H, r, P)
+        _check_inputs(z, zq, v, gamma)
+        g32 = _gamma32(gamma, x.device)
+        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params)
+        ctx.params, ctx.hrp = params, (H, r, P)
+        ctx.gamma_dtype, ctx.gamma_shape = gamma.dtype, gamma.shape
+        ctx.save_for_backward(x, w, proj, g32, saved)
+        return y
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, dy):
+        x, w, proj, g32, saved = ctx.saved_tensors
+        H, r, P = ctx.hrp
+        z, zq, v = _split_proj(proj, H, r, P)
+        dy = _feature_contiguous(dy.to(proj.dtype))
+        dproj = torch.empty_like(proj)
+        dz, dzq, dv = _split_proj(dproj, H, r, P)
+        dgamma = _core_bwd(z, zq, v, g32, dy, ctx.params, saved, ctx.saved_bytes, ctx.scratch_bytes, dz, dzq, dv)
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.matmul(dproj, w.to(dproj.dtype) if not torch.is_autocast_enabled() else w)
+        if ctx.needs_input_grad[1]:
+            x2 = x.reshape(-1, x.shape[-1])
+            d2 = dproj.reshape(-1, dproj.shape[-1])
+            dw = torch.matmul(d2.t(), x2.to(d2.dtype) if not torch.is_autocast_enabled() else x2)
+        dg = dgamma.to(ctx.gamma_dtype).reshape(ctx.gamma_shape)
+        return dx, dw, dg, None, None, None, None
 
 
 def ska_core(z, zq, v, gamma, *, chunk_size=64, ridge_eps=1e-3, power_K=2, chunk_strategy="standard",
@@ -203,20 +271,24 @@ class SKAModule(nn.Module):
         self.eta = nn.Parameter(torch.tensor(scale))
         self.ssn_gamma = nn.Parameter(torch.tensor(1.0))
 
+    def _params(self) -> _Params:
+        if self.chunk_strategy == "standard":
+            strategy, alpha = _lib.SKA_STRATEGY_STANDARD, 1.0
+        else:
+            strategy, alpha = _lib.SKA_STRATEGY_DECAY, float(self.decay_alpha)
+        return _Params(self.chunk_size, self.ridge_eps, self.power_K, strategy, alpha)
+
     def forward(self, hidden_states):
+        """``ska.py:423-461``: projections, SKA core, eta and out_proj.  The three
+        projections run as one GEMM whose column slices go to the kernels without
+        copies (ProjectedSkaFunction), and eta is folded into the out_proj weight
+        (``out_proj(eta y) = y (eta W_o)^T``), which saves a pass over y."""
         B, T, _ = hidden_states.shape
         r, H, P = self.rank, self.H, self.P
-        z = self.key_proj(hidden_states).reshape(B, T, H, r)
-        zq = self.query_proj(hidden_states).reshape(B, T, H, r)
-        v = self.value_proj(hidden_states).reshape(B, T, H, P)
-        dt = z.dtype if z.dtype in _DTYPES else torch.float32
-        z, zq, v = (t.to(dt) for t in (z, zq, v))
-        with torch.autocast(device_type="cuda", enabled=False):
-            y_hat = ska_core(z, zq, v, self.ssn_gamma, chunk_size=self.chunk_size, ridge_eps=self.ridge_eps,
-                             power_K=self.power_K, chunk_strategy=self.chunk_strategy,
-                             decay_alpha=self.decay_alpha)
-        y_hat = self.eta * y_hat.to(hidden_states.dtype)
-        return self.out_proj(y_hat.reshape(B, T, H * P))
+        w = torch.cat([self.key_proj.weight, self.query_proj.weight, self.value_proj.weight], 0)
+        y_hat = ProjectedSkaFunction.apply(hidden_states, w, self.ssn_gamma, H, r, P, self._params())
+        w_out = self.out_proj.weight * self.eta
+        return torch.nn.functional.linear(y_hat.reshape(B, T, H * P).to(hidden_states.dtype), w_out)
 
     def extra_repr(self):
         parts = [

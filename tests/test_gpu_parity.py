@@ -325,3 +325,58 @@ def test_bf16_model_config_heads(B, T, H, r, P, chunk):
     ref = ska_core_fwd_bwd(z, zq, v, 1.15, dy, SkaParams(chunk_size=chunk), np.float32)
     assert_close(got[:4], ref[:4], BF16_TOL)
     assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
+def test_module_under_bf16_autocast_against_reference_fixture():
+    """SKAModule under torch.autocast(bfloat16) (the usual mixed-precision training
+    setup: fp32 hidden states, bf16 projections, so the core runs with bf16 I/O)
+    against the reference module's fp64 run, within the bf16 bar on the output, dx
+    and every parameter gradient.  The core's bf16 output and incoming gradient are
+    roundings the reference (which keeps y_hat in fp32 up to out_proj) does not
+    make; this bounds their effect."""
+    d = load("module_small")
+    m = SKAModule(int(d["meta_d_model"]), int(d["meta_H"]), rank=int(d["meta_r"]),
+                  chunk_size=int(d["meta_CS"])).to(DEV)
+    m.load_state_dict({k[3:]: torch.from_numpy(v) for k, v in d.items() if k.startswith("sd_")})
+    x = torch.from_numpy(d["x"]).to(DEV).requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = m(x)
+    assert out.dtype == torch.bfloat16
+    out.float().backward(torch.from_numpy(d["dout"]).to(DEV))
+    assert rel_fro(out.detach().float().cpu().numpy(), d["out"]) <= BF16_TOL
+    assert rel_fro(x.grad.cpu().numpy(), d["dx"]) <= BF16_TOL
+    for name, p in m.named_parameters():
+        ref = d["grad_" + name]
+        got = p.grad.detach().float().cpu().numpy()
+        if got.ndim == 0:
+            assert abs(float(got) - float(ref)) <= BF16_TOL * max(1.0, abs(float(ref))), name
+        else:
+            assert rel_fro(got, ref) <= BF16_TOL, name
+
+
+def test_module_fused_projection_matches_separate_projections():
+    """The module's one-GEMM projection path gives what three separate projections
+    through ska_core give (fp32, forward and every gradient)."""
+    torch.manual_seed(11)
+    m = SKAModule(96, 3, rank=16, chunk_size=32).to(DEV)
+    with torch.no_grad():
+        m.out_proj.weight.normal_(0, 0.05)
+        m.ssn_gamma.fill_(1.2)
+    x = torch.randn(2, 150, 96, device=DEV, requires_grad=True)
+    dout = torch.randn(2, 150, 96, device=DEV)
+    out = m(x)
+    out.backward(dout)
+    g1 = [x.grad.clone()] + [p.grad.clone() for p in m.parameters()]
+    x.grad = None
+    m.zero_grad()
+    B, T, _ = x.shape
+    z = m.key_proj(x).reshape(B, T, 3, 16)
+    zq = m.query_proj(x).reshape(B, T, 3, 16)
+    v = m.value_proj(x).reshape(B, T, 3, 32)
+    y = ska_core(z, zq, v, m.ssn_gamma, chunk_size=32)
+    out2 = m.out_proj(m.eta * y.reshape(B, T, 96))
+    out2.backward(dout)
+    g2 = [x.grad] + [p.grad for p in m.parameters()]
+    assert rel_fro(out.detach().cpu().numpy(), out2.detach().cpu().numpy()) <= 1e-5
+    for a, b in zip(g1, g2):
+        assert rel_fro(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5
