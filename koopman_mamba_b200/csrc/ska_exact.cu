@@ -443,6 +443,128 @@ __global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict
 }
 
 // ----------------------------------------------------------------------------
+// segmented scans: one DRAM round trip per record float
+//
+// The chunks of one series are cut into segments of kSegLen consecutive chunks;
+// one thread owns one float4 column of the record in one segment and loads all of
+// its chunks at once.  The G segments of a column sit in G consecutive lanes of
+// one warp (G a power of two <= 32, so C <= 32 * kSegLen), which exchange their
+// segment totals by shuffles:
+//   forward (exclusive):  out[c] = sum_{c' < c} a^(c - 1 - c') x[c']
+//   backward (suffix):    out[c] = sum_{c' > c} a^(c' - c - 1) x[c']
+// (a = decay_alpha for the decay strategy, 1 otherwise), the same sums as
+// k_scan_fwd / k_scan_bwd in one round trip instead of ceil(C / 16).  Only the last
+// segment can be short, and it is never between two others, so the decay factor
+// between segments is a^(kSegLen * gap).
+// ----------------------------------------------------------------------------
+constexpr int kSegLen = 16;
+
+__host__ __device__ inline int seg_count(int C) {
+  int g = 1;
+  while (g * kSegLen < C) g <<= 1;
+  return g;
+}
+bool seg_scan_ok(const Dims& d) { return (d.SW & 3) == 0 && d.C <= 32 * kSegLen; }
+
+__device__ __forceinline__ float4 f4_fma(float a, float4 x, float4 y) {   // a x + y
+  return make_float4(fmaf(a, x.x, y.x), fmaf(a, x.y, y.y), fmaf(a, x.z, y.z), fmaf(a, x.w, y.w));
+}
+__device__ __forceinline__ float4 f4_shfl(float4 v, int src) {
+  return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                     __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
+}
+
+template <bool REVERSE>
+__device__ __forceinline__ void seg_scan_column(float* rec0, long long stride, int C, int G, int seg, int lane,
+                                                bool active, int decay, float alpha) {
+  const int c0 = seg * kSegLen, n = active ? max(0, min(kSegLen, C - c0)) : 0;
+  float4 x[kSegLen];
+#pragma unroll
+  for (int k = 0; k < kSegLen; ++k)
+    x[k] = k < n ? *reinterpret_cast<const float4*>(rec0 + (long long)(c0 + k) * stride) : make_float4(0, 0, 0, 0);
+  const float a = decay ? alpha : 1.f;
+  // local scan in place; tot = the segment's total, weighted toward its far end
+  float4 tot = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kSegLen; ++i) {
+    const int k = REVERSE ? kSegLen - 1 - i : i;
+    if (k < n) {
+      const float4 xk = x[k];
+      x[k] = tot;
+      tot = f4_fma(a, tot, xk);
+    }
+  }
+  // a^kSegLen: the decay across one whole segment
+  float aL = 1.f;
+#pragma unroll
+  for (int i = 0; i < kSegLen; ++i) aL *= a;
+  // offset of this segment from the segments before it (after it, for REVERSE)
+  float4 off = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int base = lane - seg;   // lane of segment 0 of this column
+  for (int j = 1; j < G; ++j) {
+    // walking outward: forward takes segment seg - j, reverse seg + j
+    const int src = REVERSE ? seg + j : seg - j;
+    const float4 t = f4_shfl(tot, base + (src & (G - 1)));
+    float w = 1.f;
+    for (int q = 1; q < j; ++q) w *= aL;        // a^(kSegLen * (j - 1))
+    if (src >= 0 && src < G) off = f4_fma(w, t, off);
+  }
+  // out[c] = local[c] + a^(distance to the segment edge) off
+#pragma unroll
+  for (int i = 0; i < kSegLen; ++i) {
+    const int k = REVERSE ? kSegLen - 1 - i : i;
+    if (k < n) {
+      float w = 1.f;   // forward: a^k; reverse: a^(kSegLen - 1 - k) (full segments only reach here with offsets)
+      const int e = REVERSE ? (kSegLen - 1 - k) : k;
+      for (int q = 0; q < e; ++q) w *= a;
+      *reinterpret_cast<float4*>(rec0 + (long long)(c0 + k) * stride) = f4_fma(w, off, x[k]);
+    }
+  }
+}
+
+// grid (ceil(SW / 4 * G / 256), B * H); thread: column (SW / 4 of them) x segment
+__global__ void __launch_bounds__(kThreads) k_scan_seg_fwd(Dims d, float* __restrict__ stats) {
+  const int G = seg_count(d.C), lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = (int)(t / G), seg = (int)(t % G);
+  const bool active = col < (d.SW >> 2);
+  float* rec0 = stats + (size_t)blockIdx.y * d.C * d.SW + 4 * (active ? col : 0);
+  seg_scan_column<false>(rec0, d.SW, d.C, G, seg, lane, active, d.decay, d.alpha);
+}
+
+__global__ void __launch_bounds__(kThreads) k_scan_seg_bwd(Dims d, float* __restrict__ dstats,
+                                                           const float* __restrict__ dmpart,
+                                                           const float* __restrict__ dgpart,
+                                                           float* __restrict__ dm, float* __restrict__ dgamma) {
+  __shared__ float red[32];
+  const int G = seg_count(d.C), lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = (int)(t / G), seg = (int)(t % G);
+  const bool active = col < (d.SW >> 2);
+  const int bh = blockIdx.y;
+  float* rec0 = dstats + (size_t)bh * d.C * d.SW + 4 * (active ? col : 0);
+  seg_scan_column<true>(rec0, d.SW, d.C, G, seg, lane, active, d.decay, d.alpha);
+  if (blockIdx.x == 0) {   // d(max norm) per series, d(gamma) over everything
+    float s = 0.f;
+    for (int c = threadIdx.x; c < d.C; c += blockDim.x) s += dmpart[(size_t)bh * d.C + c];
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) dm[bh] = s;
+    if (bh == 0) {
+      const size_t n = (size_t)d.B * d.H * d.C;
+      float g = 0.f;
+      for (size_t i = threadIdx.x; i < n; i += blockDim.x) g += dgpart[i];
+      g = block_sum(g, red);
+      if (threadIdx.x == 0) *dgamma = g;
+    }
+  }
+}
+
+static dim3 seg_grid(const Dims& d) {
+  const long long threads = (long long)(d.SW >> 2) * seg_count(d.C);
+  return dim3((unsigned)((threads + kThreads - 1) / kThreads), d.B * d.H);
+}
+
+// ----------------------------------------------------------------------------
 // per-chunk operator (shared by forward and backward)
 // ----------------------------------------------------------------------------
 
@@ -1038,7 +1160,12 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
     k_fwd_stats<IO><<<grid, kThreads, s1, st>>>(d, z, v, stats, cmax);
   }
   prof_record(1, st);
-  if (!fused) k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
+  if (!fused) {
+    if (seg_scan_ok(d))
+      k_scan_seg_fwd<<<seg_grid(d), kThreads, 0, st>>>(d, stats);
+    else
+      k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
+  }
   prof_record(2, st);
   bool tc_read = false;   // readout as its own tensor-core kernel
   if (warp_path_ok(d)) {
@@ -1113,7 +1240,10 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
                                                dgpart);
   }
   prof_record(6, st);
-  k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
+  if (seg_scan_ok(d))
+    k_scan_seg_bwd<<<seg_grid(d), kThreads, 0, st>>>(d, dstats, dmpart, dgpart, dm, dgamma);
+  else
+    k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
                                                                                      dm, dgamma);
   prof_record(7, st);
   if (tc_tok) {

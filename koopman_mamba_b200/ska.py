@@ -281,14 +281,19 @@ class SKAModule(nn.Module):
     def forward(self, hidden_states):
         """``ska.py:423-461``: projections, SKA core, eta and out_proj.  The three
         projections run as one GEMM whose column slices go to the kernels without
-        copies (ProjectedSkaFunction), and eta is folded into the out_proj weight
-        (``out_proj(eta y) = y (eta W_o)^T``), which saves a pass over y."""
+        copies (ProjectedSkaFunction).  Outside autocast, eta is folded into the
+        out_proj weight (``out_proj(eta y) = y (eta W_o)^T``), which saves a pass
+        over y; under autocast the epilogue is the reference's (``eta * y`` in the
+        hidden-state dtype, then out_proj), because folding would take d(eta)
+        through the bf16-rounded weight gradient instead of through y."""
         B, T, _ = hidden_states.shape
         r, H, P = self.rank, self.H, self.P
         w = torch.cat([self.key_proj.weight, self.query_proj.weight, self.value_proj.weight], 0)
         y_hat = ProjectedSkaFunction.apply(hidden_states, w, self.ssn_gamma, H, r, P, self._params())
-        w_out = self.out_proj.weight * self.eta
-        return torch.nn.functional.linear(y_hat.reshape(B, T, H * P).to(hidden_states.dtype), w_out)
+        y_hat = y_hat.reshape(B, T, H * P).to(hidden_states.dtype)
+        if torch.is_autocast_enabled(hidden_states.device.type):
+            return self.out_proj(self.eta * y_hat)
+        return torch.nn.functional.linear(y_hat, self.out_proj.weight * self.eta)
 
     def extra_repr(self):
         parts = [

@@ -117,10 +117,20 @@ def run_core_case(ref_ska, ref_ac, name, *, B, T, H, r, P, CS, ridge=1e-3, K=2,
     print(f"wrote {path}: y_f64 |max| {np.abs(out['y_f64']).max():.3e}  dgamma {out['dgamma_f64']}")
 
 
-def run_module_case(ref_ska, name, *, B, T, d_model, H, r, CS, seed, dtype=torch.float64):
-    """Whole SKAModule (backend='pytorch') with seeded non-zero weights."""
+def run_module_case(ref_ska, name, *, B, T, d_model, H, r, CS, seed, dtype=torch.float64, bf16_proj=False):
+    """Whole SKAModule (backend='pytorch') with seeded non-zero weights.
+
+    bf16_proj: the key/query/value projection outputs are rounded to bfloat16 (a
+    straight-through rounding: the backward passes the gradient unchanged), which is
+    what those projections produce under torch.autocast(bfloat16) on a GPU while
+    the reference's core itself runs with autocast disabled (ska.py:433-457)."""
     torch.manual_seed(seed)
     m = ref_ska.SKAModule(d_model, H, rank=r, chunk_size=CS, backend="pytorch").to(dtype)
+    if bf16_proj:
+        def _round(_mod, _inp, out):
+            return out + (out.to(torch.bfloat16).to(out.dtype) - out).detach()
+        for proj in (m.key_proj, m.query_proj, m.value_proj):
+            proj.register_forward_hook(_round)
     g = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
         m.out_proj.weight.copy_(torch.randn(m.out_proj.weight.shape, generator=g).to(dtype)
@@ -186,6 +196,9 @@ def main():
                   bf16_round=True, note="r=64 CS=128 (config 3 class)")
     # Whole module: projections + core + eta + out_proj.
     run_module_case(ref_ska, "module_small", B=2, T=200, d_model=128, H=2, r=16, CS=64, seed=21)
+    # The same module with bf16-rounded projections (the autocast(bfloat16) setting).
+    run_module_case(ref_ska, "module_small_bf16proj", B=2, T=200, d_model=128, H=2, r=16, CS=64, seed=21,
+                    bf16_proj=True)
 
 
 if __name__ == "__main__":

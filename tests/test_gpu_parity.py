@@ -328,13 +328,19 @@ def test_bf16_model_config_heads(B, T, H, r, P, chunk):
 
 
 def test_module_under_bf16_autocast_against_reference_fixture():
-    """SKAModule under torch.autocast(bfloat16) (the usual mixed-precision training
-    setup: fp32 hidden states, bf16 projections, so the core runs with bf16 I/O)
-    against the reference module's fp64 run, within the bf16 bar on the output, dx
-    and every parameter gradient.  The core's bf16 output and incoming gradient are
-    roundings the reference (which keeps y_hat in fp32 up to out_proj) does not
-    make; this bounds their effect."""
-    d = load("module_small")
+    """SKAModule under torch.autocast(bfloat16) (fp32 hidden states, bf16 projections,
+    so the core runs with bf16 I/O) against the reference module run with the same
+    bf16-rounded projections (tests/golden/module_small_bf16proj.npz, fp64
+    elsewhere): output, dx and every weight gradient within the bf16 bar.
+
+    d(eta) is a dot product of ~51K cancelling terms, <d(eta y), y>, whose value
+    under autocast depends on where the bf16 GEMM of out_proj's backward rounds:
+    the reference's own autocast epilogue (d(eta y) = bf16(dout W_o)) moves it by
+    ~5% from its fp64 value on this fixture.  It is therefore checked against that
+    epilogue, emulated here on the CPU from the oracle's y_hat; the remaining
+    difference is this core's bf16 rounding of y_hat, which the reference does not
+    make."""
+    d = load("module_small_bf16proj")
     m = SKAModule(int(d["meta_d_model"]), int(d["meta_H"]), rank=int(d["meta_r"]),
                   chunk_size=int(d["meta_CS"])).to(DEV)
     m.load_state_dict({k[3:]: torch.from_numpy(v) for k, v in d.items() if k.startswith("sd_")})
@@ -346,12 +352,28 @@ def test_module_under_bf16_autocast_against_reference_fixture():
     assert rel_fro(out.detach().float().cpu().numpy(), d["out"]) <= BF16_TOL
     assert rel_fro(x.grad.cpu().numpy(), d["dx"]) <= BF16_TOL
     for name, p in m.named_parameters():
-        ref = d["grad_" + name]
         got = p.grad.detach().float().cpu().numpy()
         if got.ndim == 0:
-            assert abs(float(got) - float(ref)) <= BF16_TOL * max(1.0, abs(float(ref))), name
-        else:
-            assert rel_fro(got, ref) <= BF16_TOL, name
+            continue
+        assert rel_fro(got, d["grad_" + name]) <= BF16_TOL, name
+    # ssn_gamma: the core's own scalar (fp32 reduction of the backward kernels)
+    ref_g = float(d["grad_ssn_gamma"])
+    assert abs(float(m.ssn_gamma.grad) - ref_g) <= BF16_TOL * max(1.0, abs(ref_g))
+    # eta: against the reference's autocast epilogue, emulated from the oracle's y_hat
+    B, T, dm = d["x"].shape
+    H, r = int(d["meta_H"]), int(d["meta_r"])
+    P = dm // H
+    bf = lambda a: torch.as_tensor(a, dtype=torch.float64).bfloat16().double()   # noqa: E731
+    xs = torch.as_tensor(d["x"], dtype=torch.float64)
+    proj = [bf(xs @ torch.as_tensor(d["sd_" + k + ".weight"], dtype=torch.float64).T)
+            for k in ("key_proj", "query_proj", "value_proj")]
+    y, _ = ska_core_forward(proj[0].reshape(B, T, H, r).numpy(), proj[1].reshape(B, T, H, r).numpy(),
+                            proj[2].reshape(B, T, H, P).numpy(), float(d["sd_ssn_gamma"]),
+                            SkaParams(chunk_size=int(d["meta_CS"])))
+    g = bf(bf(d["dout"]).numpy() @ bf(d["sd_out_proj.weight"]).numpy())       # bf16(dout W_o)
+    deta_ref_autocast = float((g.numpy() * y.reshape(B, T, H * P)).sum())
+    assert abs(float(m.eta.grad) - deta_ref_autocast) <= BF16_TOL * max(1.0, abs(deta_ref_autocast)), \
+        (float(m.eta.grad), deta_ref_autocast, float(d["grad_eta"]))
 
 
 def test_module_fused_projection_matches_separate_projections():
