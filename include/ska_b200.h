@@ -23,8 +23,9 @@
  *     contiguous; the three other strides are given in ELEMENTS and may be
  *     arbitrary (e.g. column slices of one fused projection output).
  *   - io_dtype selects the element type of z, zq, v, y, dy, dz, dzq, dv:
- *     SKA_DTYPE_F32 or SKA_DTYPE_BF16.  All arithmetic is fp32 (the reference
- *     upcasts with .float(), ska.py:436-438).
+ *     SKA_DTYPE_F32 or SKA_DTYPE_BF16 (or, for ska_fwd, SKA_DTYPE_BF16_Y32).
+ *     All arithmetic is fp32 (the reference upcasts with .float(),
+ *     ska.py:436-438).
  *   - gamma / dgamma are device pointers to one fp32 scalar; dgamma is
  *     OVERWRITTEN (not accumulated).
  *   - The caller owns all memory.  ska_fwd writes a "saved" buffer that
@@ -52,6 +53,12 @@ extern "C" {
 enum {
   SKA_DTYPE_F32 = 0,
   SKA_DTYPE_BF16 = 1,
+  /* ska_fwd only: bf16 z, zq, v and an fp32 y (what the reference's module
+   * produces under autocast: bf16 projections, fp32 core output).  Needs the
+   * tensor-core readout layout (SKA_PATH_TC_READOUT_FWD) and returns
+   * SKA_ERR_UNSUPPORTED otherwise.  ska_bwd of such a forward takes
+   * SKA_DTYPE_BF16 (a bf16 dy). */
+  SKA_DTYPE_BF16_Y32 = 2,
 };
 
 enum {

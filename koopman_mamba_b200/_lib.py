@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libska_b200.so")
 SKA_ABI_VERSION = 1
 SKA_DTYPE_F32 = 0
 SKA_DTYPE_BF16 = 1
+SKA_DTYPE_BF16_Y32 = 2
 SKA_STRATEGY_STANDARD = 0
 SKA_STRATEGY_DECAY = 1
 

@@ -11,7 +11,7 @@
 namespace ska {
 template <typename T>
 cudaError_t launch_fwd(const Dims&, const In&, const In&, const In&, const float*, const Out&,
-                       const SavedLayout&, char*, cudaStream_t);
+                       const SavedLayout&, char*, cudaStream_t, bool);
 template <typename T>
 cudaError_t launch_bwd(const Dims&, const In&, const In&, const In&, const float*, const In&,
                        const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&, const Out&,
@@ -152,6 +152,7 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   Dims d{};
   int rc = make_dims(shape, &d);
   if (rc) return rc;
+  if (io_dtype == SKA_DTYPE_BF16_Y32) io_dtype = SKA_DTYPE_BF16;   // the same kernels
   const int es = elem_size(io_dtype);
   if (!es) return SKA_ERR_DTYPE;
   ska::In iz{}, iv{};
@@ -247,25 +248,28 @@ int ska_fwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   Dims d{};
   int rc = make_dims(shape, &d);
   if (rc) return rc;
-  const int es = elem_size(io_dtype);
+  // SKA_DTYPE_BF16_Y32: bf16 z, zq, v with an fp32 y
+  const bool y32 = io_dtype == SKA_DTYPE_BF16_Y32;
+  const int es = elem_size(y32 ? SKA_DTYPE_BF16 : io_dtype);
   if (!es) return SKA_ERR_DTYPE;
   const bool work = d.B > 0;
   ska::In iz{}, izq{}, iv{};
   ska::Out oy{};
   if ((rc = check_tensor(z, es, work, &iz)) || (rc = check_tensor(zq, es, work, &izq)) ||
-      (rc = check_tensor(v, es, work, &iv)) || (rc = check_out(y, es, work, &oy)))
+      (rc = check_tensor(v, es, work, &iv)) || (rc = check_out(y, y32 ? 4 : es, work, &oy)))
     return rc;
   if (!work) return SKA_OK;
   if (!gamma || !saved) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
   const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
   if (saved_bytes < L.total) return SKA_ERR_WORKSPACE;
+  if (y32 && !ska::fwd_tc_readout<__nv_bfloat16>(d, izq, oy)) return SKA_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (io_dtype == SKA_DTYPE_F32)
-    e = ska::launch_fwd<float>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st);
+    e = ska::launch_fwd<float>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, false);
   else
-    e = ska::launch_fwd<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st);
+    e = ska::launch_fwd<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, y32);
   return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
 }
 

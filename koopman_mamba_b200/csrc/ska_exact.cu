@@ -1075,8 +1075,8 @@ cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In&
 bool dw_tc_ok(const Dims& d, const In& zq, const In& dy);
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st);
 bool readout_tc_ok(const Dims& d, const In& zq, const Out& y);
-cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, int* status,
-                              cudaStream_t st);
+cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, bool y32,
+                              int* status, cudaStream_t st);
 }  // namespace tc
 cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                                const float* invs, const float* ops, const float* dwraw, float* dstats,
@@ -1133,9 +1133,11 @@ bool fwd_tc_readout(const Dims& d, const In& zq, const Out& y) {
 template bool fwd_tc_readout<float>(const Dims&, const In&, const Out&);
 template bool fwd_tc_readout<__nv_bfloat16>(const Dims&, const In&, const Out&);
 
+// y32: bf16 inputs with an fp32 y (the tensor-core readout path only; the caller checks
+// fwd_tc_readout first)
 template <typename IO>
 cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
-                       const SavedLayout& L, char* saved, cudaStream_t st) {
+                       const SavedLayout& L, char* saved, cudaStream_t st, bool y32) {
   float* stats = reinterpret_cast<float*>(saved + L.stats);
   unsigned long long* cmax = reinterpret_cast<unsigned long long*>(saved + L.cmax);
   float* invs = reinterpret_cast<float*>(saved + L.invs);
@@ -1189,7 +1191,7 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   prof_record(3, st);
   if (tc_read) {
     const unsigned char* wm = reinterpret_cast<const unsigned char*>(saved + L.wm);
-    if ((e = tc::launch_readout_tc(d, zq, wm, y, reinterpret_cast<int*>(saved + L.status), st)) != cudaSuccess)
+    if ((e = tc::launch_readout_tc(d, zq, wm, y, y32, reinterpret_cast<int*>(saved + L.status), st)) != cudaSuccess)
       return e;
   }
   prof_record(9, st);
@@ -1258,9 +1260,9 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
 }
 
 template cudaError_t launch_fwd<float>(const Dims&, const In&, const In&, const In&, const float*, const Out&,
-                                       const SavedLayout&, char*, cudaStream_t);
+                                       const SavedLayout&, char*, cudaStream_t, bool);
 template cudaError_t launch_fwd<__nv_bfloat16>(const Dims&, const In&, const In&, const In&, const float*,
-                                               const Out&, const SavedLayout&, char*, cudaStream_t);
+                                               const Out&, const SavedLayout&, char*, cudaStream_t, bool);
 template cudaError_t launch_bwd<float>(const Dims&, const In&, const In&, const In&, const float*, const In&,
                                        const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&,
                                        const Out&, const Out&, float*, cudaStream_t);

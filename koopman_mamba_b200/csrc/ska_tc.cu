@@ -629,6 +629,19 @@ __device__ __forceinline__ __nv_bfloat16* tok_ptr(const Out& o, int b, int t, in
   return static_cast<__nv_bfloat16*>(o.p) + (long long)b * o.sb + (long long)t * o.st + (long long)h * o.sh;
 }
 
+// 16 fp32 accumulator columns of token (b, t, h) -> y[j0 .. j0 + 16) as bf16, or as
+// fp32 (y32: the bf16-input / fp32-output mode)
+__device__ __forceinline__ void store_y16(const Out& y, int b, int t, int h, int j0, const float (&x)[16], bool y32) {
+  if (y32) {
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(y.p) + (long long)b * y.sb + (long long)t * y.st +
+                                          (long long)h * y.sh + j0);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) p[e] = make_float4(x[4 * e], x[4 * e + 1], x[4 * e + 2], x[4 * e + 3]);
+  } else {
+    store_bf16x16(tok_ptr(y, b, t, h) + j0, x);
+  }
+}
+
 __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_constant__ CUtensorMap mz,
                                                                const __grid_constant__ CUtensorMap mv,
                                                                const __grid_constant__ CUtensorMap mdy, Dims d,
@@ -1275,7 +1288,7 @@ __host__ __device__ inline ReadGeom read_geom(int r, int P, int CS) {
 
 __global__ void __launch_bounds__(kReadThreads) k_readout_tc(const __grid_constant__ CUtensorMap mzq, Dims d,
                                                              ReadGeom g, const unsigned char* __restrict__ wm,
-                                                             Out y, int* __restrict__ status) {
+                                                             Out y, bool y32, int* __restrict__ status) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint64_t bar_load, bar_mma;
   __shared__ uint32_t tmem_slot;
@@ -1349,7 +1362,7 @@ __global__ void __launch_bounds__(kReadThreads) k_readout_tc(const __grid_consta
 #pragma unroll
         for (int e = 0; e < 16; ++e) x[e] = nan;
       }
-      store_bf16x16(tok_ptr(y, b, t, h) + j0, x);
+      store_y16(y, b, t, h, j0, x, y32);
     }
   }
   if (tid == 0 && st) status[q] |= st << 2;            // bits 2-3 (bits 0-1: the statistics kernel)
@@ -1358,6 +1371,179 @@ __global__ void __launch_bounds__(kReadThreads) k_readout_tc(const __grid_consta
   if (warp == 0) {
     fence_after_sync();
     tmem_dealloc(tbase, g.ncols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_readout_ps: the same readout, many chunks per CTA (persistent, two CTAs per
+// SM), so that one chunk's copies overlap the previous chunks' products and
+// stores:
+//   warp 0      TMA copy of chunk j's zq tile and bulk copy of its W / m planes
+//               into shared stage j % ns;
+//   warp 1      chunk j's products into TMEM buffer j % kReadBufs;
+//   warps 2-5   the epilogue: warp w reads TMEM lane quarter w % 4 (rows
+//               32 (w % 4) + lane for M = 128, rows 16 (w % 4) + lane of lanes 0-15
+//               for M = 64) and stores the chunk's y rows as bf16.
+// Each warp waits together and one lane issues; the roles meet only at mbarriers.
+// The CTA takes chunks blockIdx.x, blockIdx.x + gridDim.x, ...
+// ---------------------------------------------------------------------------
+constexpr int kReadPsThreads = 192;
+constexpr int kReadStagesMax = 6;
+constexpr int kReadBufs = 4;
+
+__global__ void __launch_bounds__(kReadPsThreads, 1) k_readout_ps(const __grid_constant__ CUtensorMap mzq, Dims d,
+                                                                  ReadGeom g, uint32_t stage_bytes, int ns,
+                                                                  const unsigned char* __restrict__ wm, Out y,
+                                                                  bool y32, int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint64_t bar_load[kReadStagesMax], bar_free[kReadStagesMax], bar_mma[kReadBufs], bar_read[kReadBufs];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int err;
+  unsigned char* stages = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = d.r, P = d.P, CS = d.CS, T = d.T;
+  const long long nq = (long long)d.B * d.H * d.C;
+  const int nj = (int)((nq - (long long)blockIdx.x + gridDim.x - 1) / gridDim.x);   // this CTA's chunks
+  const auto chunk_of = [&](int j) { return (long long)blockIdx.x + (long long)j * gridDim.x; };
+
+  if (tid == 0) {
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(&bar_load[i], 1);
+      mbar_init(&bar_free[i], 1);
+    }
+    for (int i = 0; i < kReadBufs; ++i) {
+      mbar_init(&bar_mma[i], 1);
+      mbar_init(&bar_read[i], 4);
+    }
+    err = 0;
+    mbar_fence_init();
+    tma_prefetch_map(&mzq);
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, kReadBufs * g.ncols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {
+    // ---- copies ----
+    int nload = 0;
+    bool ok = true;
+    for (int j = 0; j < nj; ++j) {
+      if (j >= ns) {   // chunk j - ns's products have read the stage
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_free[j % ns], (uint32_t)(j / ns - 1) & 1u, d.wlim));
+        if (!ok) break;
+      }
+      if (lane == 0) {
+        const long long q = chunk_of(j);
+        const int c = (int)(q % d.C);
+        const long long bh = q / d.C;
+        const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+        unsigned char* tile = stages + (size_t)(j % ns) * stage_bytes;
+        uint64_t* bar = &bar_load[j % ns];
+        mbar_expect_tx(bar, (uint32_t)r * (uint32_t)CS * 2u + g.wbytes);
+        for (int k = 0; k < r / 8; ++k) tma_load_4d(tile + (size_t)k * g.grp, &mzq, bar, 8 * k, h, c * CS, b);
+        bulk_load(tile + g.o_w, wm + (size_t)q * g.wbytes, g.wbytes, bar);
+      }
+      __syncwarp();
+      nload = j + 1;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every copy has landed before the CTA leaves (bounded)
+      for (int s = 0; s < ns; ++s) {
+        int last = -1;
+        for (int j = s; j < nload; j += ns) last = j;
+        if (last >= 0) mbar_wait(&bar_load[s], (uint32_t)(last / ns) & 1u, kWaitLimit);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- products ----
+    const uint32_t id = idesc_bf16(g.mrows, P, false, false);
+    const uint32_t lbo_b = (uint32_t)P * 16u;
+    int nmma = 0;
+    bool ok = true;
+    for (int j = 0; j < nj; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_load[j % ns], (uint32_t)(j / ns) & 1u, d.wlim));
+      if (ok && j >= kReadBufs)
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_read[j % kReadBufs], (uint32_t)(j / kReadBufs - 1) & 1u, d.wlim));
+      if (!ok) break;
+      if (lane == 0) {
+        fence_after_sync();
+        const uint32_t a0 = smem_u32(stages + (size_t)(j % ns) * stage_bytes);
+        const uint32_t b0 = a0 + g.o_w;
+        const uint32_t acc = tbase + (uint32_t)(j % kReadBufs) * g.ncols;
+        for (int part = 0; part < 2; ++part)
+          for (int ks = 0; ks < r / 16; ++ks)
+            mma_bf16(acc, sdesc(a0 + 2u * g.grp * ks, g.grp, 128u),
+                     sdesc(b0 + (uint32_t)part * (uint32_t)(P * r * 2) + 2u * lbo_b * ks, lbo_b, 128u), id,
+                     part > 0 || ks > 0);
+        mma_commit(&bar_mma[j % kReadBufs]);
+      }
+      __syncwarp();
+      nmma = j + 1;
+    }
+    if (!ok && lane == 0) atomicExch(&err, 1);
+    if (lane == 0) {   // every product has completed before the CTA leaves (bounded)
+      for (int s = 0; s < kReadBufs; ++s) {
+        int last = -1;
+        for (int j = s; j < nmma; j += kReadBufs) last = j;
+        if (last >= 0) mbar_wait(&bar_mma[s], (uint32_t)(last / kReadBufs) & 1u, kWaitLimit);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue ----
+    const int qd = warp & 3;
+    const int m = g.mrows == 64 ? 16 * qd + lane : 32 * qd + lane;
+    const bool lane_ok = g.mrows == 128 || lane < 16;
+    for (int j = 0; j < nj; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar_mma[j % kReadBufs], (uint32_t)(j / kReadBufs) & 1u, d.wlim))) {
+        if (lane == 0) atomicExch(&err, 1);
+        break;
+      }
+      fence_after_sync();
+      if (warp == 2 && lane == 0) mbar_arrive(&bar_free[j % ns]);   // the products have read the stage
+      const long long q = chunk_of(j);
+      const int c = (int)(q % d.C);
+      const long long bh = q / d.C;
+      const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+      const int t = c * CS + m;
+      const bool live = lane_ok && m < CS && t < T;
+      const uint32_t ta = tbase + (uint32_t)(j % kReadBufs) * g.ncols + ((uint32_t)(32 * qd) << 16);
+      for (int j0 = 0; j0 < P; j0 += 16) {
+        float x[16];
+        tmem_ld16(ta + (uint32_t)j0, x);
+        if (live) store_y16(y, b, t, h, j0, x, y32);
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_read[j % kReadBufs]);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (err) {   // poison this CTA's chunks
+    const float nan = __int_as_float(0x7fc00000);
+    float xn[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) xn[e] = nan;
+    for (int j = 0; j < nj; ++j) {
+      const long long q = chunk_of(j);
+      const int c = (int)(q % d.C);
+      const long long bh = q / d.C;
+      const int h = (int)(bh % d.H), b = (int)(bh / d.H);
+      for (int m = tid; m < CS; m += kReadPsThreads) {
+        const int t = c * CS + m;
+        if (t < T)
+          for (int j0 = 0; j0 < P; j0 += 16) store_y16(y, b, t, h, j0, xn, y32);
+      }
+      if (tid == 0) status[q] |= 1 << 2;
+    }
+  }
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, kReadBufs * g.ncols);
   }
 }
 
@@ -1370,16 +1556,33 @@ bool readout_tc_ok(const Dims& d, const In& zq, const Out& y) {
   return s8(y.st, d.T) && s8(y.sh, d.H) && s8(y.sb, d.B) && read_geom(d.r, d.P, d.CS).smem <= 227u * 1024u - 64u;
 }
 
-cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, int* status,
-                              cudaStream_t st) {
+cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, bool y32,
+                              int* status, cudaStream_t st) {
   CUtensorMap mq;
   const ReadGeom g = read_geom(d.r, d.P, d.CS);
   if (!token_map(&mq, zq, d.B, d.T, d.H, d.r, d.CS)) return cudaErrorInvalidValue;
+  // persistent CTAs, two per SM, when at least two stages fit in half an SM's shared memory
+  // and the TMEM buffers of two CTAs fit the SM's 512 columns
+  const uint32_t stage = up128(g.o_w + g.wbytes);
+  const int ns = (int)std::min<size_t>(kReadStagesMax, (100u * 1024u - 128u) / stage);
+  if (ns >= 2 && 2u * kReadBufs * g.ncols <= kTmemCols) {
+    // no third CTA on an SM: its TMEM allocation would wait for a whole other CTA
+    const size_t smem = tmem_safe_smem(kReadBufs * g.ncols, kReadPsThreads, (size_t)ns * stage + 128);
+    cudaError_t e = cudaFuncSetAttribute(k_readout_ps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    const long long n = (long long)d.B * d.H * d.C;
+    const unsigned grid = (unsigned)std::min<long long>(n, 2LL * sms);
+    k_readout_ps<<<grid, kReadPsThreads, smem, st>>>(mq, d, g, stage, ns, wm, y, y32, status);
+    return cudaGetLastError();
+  }
   const size_t smem = tmem_safe_smem(g.ncols, kReadThreads, g.smem);
   cudaError_t e = cudaFuncSetAttribute(k_readout_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const long long n = (long long)d.B * d.H * d.C;
-  k_readout_tc<<<(unsigned)n, kReadThreads, smem, st>>>(mq, d, g, wm, y, status);
+  k_readout_tc<<<(unsigned)n, kReadThreads, smem, st>>>(mq, d, g, wm, y, y32, status);
   return cudaGetLastError();
 }
 

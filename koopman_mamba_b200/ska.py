@@ -76,17 +76,30 @@ def _stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def _core_fwd(z, zq, v, g32, params: _Params):
-    """ska_fwd on caller-owned tensors; returns (y, saved, saved_bytes, scratch_bytes)."""
+def _y32_ok(z, v, params: _Params) -> bool:
+    """bf16 z, zq, v whose layout reaches the tensor-core readout, which can write an
+    fp32 y (SKA_DTYPE_BF16_Y32)."""
+    if z.dtype != torch.bfloat16:
+        return False
+    shape = _shape(z, v, params)
+    mask = _lib.lib().ska_kernel_path(ctypes.byref(shape), _lib.SKA_DTYPE_BF16, ctypes.byref(_tensor_desc(z)),
+                                      ctypes.byref(_tensor_desc(v)))
+    return mask >= 0 and bool(mask & _lib.SKA_PATH_TC_READOUT_FWD)
+
+
+def _core_fwd(z, zq, v, g32, params: _Params, y32: bool = False):
+    """ska_fwd on caller-owned tensors; returns (y, saved, saved_bytes, scratch_bytes).
+    y32: bf16 inputs with an fp32 y (the caller checked _y32_ok)."""
     dev = z.device
     shape = _shape(z, v, params)
     saved_bytes, scratch_bytes = _lib.workspace_size(shape)
     B, T, H, _ = z.shape
-    y = torch.empty((B, T, H, v.shape[-1]), dtype=z.dtype, device=dev)
+    y = torch.empty((B, T, H, v.shape[-1]), dtype=torch.float32 if y32 else z.dtype, device=dev)
     saved = torch.empty(max(saved_bytes, 1), dtype=torch.uint8, device=dev)
     dz_, dzq_, dv_, dy_ = (_tensor_desc(t) for t in (z, zq, v, y))
+    io = _lib.SKA_DTYPE_BF16_Y32 if y32 else _DTYPES[z.dtype]
     with torch.cuda.device(dev):
-        rc = _lib.lib().ska_fwd(ctypes.byref(shape), _DTYPES[z.dtype], ctypes.byref(dz_),
+        rc = _lib.lib().ska_fwd(ctypes.byref(shape), io, ctypes.byref(dz_),
                                 ctypes.byref(dzq_), ctypes.byref(dv_), ctypes.c_void_p(g32.data_ptr()),
                                 ctypes.byref(dy_), ctypes.c_void_p(saved.data_ptr()), saved_bytes,
                                 ctypes.c_void_p(_stream_ptr(dev)))
@@ -172,7 +185,11 @@ class ProjectedSkaFunction(torch.autograd.Function):
         z, zq, v = _split_proj(proj, H, r, P)
         _check_inputs(z, zq, v, gamma)
         g32 = _gamma32(gamma, x.device)
-        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params)
+        # fp32 hidden states with bf16 projections (autocast): the reference keeps the
+        # core's output in fp32 (ska.py:436-458), so y is written in fp32 where the
+        # tensor-core readout allows it
+        y32 = x.dtype == torch.float32 and proj.dtype == torch.bfloat16 and _y32_ok(z, v, params)
+        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params, y32)
         ctx.params, ctx.hrp = params, (H, r, P)
         ctx.gamma_dtype, ctx.gamma_shape = gamma.dtype, gamma.shape
         ctx.save_for_backward(x, w, proj, g32, saved)

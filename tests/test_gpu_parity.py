@@ -402,3 +402,42 @@ def test_module_fused_projection_matches_separate_projections():
     assert rel_fro(out.detach().cpu().numpy(), out2.detach().cpu().numpy()) <= 1e-5
     for a, b in zip(g1, g2):
         assert rel_fro(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("r,P,chunk", [(32, 64, 64), (64, 64, 128), (16, 32, 64)])
+def test_bf16_inputs_fp32_y(r, P, chunk):
+    """SKA_DTYPE_BF16_Y32: bf16 z, zq, v with an fp32 y (the autocast setting of the
+    reference module).  Everything after the bf16 inputs is fp32-level, so y meets
+    the fp32 bar against the oracle on the same bf16-rounded inputs; the bf16-y run
+    agrees with it to bf16 rounding.  A layout that does not reach the tensor-core
+    readout (r = 20) is refused."""
+    import ctypes
+    from koopman_mamba_b200 import _lib
+    B, T, H = 2, 300, 3
+    z, zq, v = _inputs(B, T, H, r, P, 80 + r, dy=False)
+    t = [torch.as_tensor(a).to(DEV, torch.bfloat16) for a in (z, zq, v)]
+    shape = _lib.make_shape(B, T, H, r, P, chunk, 2, 1e-3)
+    saved_bytes, _ = _lib.workspace_size(shape)
+    saved = torch.empty(saved_bytes, dtype=torch.uint8, device=DEV)
+    g = torch.tensor(1.1, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    d = lambda x: _lib.SkaTensor(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2))   # noqa: E731
+    outs = {}
+    for code, dt in ((_lib.SKA_DTYPE_BF16_Y32, torch.float32), (_lib.SKA_DTYPE_BF16, torch.bfloat16)):
+        y = torch.empty(B, T, H, P, dtype=dt, device=DEV)
+        _lib.check("ska_fwd", _lib.lib().ska_fwd(ctypes.byref(shape), code, *[ctypes.byref(d(x)) for x in t],
+                                                 ctypes.c_void_p(g.data_ptr()), ctypes.byref(d(y)),
+                                                 ctypes.c_void_p(saved.data_ptr()), saved_bytes, stream))
+        torch.cuda.synchronize()
+        outs[dt] = y.double().cpu().numpy()
+    ref, _ = ska_core_forward(z, zq, v, 1.1, SkaParams(chunk_size=chunk))
+    assert rel_fro(outs[torch.float32], ref) <= FP32_TOL
+    assert rel_fro(outs[torch.bfloat16], outs[torch.float32]) <= 4e-3
+    # no tensor-core readout for r = 20: refused, nothing launched
+    s20 = _lib.make_shape(B, T, H, 20, P, chunk, 2, 1e-3)
+    z20 = torch.zeros(B, T, H, 20, dtype=torch.bfloat16, device=DEV)
+    y = torch.empty(B, T, H, P, dtype=torch.float32, device=DEV)
+    rc = _lib.lib().ska_fwd(ctypes.byref(s20), _lib.SKA_DTYPE_BF16_Y32, ctypes.byref(d(z20)), ctypes.byref(d(z20)),
+                            ctypes.byref(d(t[2])), ctypes.c_void_p(g.data_ptr()), ctypes.byref(d(y)),
+                            ctypes.c_void_p(saved.data_ptr()), saved_bytes, stream)
+    assert rc == _lib.SKA_ERR_UNSUPPORTED
