@@ -437,7 +437,9 @@ def test_bf16_inputs_fp32_y(r, P, chunk):
     s20 = _lib.make_shape(B, T, H, 20, P, chunk, 2, 1e-3)
     z20 = torch.zeros(B, T, H, 20, dtype=torch.bfloat16, device=DEV)
     y = torch.empty(B, T, H, P, dtype=torch.float32, device=DEV)
+    sb20, _ = _lib.workspace_size(s20)
+    saved20 = torch.empty(sb20, dtype=torch.uint8, device=DEV)
     rc = _lib.lib().ska_fwd(ctypes.byref(s20), _lib.SKA_DTYPE_BF16_Y32, ctypes.byref(d(z20)), ctypes.byref(d(z20)),
                             ctypes.byref(d(t[2])), ctypes.c_void_p(g.data_ptr()), ctypes.byref(d(y)),
-                            ctypes.c_void_p(saved.data_ptr()), saved_bytes, stream)
+                            ctypes.c_void_p(saved20.data_ptr()), sb20, stream)
     assert rc == _lib.SKA_ERR_UNSUPPORTED
