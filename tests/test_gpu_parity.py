@@ -333,13 +333,14 @@ def test_module_under_bf16_autocast_against_reference_fixture():
     bf16-rounded projections (tests/golden/module_small_bf16proj.npz, fp64
     elsewhere): output, dx and every weight gradient within the bf16 bar.
 
-    d(eta) is a dot product of ~51K cancelling terms, <d(eta y), y>, whose value
-    under autocast depends on where the bf16 GEMM of out_proj's backward rounds:
-    the reference's own autocast epilogue (d(eta y) = bf16(dout W_o)) moves it by
-    ~5% from its fp64 value on this fixture.  It is therefore checked against that
-    epilogue, emulated here on the CPU from the oracle's y_hat; the remaining
-    difference is this core's bf16 rounding of y_hat, which the reference does not
-    make."""
+    d(eta) is the dot product <d(eta y), y> of ~51K terms that cancel (on this
+    fixture their magnitudes sum to thousands of times the result), so under
+    autocast its value is set by where the bf16 GEMM of out_proj's backward rounds
+    d(eta y): the reference's own autocast epilogue (d(eta y) = bf16(dout W_o)),
+    emulated here on the CPU from the oracle's y_hat, moves it by ~5% from its fp64
+    value, and any other valid rounding order lands elsewhere in that band.  It is
+    checked against that emulation within three times the rounding-noise scale
+    2^-9 ||d(eta y) * y||_2; the fp32 module test pins d(eta) at 1e-4."""
     d = load("module_small_bf16proj")
     m = SKAModule(int(d["meta_d_model"]), int(d["meta_H"]), rank=int(d["meta_r"]),
                   chunk_size=int(d["meta_CS"])).to(DEV)
@@ -371,9 +372,11 @@ def test_module_under_bf16_autocast_against_reference_fixture():
                             proj[2].reshape(B, T, H, P).numpy(), float(d["sd_ssn_gamma"]),
                             SkaParams(chunk_size=int(d["meta_CS"])))
     g = bf(bf(d["dout"]).numpy() @ bf(d["sd_out_proj.weight"]).numpy())       # bf16(dout W_o)
-    deta_ref_autocast = float((g.numpy() * y.reshape(B, T, H * P)).sum())
-    assert abs(float(m.eta.grad) - deta_ref_autocast) <= BF16_TOL * max(1.0, abs(deta_ref_autocast)), \
-        (float(m.eta.grad), deta_ref_autocast, float(d["grad_eta"]))
+    terms = g.numpy() * y.reshape(B, T, H * P)
+    deta_ref_autocast = float(terms.sum())
+    noise = 2.0 ** -9 * float(np.sqrt((terms ** 2).sum()))
+    assert abs(float(m.eta.grad) - deta_ref_autocast) <= 3.0 * noise, \
+        (float(m.eta.grad), deta_ref_autocast, float(d["grad_eta"]), noise)
 
 
 def test_module_fused_projection_matches_separate_projections():
