@@ -36,6 +36,14 @@ EXPORTED = (
     "ska_prefill_state",
     "ska_step",
 )
+SKA_ERR_NULL = -1
+SKA_ERR_SHAPE = -2
+SKA_ERR_UNSUPPORTED = -3
+SKA_ERR_DTYPE = -4
+SKA_ERR_WORKSPACE = -5
+SKA_ERR_ALIGN = -6
+SKA_ERR_LAUNCH = -7
+SKA_ERR_STRATEGY = -8
 SKA_ERR_TIMEOUT = -9
 SKA_STATUS_BWD_BASE = 16
 SKA_WAIT_LIMIT_DEFAULT = 0xFFFFFFFF
