@@ -445,17 +445,18 @@ __global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict
 // ----------------------------------------------------------------------------
 // segmented scans: one DRAM round trip per record float
 //
-// The chunks of one series are cut into segments of kSegLen consecutive chunks;
-// one thread owns one float4 column of the record in one segment and loads all of
-// its chunks at once.  The G segments of a column sit in G consecutive lanes of
-// one warp (G a power of two <= 32, so C <= 32 * kSegLen), which exchange their
-// segment totals by shuffles:
+// The chunks of one series are cut into G segments of kSegLen consecutive chunks
+// (G a power of two <= 16, so C <= 16 * kSegLen).  A CTA of 32 x G threads takes
+// 32 consecutive float4 columns of the record: lane x = column, warp y = segment,
+// so every load and store instruction of a warp covers 512 contiguous bytes.
+// Each thread loads all of its segment's chunks at once, scans them locally, and
+// the segment totals meet in shared memory:
 //   forward (exclusive):  out[c] = sum_{c' < c} a^(c - 1 - c') x[c']
 //   backward (suffix):    out[c] = sum_{c' > c} a^(c' - c - 1) x[c']
-// (a = decay_alpha for the decay strategy, 1 otherwise), the same sums as
-// k_scan_fwd / k_scan_bwd in one round trip instead of ceil(C / 16).  Only the last
-// segment can be short, and it is never between two others, so the decay factor
-// between segments is a^(kSegLen * gap).
+// (a = decay_alpha for the decay strategy, 1 otherwise): the sums of k_scan_fwd /
+// k_scan_bwd in one round trip instead of ceil(C / 16).  Only the last segment
+// can be short, and it is never between two others, so the decay between
+// segments is a^(kSegLen * gap).
 // ----------------------------------------------------------------------------
 constexpr int kSegLen = 16;
 
@@ -464,20 +465,23 @@ __host__ __device__ inline int seg_count(int C) {
   while (g * kSegLen < C) g <<= 1;
   return g;
 }
-bool seg_scan_ok(const Dims& d) { return (d.SW & 3) == 0 && d.C <= 32 * kSegLen; }
+// G <= 16 (C <= 256): 512 threads at most, so a thread may keep its 16 float4 in registers
+bool seg_scan_ok(const Dims& d) { return (d.SW & 3) == 0 && d.C <= 16 * kSegLen; }
 
 __device__ __forceinline__ float4 f4_fma(float a, float4 x, float4 y) {   // a x + y
   return make_float4(fmaf(a, x.x, y.x), fmaf(a, x.y, y.y), fmaf(a, x.z, y.z), fmaf(a, x.w, y.w));
 }
-__device__ __forceinline__ float4 f4_shfl(float4 v, int src) {
-  return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
-                     __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
-}
 
+// scans column threadIdx.x of the CTA's 32 columns, segment threadIdx.y; `tots`
+// holds 32 x G float4 in shared memory
 template <bool REVERSE>
-__device__ __forceinline__ void seg_scan_column(float* rec0, long long stride, int C, int G, int seg, int lane,
-                                                bool active, int decay, float alpha) {
+__device__ __forceinline__ void seg_scan_column(float* series, long long stride, int ncols, int C, float4* tots,
+                                                int decay, float alpha) {
+  const int G = blockDim.y, seg = threadIdx.y, lane = threadIdx.x;
+  const int col = blockIdx.x * 32 + lane;
+  const bool active = col < ncols;
   const int c0 = seg * kSegLen, n = active ? max(0, min(kSegLen, C - c0)) : 0;
+  float* rec0 = series + 4 * (size_t)(active ? col : 0);
   float4 x[kSegLen];
 #pragma unroll
   for (int k = 0; k < kSegLen; ++k)
@@ -494,75 +498,74 @@ __device__ __forceinline__ void seg_scan_column(float* rec0, long long stride, i
       tot = f4_fma(a, tot, xk);
     }
   }
-  // a^kSegLen: the decay across one whole segment
-  float aL = 1.f;
+  tots[seg * 32 + lane] = tot;
+  __syncthreads();
+  float aL = 1.f;   // a^kSegLen: the decay across one whole segment
 #pragma unroll
   for (int i = 0; i < kSegLen; ++i) aL *= a;
-  // offset of this segment from the segments before it (after it, for REVERSE)
+  // offset from the segments before this one (after it, for REVERSE), nearest first
   float4 off = make_float4(0.f, 0.f, 0.f, 0.f);
-  const int base = lane - seg;   // lane of segment 0 of this column
+  float w = 1.f;
   for (int j = 1; j < G; ++j) {
-    // walking outward: forward takes segment seg - j, reverse seg + j
     const int src = REVERSE ? seg + j : seg - j;
-    const float4 t = f4_shfl(tot, base + (src & (G - 1)));
-    float w = 1.f;
-    for (int q = 1; q < j; ++q) w *= aL;        // a^(kSegLen * (j - 1))
-    if (src >= 0 && src < G) off = f4_fma(w, t, off);
+    if (src < 0 || src >= G) break;
+    off = f4_fma(w, tots[src * 32 + lane], off);
+    w *= aL;
   }
-  // out[c] = local[c] + a^(distance to the segment edge) off
+  // out[c] = local[c] + a^(distance to the segment's edge) off
 #pragma unroll
   for (int i = 0; i < kSegLen; ++i) {
     const int k = REVERSE ? kSegLen - 1 - i : i;
     if (k < n) {
-      float w = 1.f;   // forward: a^k; reverse: a^(kSegLen - 1 - k) (full segments only reach here with offsets)
+      float wk = 1.f;
       const int e = REVERSE ? (kSegLen - 1 - k) : k;
-      for (int q = 0; q < e; ++q) w *= a;
-      *reinterpret_cast<float4*>(rec0 + (long long)(c0 + k) * stride) = f4_fma(w, off, x[k]);
+      for (int q = 0; q < e; ++q) wk *= a;
+      *reinterpret_cast<float4*>(rec0 + (long long)(c0 + k) * stride) = f4_fma(wk, off, x[k]);
     }
   }
 }
 
-// grid (ceil(SW / 4 * G / 256), B * H); thread: column (SW / 4 of them) x segment
-__global__ void __launch_bounds__(kThreads) k_scan_seg_fwd(Dims d, float* __restrict__ stats) {
-  const int G = seg_count(d.C), lane = threadIdx.x & 31;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int col = (int)(t / G), seg = (int)(t % G);
-  const bool active = col < (d.SW >> 2);
-  float* rec0 = stats + (size_t)blockIdx.y * d.C * d.SW + 4 * (active ? col : 0);
-  seg_scan_column<false>(rec0, d.SW, d.C, G, seg, lane, active, d.decay, d.alpha);
+// grid (ceil(SW / 4 / 32), B * H), block (32, G)
+__global__ void __launch_bounds__(512) k_scan_seg_fwd(Dims d, float* __restrict__ stats) {
+  __shared__ float4 tots[32 * 16];
+  seg_scan_column<false>(stats + (size_t)blockIdx.y * d.C * d.SW, d.SW, d.SW >> 2, d.C, tots, d.decay, d.alpha);
 }
 
-__global__ void __launch_bounds__(kThreads) k_scan_seg_bwd(Dims d, float* __restrict__ dstats,
-                                                           const float* __restrict__ dmpart,
-                                                           const float* __restrict__ dgpart,
-                                                           float* __restrict__ dm, float* __restrict__ dgamma) {
+// sum over a (32, blockDim.y) block; every thread receives the total
+__device__ float block_sum_2d(float x, float* red) {
+  x = warp_sum(x);
+  __syncthreads();
+  if (threadIdx.x == 0) red[threadIdx.y] = x;
+  __syncthreads();
+  return warp_sum(threadIdx.x < blockDim.y ? red[threadIdx.x] : 0.f);
+}
+
+__global__ void __launch_bounds__(512) k_scan_seg_bwd(Dims d, float* __restrict__ dstats,
+                                                       const float* __restrict__ dmpart,
+                                                       const float* __restrict__ dgpart,
+                                                       float* __restrict__ dm, float* __restrict__ dgamma) {
+  __shared__ float4 tots[32 * 16];
   __shared__ float red[32];
-  const int G = seg_count(d.C), lane = threadIdx.x & 31;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int col = (int)(t / G), seg = (int)(t % G);
-  const bool active = col < (d.SW >> 2);
   const int bh = blockIdx.y;
-  float* rec0 = dstats + (size_t)bh * d.C * d.SW + 4 * (active ? col : 0);
-  seg_scan_column<true>(rec0, d.SW, d.C, G, seg, lane, active, d.decay, d.alpha);
+  seg_scan_column<true>(dstats + (size_t)bh * d.C * d.SW, d.SW, d.SW >> 2, d.C, tots, d.decay, d.alpha);
   if (blockIdx.x == 0) {   // d(max norm) per series, d(gamma) over everything
-    float s = 0.f;
-    for (int c = threadIdx.x; c < d.C; c += blockDim.x) s += dmpart[(size_t)bh * d.C + c];
-    s = block_sum(s, red);
-    if (threadIdx.x == 0) dm[bh] = s;
+    const int tid = threadIdx.y * 32 + threadIdx.x, nt = 32 * blockDim.y;
+    float sum = 0.f;
+    for (int c = tid; c < d.C; c += nt) sum += dmpart[(size_t)bh * d.C + c];
+    sum = block_sum_2d(sum, red);
+    if (tid == 0) dm[bh] = sum;
     if (bh == 0) {
       const size_t n = (size_t)d.B * d.H * d.C;
       float g = 0.f;
-      for (size_t i = threadIdx.x; i < n; i += blockDim.x) g += dgpart[i];
-      g = block_sum(g, red);
-      if (threadIdx.x == 0) *dgamma = g;
+      for (size_t i = tid; i < n; i += nt) g += dgpart[i];
+      g = block_sum_2d(g, red);
+      if (tid == 0) *dgamma = g;
     }
   }
 }
 
-static dim3 seg_grid(const Dims& d) {
-  const long long threads = (long long)(d.SW >> 2) * seg_count(d.C);
-  return dim3((unsigned)((threads + kThreads - 1) / kThreads), d.B * d.H);
-}
+static dim3 seg_grid(const Dims& d) { return dim3((unsigned)(((d.SW >> 2) + 31) / 32), d.B * d.H); }
+static dim3 seg_block(const Dims& d) { return dim3(32, seg_count(d.C)); }
 
 // ----------------------------------------------------------------------------
 // per-chunk operator (shared by forward and backward)
@@ -1164,7 +1167,7 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   prof_record(1, st);
   if (!fused) {
     if (seg_scan_ok(d))
-      k_scan_seg_fwd<<<seg_grid(d), kThreads, 0, st>>>(d, stats);
+      k_scan_seg_fwd<<<seg_grid(d), seg_block(d), 0, st>>>(d, stats);
     else
       k_scan_fwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, stats);
   }
@@ -1243,7 +1246,7 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   }
   prof_record(6, st);
   if (seg_scan_ok(d))
-    k_scan_seg_bwd<<<seg_grid(d), kThreads, 0, st>>>(d, dstats, dmpart, dgpart, dm, dgamma);
+    k_scan_seg_bwd<<<seg_grid(d), seg_block(d), 0, st>>>(d, dstats, dmpart, dgpart, dm, dgamma);
   else
     k_scan_bwd<<<dim3((d.SW + 4 * kThreads - 1) / (4 * kThreads), d.B * d.H), kThreads, 0, st>>>(d, dstats, dmpart, dgpart,
                                                                                      dm, dgamma);
