@@ -446,9 +446,9 @@ __global__ void __launch_bounds__(kThreads) k_scan_bwd(Dims d, float* __restrict
 // segmented scans: one DRAM round trip per record float
 //
 // The chunks of one series are cut into G segments of kSegLen consecutive chunks
-// (G a power of two <= 16, so C <= 16 * kSegLen).  A CTA of 32 x G threads takes
-// 32 consecutive float4 columns of the record: lane x = column, warp y = segment,
-// so every load and store instruction of a warp covers 512 contiguous bytes.
+// (G a power of two <= 16, so C <= 16 * kSegLen).  A CTA takes groups of 32
+// consecutive float4 columns of the record, one warp per (group, segment), lane =
+// column, so every load and store instruction of a warp covers 512 contiguous bytes.
 // Each thread loads all of its segment's chunks at once, scans them locally, and
 // the segment totals meet in shared memory:
 //   forward (exclusive):  out[c] = sum_{c' < c} a^(c - 1 - c') x[c']
@@ -472,13 +472,16 @@ __device__ __forceinline__ float4 f4_fma(float a, float4 x, float4 y) {   // a x
   return make_float4(fmaf(a, x.x, y.x), fmaf(a, x.y, y.y), fmaf(a, x.z, y.z), fmaf(a, x.w, y.w));
 }
 
-// scans column threadIdx.x of the CTA's 32 columns, segment threadIdx.y; `tots`
-// holds 32 x G float4 in shared memory
+// column groups per CTA: 256-thread CTAs for G <= 8 (G = 16: 512 threads)
+__host__ __device__ inline int seg_groups(int G) { return G >= 8 ? 1 : 8 / G; }
+
+// the CTA takes seg_groups(G) groups of 32 consecutive columns; thread (x, y):
+// column x of group y / G, segment y % G; `tots` holds blockDim.y x 32 float4
 template <bool REVERSE>
 __device__ __forceinline__ void seg_scan_column(float* series, long long stride, int ncols, int C, float4* tots,
                                                 int decay, float alpha) {
-  const int G = blockDim.y, seg = threadIdx.y, lane = threadIdx.x;
-  const int col = blockIdx.x * 32 + lane;
+  const int G = seg_count(C), seg = threadIdx.y % G, cg = threadIdx.y / G, lane = threadIdx.x;
+  const int col = (blockIdx.x * seg_groups(G) + cg) * 32 + lane;
   const bool active = col < ncols;
   const int c0 = seg * kSegLen, n = active ? max(0, min(kSegLen, C - c0)) : 0;
   float* rec0 = series + 4 * (size_t)(active ? col : 0);
@@ -498,7 +501,7 @@ __device__ __forceinline__ void seg_scan_column(float* series, long long stride,
       tot = f4_fma(a, tot, xk);
     }
   }
-  tots[seg * 32 + lane] = tot;
+  tots[threadIdx.y * 32 + lane] = tot;
   __syncthreads();
   float aL = 1.f;   // a^kSegLen: the decay across one whole segment
 #pragma unroll
@@ -509,7 +512,7 @@ __device__ __forceinline__ void seg_scan_column(float* series, long long stride,
   for (int j = 1; j < G; ++j) {
     const int src = REVERSE ? seg + j : seg - j;
     if (src < 0 || src >= G) break;
-    off = f4_fma(w, tots[src * 32 + lane], off);
+    off = f4_fma(w, tots[(cg * G + src) * 32 + lane], off);
     w *= aL;
   }
   // out[c] = local[c] + a^(distance to the segment's edge) off
@@ -525,7 +528,7 @@ __device__ __forceinline__ void seg_scan_column(float* series, long long stride,
   }
 }
 
-// grid (ceil(SW / 4 / 32), B * H), block (32, G)
+// grid (ceil(SW / 4 / (32 groups)), B * H), block (32, G * groups)
 __global__ void __launch_bounds__(512) k_scan_seg_fwd(Dims d, float* __restrict__ stats) {
   __shared__ float4 tots[32 * 16];
   seg_scan_column<false>(stats + (size_t)blockIdx.y * d.C * d.SW, d.SW, d.SW >> 2, d.C, tots, d.decay, d.alpha);
@@ -564,8 +567,14 @@ __global__ void __launch_bounds__(512) k_scan_seg_bwd(Dims d, float* __restrict_
   }
 }
 
-static dim3 seg_grid(const Dims& d) { return dim3((unsigned)(((d.SW >> 2) + 31) / 32), d.B * d.H); }
-static dim3 seg_block(const Dims& d) { return dim3(32, seg_count(d.C)); }
+static dim3 seg_grid(const Dims& d) {
+  const int cols_per_cta = 32 * seg_groups(seg_count(d.C));
+  return dim3((unsigned)(((d.SW >> 2) + cols_per_cta - 1) / cols_per_cta), d.B * d.H);
+}
+static dim3 seg_block(const Dims& d) {
+  const int G = seg_count(d.C);
+  return dim3(32, G * seg_groups(G));
+}
 
 // ----------------------------------------------------------------------------
 // per-chunk operator (shared by forward and backward)
