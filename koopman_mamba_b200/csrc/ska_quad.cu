@@ -236,45 +236,47 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   // ---- A0 = Mn S ----
   mul_block(RA, RK, R0, w & 1, w >> 1, im2);
   __syncthreads();
-  // ---- spectral norm (warps 0, 1) ----
+  // ---- spectral norm (warps 0, 1) while warps 2, 3 form A0^K ----
+  // A = kk A0 with kk = clamp(gamma, 1, 1.5) / max(sigma, 1), so A^K = kk^K A0^K:
+  // the power of the unscaled A0 does not wait for sigma, and kk^K goes into the
+  // alpha of the next product.  A0^K ping-pongs between RK (Mn, dead) and R0 (S, dead);
+  // K = 0 gives the identity, K = 1 A0 itself.
+  float* AK = RA;
   if (w < 2) {
     const float sg = power_sigma64(RA, vsh, part, red, r, w, lane);
     if (tid == 0) {
       s_sigma = sg;
-      const float invs = 1.f / fmaxf(sg, 1.f);
-      invs_out[q] = invs;
+      invs_out[q] = 1.f / fmaxf(sg, 1.f);
       flags_out[q] = s_flag;
     }
+  } else if (d.K == 0) {
+    float t[32];
+#pragma unroll 1
+    for (int bi = 0; bi < 2; ++bi) {
+      const int bj = w - 2;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = (bi == bj && j == lane) ? 1.f : 0.f;
+      st_row(blk(RK, bi, bj), lane, t);
+    }
+  } else {
+    const float* prev = RA;
+    for (int s = 1; s < d.K; ++s) {
+      float* out = (prev == RK) ? R0 : RK;
+      const int bj = w - 2;   // warps 2, 3: column block 0, 1 (both row blocks)
+      mul_block(out, const_cast<float*>(prev), RA, 0, bj, 1.f);
+      mul_block(out, const_cast<float*>(prev), RA, 1, bj, 1.f);
+      asm volatile("bar.sync 2, 64;" ::: "memory");   // warps 2, 3: the power is complete
+      prev = out;
+    }
+  }
+  if (d.K == 0) AK = RK;
+  else {
+    for (int s = 1; s < d.K; ++s) AK = (AK == RK) ? R0 : RK;
   }
   __syncthreads();
   const float kk = gs * (1.f / fmaxf(s_sigma, 1.f));     // as the backward forms it from invs
-  {
-    float t[32];
-    float* T = blk(RA, w & 1, w >> 1);
-    ld_row(t, T, lane);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) t[j] *= kk;
-    st_row(T, lane, t);                                    // A
-  }
-  __syncthreads();
-  // ---- A^K: K = 0 identity, K = 1 A itself, else ping-pong RK / R0 ----
-  float* AK = RA;
-  if (d.K == 0) {
-    float t[32];
-    const int bi = w & 1, bj = w >> 1;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) t[j] = (bi == bj && j == lane) ? 1.f : 0.f;
-    st_row(blk(RK, bi, bj), lane, t);
-    AK = RK;
-  } else {
-    for (int s = 1; s < d.K; ++s) {
-      float* out = (AK == RK) ? R0 : RK;
-      mul_block(out, AK, RA, w & 1, w >> 1, 1.f);
-      __syncthreads();
-      AK = out;
-    }
-  }
-  __syncthreads();
+  float kkK = 1.f;
+  for (int s = 0; s < d.K; ++s) kkK *= kk;
   // regions now: RLi = Li, AK in one of {RA, RK, R0}; A (RA) dead unless AK is RA
   float* cand[3] = {R0, RK, RA};
   float* RU = nullptr;
@@ -294,13 +296,13 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
                     r - 32 * bj, lane);
     cp_async_commit();
   }
-  // ---- U = A^K Li (Li block (0, 1) is zero) ----
+  // ---- U = A^K Li = kk^K A0^K Li (Li block (0, 1) is zero) ----
   {
     const int bi = w & 1, bj = w >> 1;
     if (bj == 0)
-      wmmp<false, 32, 64, false, false, false>(blk(RU, bi, 0), blk(AK, bi, 0), 2 * kTile, RLi, 1.f);
+      wmmp<false, 32, 64, false, false, false>(blk(RU, bi, 0), blk(AK, bi, 0), 2 * kTile, RLi, kkK);
     else
-      wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), 1.f);
+      wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), kkK);
   }
   __syncthreads();
   // ---- V = Li^T U (into the A^K region, dead now) ----
