@@ -70,13 +70,19 @@ WORKLOADS = {
 }
 
 
+LM_WORKLOAD = ("hybrid Mamba-2 + SKA LM training step: config_50m_mamba_attn hyper-parameters with its attention "
+               "layers [2, 5, 8] as SKA layers (d_model 448, 12 layers, SKA H=7 r=48 P=64, d_state 128, vocab 32000), "
+               "batch 32 x 2048 tokens per GPU, bf16 autocast, AdamW, DDP with an NCCL gradient all-reduce")
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("c2", "c3"), default="c2")
+    ap.add_argument("--workload", choices=("c2", "c3", "lm"), default="c2",
+                    help="c2 (default, with a c3 block), c3, or lm (the full-model training step of config 4)")
     ap.add_argument("--no-c3", action="store_true", help="skip the c3 block of the default c2 run")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -648,9 +654,91 @@ def measure(key, args, rank, world, local, dev, barrier, max_over_ranks):
     return line
 
 
+def measure_lm(args, rank, world, local, dev, barrier, max_over_ranks):
+    """Config 4: the whole language model's training step (forward, backward with the
+    DDP all-reduce over NCCL, AdamW) on synthetic token ids (uniform over the
+    vocabulary, seed 3 + 1000 * rank).  The Mamba-2 layers are the package's
+    PyTorch stand-in unless mamba_ssm is importable."""
+    import torch
+    from koopman_mamba_b200.lm import HybridLM, Mamba2Mixer, config_50m_mamba_ska
+    B, L = 32, 2048
+    cfg = config_50m_mamba_ska()
+    torch.manual_seed(3)
+    model = HybridLM(cfg).to(dev)
+    mamba_kind = "PyTorch Mamba-2 stand-in (mamba_ssm not installed)" \
+        if any(isinstance(mm, Mamba2Mixer) for mm in model.modules()) else "mamba_ssm.Mamba2"
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], find_unused_parameters=False)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    g = torch.Generator().manual_seed(3 + 1000 * rank)
+    host_ids = torch.randint(0, cfg.vocab_size, (B, L + 1), generator=g).pin_memory()
+    ids = host_ids.to(dev)
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def step(x):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = net(x[:, :-1], x[:, 1:])["loss"]
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    clocks = ClockSampler()
+    clocks.start(local)
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    losses = []
+    for i in range(args.steps):
+        ev0[i].record(stream)
+        losses.append(step(ids))
+        ev1[i].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t1 = time.perf_counter()
+    clock_info = clocks.stop(t0, t1)
+    dev_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ev0, ev1)), dev)
+    tokens = world * B * L
+    # end to end: every step copies its token ids in and its loss out
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ea.record(stream)
+    for _ in range(args.steps):
+        ids.copy_(host_ids, non_blocking=True)
+        loss_host.copy_(step(ids).detach(), non_blocking=True)
+    eb.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(ea.elapsed_time(eb), dev)
+    return {
+        "metric": "hybrid Mamba-2 + SKA LM training tokens/s (config 4)", "value": tokens * args.steps / (dev_ms / 1e3),
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform token ids, seed 3 + 1000*rank)",
+        "config": {"workload": LM_WORKLOAD, "B_per_gpu": B, "L": L, "mamba": mamba_kind,
+                   "parallelism": f"DDP over {world} GPU(s), NCCL all-reduce of the gradients"},
+        "e2e": {"value": tokens * args.steps / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": host_ids.numel() * 8,
+                "d2h_bytes_per_step": 4},
+        "loss_first_last": [float(losses[0]), float(losses[-1])],
+        "max_memory_gb": torch.cuda.max_memory_allocated(dev) / 1e9, "clocks": clock_info,
+        "roofline": None, "cpu_baseline": None, "wall_s": t1 - t0,
+    }
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
+        if args.workload == "lm":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's full model needs mamba_ssm, "
+                              "which is not installed on this machine or the GPU box"}), flush=True)
+            return 0
         return run_reference_arm(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -674,6 +762,18 @@ def main(argv=None):
     def barrier():
         if world > 1:
             dist.barrier()
+
+    if args.workload == "lm":
+        if pool is not None:
+            pool.close()
+            pool.join()
+        line = measure_lm(args, rank, world, local, dev, barrier, max_over_ranks)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
 
     keys = [args.workload] + (["c3"] if args.workload == "c2" and not args.no_c3 else [])
     lines = {}
