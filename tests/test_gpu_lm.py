@@ -53,6 +53,10 @@ def _step(model, opt, ids, labels):
 def test_every_ska_parameter_gets_a_gradient():
     torch.manual_seed(0)
     model = HybridLM(_small_cfg()).to(DEV)
+    with torch.no_grad():   # gamma inside the clamp [1, 1.5] (weight decay would take 1.0 just below it,
+        for layer in model.seq_layers:   # where the clamp passes no gradient, as in the reference)
+            if hasattr(layer, "ska"):
+                layer.ska.ssn_gamma.fill_(1.2)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
     ids, labels = _batch(1)
     _step(model, opt, ids, labels)          # out_proj starts at zero (ska.py:398): one step moves it
