@@ -257,7 +257,7 @@ class HybridLM(nn.Module):
         logits = self.lm_head(self.norm_f(h))
         loss = None
         if labels is not None:
-            loss = F.cross_entropy(logits.view(-1, logits.size(-1)).float(), labels.view(-1), ignore_index=-100)
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), labels.reshape(-1), ignore_index=-100)
         return {"loss": loss, "logits": logits}
 
     def ska_parameters(self):
