@@ -175,7 +175,14 @@ int ska_set_profile_events(void* const* events, int count);
  *                        P <= 64, bf16 with a TC_READOUT_FWD layout) on the
  *                        four-warp kernel (one CTA per chunk, blocked
  *                        Cholesky); otherwise, for r > 32, on the one-CTA
- *                        CUDA-core kernel */
+ *                        CUDA-core kernel
+ *   SKA_PATH_TC_CHUNK_FWD  forward chunk operators for r <= 32 on tcgen05, four
+ *                        chunks per CTA with their r x r products batched into
+ *                        one 128 x 128 product (bf16, WARP_CHUNK and
+ *                        TC_READOUT_FWD); otherwise on the warp-per-chunk kernel
+ *   SKA_PATH_TC_CHUNK_BWD  the backward's chunk operators the same way (bf16,
+ *                        TC_READOUT_BWD, r % 16 == 0, power_K <= 2); otherwise
+ *                        warp per chunk */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
@@ -183,6 +190,8 @@ int ska_set_profile_events(void* const* events, int count);
 #define SKA_PATH_FUSED_SCAN 16
 #define SKA_PATH_TC_READOUT_FWD 32
 #define SKA_PATH_QUAD_CHUNK 64
+#define SKA_PATH_TC_CHUNK_FWD 128
+#define SKA_PATH_TC_CHUNK_BWD 256
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Bounded waits of the tensor-core kernels (no counterpart in the reference,
@@ -197,9 +206,10 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
  *
  * Status entries: int32 [B][H][C] (chunk c of head h of batch b at
  * (b * H + h) * C + c), one array in `saved` (forward: bits 0-1 the statistics
- * kernel, bits 2-3 the readout kernel; each 0 ok, 1 copy wait expired,
- * 2 product wait expired) and one in `scratch` (backward: bits 0-1 the
- * readout-gradient kernel, bits 2-3 the token kernel, coded the same way).
+ * kernel, bits 2-3 the readout kernel, bits 4-5 the tensor-core chunk-operator
+ * kernel; each 0 ok, 1 copy wait expired, 2 product wait expired) and one in `scratch` (backward: bits 0-1 the
+ * readout-gradient kernel, bits 2-3 the token kernel, bits 4-5 the tensor-core
+ * chunk-operator kernel, coded the same way).
  * Layouts without tensor-core kernels write 0.
  *
  * ska_check_status synchronises `stream`, then scans the forward entries of

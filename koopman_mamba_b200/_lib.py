@@ -54,6 +54,8 @@ SKA_PATH_TC_READOUT_BWD = 8
 SKA_PATH_FUSED_SCAN = 16
 SKA_PATH_TC_READOUT_FWD = 32
 SKA_PATH_QUAD_CHUNK = 64
+SKA_PATH_TC_CHUNK_FWD = 128
+SKA_PATH_TC_CHUNK_BWD = 256
 SKA_NOALLOC_SCRATCH_BYTES = 16 << 20
 SKA_PROFILE_EVENTS = 10
 

@@ -22,6 +22,8 @@ size_t smem_bwd_chunk(const Dims&);
 size_t smem_bwd_tok(const Dims&);
 bool warp_path_ok(const Dims&);
 bool quad_path_ok(const Dims&);
+bool ops_tc_ok(const Dims&);
+bool bwd_ops_tc_ok(const Dims&);
 size_t smem_fwd_chunk_w(const Dims&);
 size_t smem_bwd_chunk_w(const Dims&);
 namespace tc {
@@ -167,7 +169,10 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
   }
   if (io_dtype == SKA_DTYPE_BF16) {   // y assumed laid out like v
     const ska::Out yv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
-    if (ska::fwd_tc_readout<__nv_bfloat16>(d, iz, yv)) mask |= SKA_PATH_TC_READOUT_FWD;
+    if (ska::fwd_tc_readout<__nv_bfloat16>(d, iz, yv)) {
+      mask |= SKA_PATH_TC_READOUT_FWD;
+      if (ska::warp_path_ok(d) && ska::ops_tc_ok(d)) mask |= SKA_PATH_TC_CHUNK_FWD;
+    }
   }
   if (io_dtype == SKA_DTYPE_BF16) {   // gradients and zq, dy assumed laid out like z and v
     const ska::Out gz{const_cast<void*>(iz.p), iz.sb, iz.st, iz.sh}, gv{const_cast<void*>(iv.p), iv.sb, iv.st, iv.sh};
@@ -175,6 +180,7 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
     ska::bwd_tc_paths<__nv_bfloat16>(d, iz, iz, iv, iv, gz, gz, gv, &full, &tok);
     if (tok) mask |= SKA_PATH_TC_TOKEN_BWD;
     if (full) mask |= SKA_PATH_TC_READOUT_BWD;
+    if (full && ska::bwd_ops_tc_ok(d)) mask |= SKA_PATH_TC_CHUNK_BWD;
   }
   return mask;
 }

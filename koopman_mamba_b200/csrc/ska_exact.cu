@@ -1093,6 +1093,10 @@ cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* 
 cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                                const float* invs, const float* ops, const float* dwraw, float* dstats,
                                float* dmpart, float* dgpart, cudaStream_t st);
+bool bwd_ops_tc_ok(const Dims& d);
+cudaError_t launch_bwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                              const float* invs, const float* ops, const float* dwraw, float* dstats, float* dmpart,
+                              float* dgpart, int* status, cudaStream_t st);
 
 // Which backward kernels run (bf16 token tensors with TMA-compatible layouts):
 //   full: dW' and dzq on tcgen05, chunk operators without a token pass (r <= 32)
@@ -1128,6 +1132,9 @@ bool tc_stats_path(const Dims& d, const In& z, const In& v) {
 template bool tc_stats_path<float>(const Dims&, const In&, const In&);
 template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 
+bool ops_tc_ok(const Dims& d);
+cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                              float* invs, int* flags, float* ops, unsigned char* wm, int* status, cudaStream_t st);
 bool quad_path_ok(const Dims& d);
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                                float* invs, int* flags, unsigned char* wm, cudaStream_t st);
@@ -1189,9 +1196,14 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
     float* ops = keep ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
     unsigned char* wm = keep ? reinterpret_cast<unsigned char*>(saved + L.wm) : nullptr;
     tc_read = fwd_tc_readout<IO>(d, zq, y);
-    const Out ychunk = tc_read ? Out{nullptr, 0, 0, 0} : y;
-    if ((e = launch_fwd_chunk_w<IO>(d, zq, gamma, ychunk, stats, cmax, invs, flags, ops, wm, st)) != cudaSuccess)
-      return e;
+    if (keep && tc_read && ops_tc_ok(d)) {   // four chunks per CTA on tcgen05
+      e = launch_fwd_ops_tc(d, gamma, stats, cmax, invs, flags, ops, wm, reinterpret_cast<int*>(saved + L.status),
+                            st);
+    } else {
+      const Out ychunk = tc_read ? Out{nullptr, 0, 0, 0} : y;
+      e = launch_fwd_chunk_w<IO>(d, zq, gamma, ychunk, stats, cmax, invs, flags, ops, wm, st);
+    }
+    if (e != cudaSuccess) return e;
   } else if (fwd_tc_readout<IO>(d, zq, y)) {   // 32 < r <= 64: four-warp operators, tensor-core readout
     tc_read = true;
     if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, reinterpret_cast<unsigned char*>(saved + L.wm),
@@ -1243,8 +1255,10 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if (full && (e = tc::launch_dw_tc(d, zq, dy, dw, status, st)) != cudaSuccess) return e;
   prof_record(5, st);
   if (full) {
-    if ((e = launch_bwd_chunk_s(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st)) != cudaSuccess)
-      return e;
+    // four chunks per CTA on tcgen05 (r % 16 == 0, power_K <= 2), else warp per chunk
+    e = bwd_ops_tc_ok(d) ? launch_bwd_ops_tc(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, status, st)
+                         : launch_bwd_chunk_s(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st);
+    if (e != cudaSuccess) return e;
   } else if (warp_path_ok(d)) {
     if ((e = launch_bwd_chunk_w<IO>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart, dgpart,
                                     st)) != cudaSuccess)

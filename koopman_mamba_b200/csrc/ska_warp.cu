@@ -318,11 +318,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
   const int flag = factor_and_invert(d, rec, lane, im2, false, T0, T1, pre);   // T1 = Li
   if (lane == 0) flags_out[q] = flag;
   float* opq = ops_out ? ops_out + q * (long long)(kNumOps * kOpFloats) : nullptr;
-  if (opq) store_mat(opq + kOpLi * kOpFloats, T1, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<true>(opq + kOpLi * kOpFloats, T1, lane);   // kept as Li^T
   wmmp<kFast, 32, 32, true, false, false>(T2, T1, kTile, T1, 1.f);        // T2 = S = Li^T Li
   cp_async_wait<0>();                                                     // M and C have landed
   __syncwarp();
-  if (opq) store_mat(opq + kOpS * kOpFloats, T2, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<false>(opq + kOpS * kOpFloats, T2, lane);
   const float* TM = TW;                                                   // M (raw): A0 = (M / m^2) S
   if (!pre_mc) {
     load_mat(T0, rec + r * r, r, r, 1.f, lane);
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     st_row(T3, lane, a);                                                  // T3 = A
   }
   __syncwarp();
-  if (opq) store_mat(opq + kOpA * kOpFloats, T3, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<false>(opq + kOpA * kOpFloats, T3, lane);
   // A^K (K = 0: identity), ping-pong in T0 / T2
   const float* AK = T3;
   if (d.K == 0) {
@@ -358,12 +358,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
     AK = out;
   }
   __syncwarp();
-  if (opq) store_mat(opq + kOpAK * kOpFloats, AK, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<false>(opq + kOpAK * kOpFloats, AK, lane);
   float* TU = (AK == T0) ? T2 : T0;
   float* TV = (d.K == 1) ? T2 : T3;
   wmmp<kFast, 32, 32, false, false, false>(TU, AK, kTile, T1, 1.f);       // U = A^K Li
   __syncwarp();
-  if (opq) store_mat(opq + kOpU * kOpFloats, TU, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<false>(opq + kOpU * kOpFloats, TU, lane);
   wmmp<kFast, 32, 32, true, false, false>(TV, T1, kTile, TU, 1.f);        // V = Li^T U
   if (!pre_mc) {
 #pragma unroll
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, c
       load_mat(TC + pb * kTile, rec + 2 * r * r + pb * 32 * r, P - pb * 32, r, 1.f, lane);   // C rows
   }
   __syncwarp();
-  if (opq) store_mat(opq + kOpV * kOpFloats, TV, 32, 32, 1.f, lane);
+  if (opq) store_op_tile<false>(opq + kOpV * kOpFloats, TV, lane);
   wmmp<kFast, 32 * NPB, 32, false, false, false>(TW, TC, kTile, TV, im2);  // W / m = (C / m) V / m
   __syncwarp();
   if (wm_out && (r & 7) == 0) {
@@ -725,8 +725,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   const int r = d.r, P = d.P;
   extern __shared__ float4 sm4[];
   float* base = reinterpret_cast<float*>(sm4) + (size_t)w * kBwdStreamTiles * kTile;
-  float* TLi = base;
-  float* TA = TLi + kTile;
+  float* TLt = base;             // Li^T (the operator is kept transposed)
+  float* TA = TLt + kTile;
   float* TAK = TA + kTile;
   float* TV = TAK + kTile;
   float* TX = TV + kTile;       // dV
@@ -738,13 +738,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   const float* dwq = dwraw + q * (long long)P * r;
   const float* crec = rec + 2 * r * r;
   // group 0: V and the first P block of C and dW'; group 1: Li, A, A^K
-  fetch_tile(TV, opq + kOpV * kOpFloats, 32, 32, lane);
+  cp_op_async(TV, opq + kOpV * kOpFloats, lane);
   fetch_tile(TP0, crec, min(32, P), r, lane);
   fetch_tile(TP1, dwq, min(32, P), r, lane);
   cp_async_commit();
-  fetch_tile(TLi, opq + kOpLi * kOpFloats, 32, 32, lane);
-  fetch_tile(TA, opq + kOpA * kOpFloats, 32, 32, lane);
-  fetch_tile(TAK, opq + kOpAK * kOpFloats, 32, 32, lane);
+  cp_op_async(TLt, opq + kOpLi * kOpFloats, lane);
+  cp_op_async(TA, opq + kOpA * kOpFloats, lane);
+  cp_op_async(TAK, opq + kOpAK * kOpFloats, lane);
   cp_async_commit();
   const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
   const float gam = *gamma_p;
@@ -791,21 +791,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) dmq = fmaf(t[j], u[j], dmq);
   __syncwarp();
   // V is dead: U -> TY, S -> TP1 (group 2)
-  fetch_tile(TY, opq + kOpU * kOpFloats, 32, 32, lane);
-  fetch_tile(TP1, opq + kOpS * kOpFloats, 32, 32, lane);
+  cp_op_async(TY, opq + kOpU * kOpFloats, lane);
+  cp_op_async(TP1, opq + kOpS * kOpFloats, lane);
   cp_async_commit();
   cp_async_wait<1>();                                     // Li, A, A^K have landed
   __syncwarp();
-  // live: TLi, TA, TAK, TX (dV); U, S in flight
+  // live: TLt, TA, TAK, TX (dV); U, S in flight
   float* TdU = TV;
   float* TdLi = TP0;
-  wmmp<false, 32, 32, false, false, false>(TdU, TLi, kTile, TX, 1.f);      // dU = Li dV
+  wmmp<false, 32, 32, true, false, false>(TdU, TLt, kTile, TX, 1.f);       // dU = Li dV
   cp_async_wait<0>();
   __syncwarp();
   wmmp<false, 32, 32, false, true, false>(TdLi, TY, kTile, TX, 1.f);       // dLi = U dV^T
   __syncwarp();
   float* TdAK = TX;                                                       // dV is dead
-  wmmp<false, 32, 32, false, true, false>(TdAK, TdU, kTile, TLi, 1.f);     // dAK = dU Li^T
+  wmmp<false, 32, 32, false, false, false>(TdAK, TdU, kTile, TLt, 1.f);    // dAK = dU Li^T
   wmmp<false, 32, 32, true, false, true>(TdLi, TAK, kTile, TdU, 1.f);      // dLi += AK^T dU
   __syncwarp();
   // dA from dAK; free: TY (U), TV (dU), TAK
@@ -877,7 +877,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] += u[j];                              // (dS + dS^T) row
   st_row(TdMn, lane, t);
   __syncwarp();
-  wmmp<false, 32, 32, false, false, true>(TdLi, TLi, kTile, TdMn, 1.f);    // dLi += Li (dS + dS^T)
+  wmmp<false, 32, 32, true, false, true>(TdLi, TLt, kTile, TdMn, 1.f);     // dLi += Li (dS + dS^T)
   __syncwarp();
   ld_row(t, TdLi, lane);
 #pragma unroll
@@ -885,7 +885,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
     if (j > lane) t[j] = 0.f;                                             // only tril(dLi) reaches L
   st_row(TdLi, lane, t);
   __syncwarp();
-  wmmp<false, 32, 32, false, true, false>(TS, TdLi, kTile, TLi, -1.f);     // -dLi Li^T (S is dead)
+  wmmp<false, 32, 32, false, false, false>(TS, TdLi, kTile, TLt, -1.f);    // -dLi Li^T (S is dead)
   __syncwarp();
   ld_row(t, TS, lane);
 #pragma unroll
@@ -899,9 +899,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32) k_bwd_chunk_s(Dims d, const fl
   for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((j <= lane) ? t[j] : u[j]);   // (Pm + tril(Pm,-1)^T) / 2
   st_row(TdS, lane, t);
   __syncwarp();
-  wmmp<false, 32, 32, false, false, false>(TdMn, TdS, kTile, TLi, 1.f);    // T1 = P' Li
+  wmmp<false, 32, 32, false, true, false>(TdMn, TdS, kTile, TLt, 1.f);     // T1 = P' Li
   __syncwarp();
-  wmmp<false, 32, 32, true, false, false>(TdS, TLi, kTile, TdMn, 1.f);     // dGn = Li^T T1
+  wmmp<false, 32, 32, false, false, false>(TdS, TLt, kTile, TdMn, 1.f);    // dGn = Li^T T1
   __syncwarp();
   ld_row(t, TdS, lane);
   ld_col<32>(u, TdS, lane);

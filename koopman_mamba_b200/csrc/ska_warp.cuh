@@ -167,6 +167,50 @@ __device__ __forceinline__ bool chol_inv32(float (&g)[32], float (&x)[32], int l
   return true;
 }
 
+// chol_inv32 with the column broadcasts through 32 floats of the warp's shared
+// memory (cb, 16-byte aligned) instead of shuffles: at step j each lane stores its
+// entry of column j and every lane reads the whole column back as 8 broadcast
+// loads, so that a step costs one store, eight loads and the FMAs (the shuffle
+// version issues 31 - j shuffles per step, and twelve or more warps per SM doing
+// that saturate the shuffle unit).  Same results and return value as chol_inv32,
+// up to the rounding of the fused scale.
+__device__ __forceinline__ bool chol_inv32_bc(float (&g)[32], float (&x)[32], float* cb, int lane) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.f : 0.f;
+  const float4* cb4 = reinterpret_cast<const float4*>(cb);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    cb[lane] = g[j];
+    __syncwarp();
+    float c[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 v = cb4[q];
+      c[4 * q] = v.x;
+      c[4 * q + 1] = v.y;
+      c[4 * q + 2] = v.z;
+      c[4 * q + 3] = v.w;
+    }
+    __syncwarp();
+    const float djj = c[j];
+    if (!(djj > 0.f)) return false;
+    const float rs = rsqrtf(djj);                      // 1 / L[j][j]
+    const float lij = lane > j ? g[j] * rs : (lane == j ? djj * rs : 0.f);
+    g[j] = lij;
+    x[j] *= rs;                                        // Li[j][lane] is final
+    const float lr = lij * rs, xr = x[j] * rs;         // L[k][j] = c[k] rs
+#pragma unroll
+    for (int k = j + 1; k < 32; ++k) {
+      g[k] = fmaf(-lr, c[k], g[k]);
+      x[k] = fmaf(-xr, c[k], x[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k)
+    if (k > lane) g[k] = 0.f;
+  return true;
+}
+
 // one halving step of the butterfly reduce-scatter: keep half N of the live
 // entries t[0..2N), exchange the other half with lane ^ OFF
 template <int N, int OFF>
@@ -315,6 +359,31 @@ __device__ __forceinline__ bool cp_tile_async(float* T, const float* src, int nr
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(s), "r"(ok ? 16 : 0) : "memory");
   }
   return true;
+}
+// Kept chunk operators (32 x 32 fp32) are stored column-quad-major: element
+// (i, j) at ((j / 4) * 32 + i) * 4 + j % 4, so that lanes that own rows move 512
+// contiguous bytes per warp instruction.
+// tile T (TRANS: its transpose) -> an operator; synchronise the warp before
+template <bool TRANS>
+static __device__ __noinline__ void store_op_tile(float* dst, const float* T, int lane) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float4 x;
+    if (TRANS)
+      x = make_float4(T[swz(4 * k, lane)], T[swz(4 * k + 1, lane)], T[swz(4 * k + 2, lane)], T[swz(4 * k + 3, lane)]);
+    else
+      x = reinterpret_cast<const float4*>(T + lane * 32)[k ^ (lane & 7)];
+    d4[k * 32 + lane] = x;
+  }
+}
+// an operator -> tile T by cp.async (part of the lane's next commit group)
+__device__ __forceinline__ void cp_op_async(float* T, const float* src, int lane) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(T + lane * 32 + ((k ^ (lane & 7)) << 2)));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + (k * 32 + lane) * 4) : "memory");
+  }
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>

@@ -97,6 +97,7 @@ def test_fwd_validation_before_any_cuda_call(built_lib):
 
 TC = _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD
 RD = _lib.SKA_PATH_TC_READOUT_FWD
+OPS = _lib.SKA_PATH_TC_CHUNK_FWD | _lib.SKA_PATH_TC_CHUNK_BWD   # r <= 32 chunk operators on tcgen05
 
 
 def _contig(base, B, T, H, D):
@@ -104,11 +105,11 @@ def _contig(base, B, T, H, D):
 
 
 @pytest.mark.parametrize("kw,dtype,zt,want", [
-    # config 2 in bf16, contiguous: every tensor-core kernel + warp chunk operators,
-    # statistics and scan fused (96 series)
-    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD),
+    # config 2 in bf16, contiguous: every tensor-core kernel (chunk operators four per
+    # CTA on tcgen05), statistics and scan fused (96 series)
+    (dict(), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD | OPS),
     # too few series to occupy the SMs one CTA per series: statistics and scan apart
-    (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
+    (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD | OPS),
     # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
     # r = 64 (config 3): tensor-core token kernels and readout, four-warp forward
@@ -122,14 +123,14 @@ def _contig(base, B, T, H, D):
     # P % 16 != 0: tensor-core statistics only
     (dict(P=40), 1, None, _lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_FUSED_SCAN),
     # r = 16 (config 5): every tensor-core kernel but the fused statistics + scan
-    (dict(r=16), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
+    (dict(r=16), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD | OPS),
     # r = 16, P = 32 (config 5's head): the same
-    (dict(r=16, P=32), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD),
+    (dict(r=16, P=32), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD | OPS),
     # token stride not a multiple of 16 bytes: CUDA-core token kernels
     (dict(), 1, _lib.SkaTensor(0x1000, 2048 * 12 * 36, 12 * 36, 36), _lib.SKA_PATH_WARP_CHUNK),
     # decay strategy shares the token kernels and the fused statistics + scan
     (dict(strategy=_lib.SKA_STRATEGY_DECAY, decay_alpha=0.9), 1, None,
-     TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD),
+     TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_FUSED_SCAN | RD | OPS),
 ])
 def test_kernel_path_selection(built_lib, kw, dtype, zt, want):
     s = _shape(**kw)

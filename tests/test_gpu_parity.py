@@ -198,7 +198,8 @@ def test_config2_takes_the_tensor_core_statistics_kernel():
     v = torch.empty(8, 2048, 12, 64, dtype=torch.bfloat16, device=DEV)
     assert _path(z, v, 32, 64) == (_lib.SKA_PATH_TC_STATS | _lib.SKA_PATH_TC_TOKEN_BWD |
                                    _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD |
-                                   _lib.SKA_PATH_FUSED_SCAN | _lib.SKA_PATH_TC_READOUT_FWD)
+                                   _lib.SKA_PATH_FUSED_SCAN | _lib.SKA_PATH_TC_READOUT_FWD |
+                                   _lib.SKA_PATH_TC_CHUNK_FWD | _lib.SKA_PATH_TC_CHUNK_BWD)
 
 
 @pytest.mark.parametrize("alpha", [None, 0.9])

@@ -104,8 +104,10 @@ def test_forward_wait_expiry_is_reported_and_recoverable(B, H):
     p.fwd()
     rc, bad, code = p.status(bwd=False)
     assert rc == _lib.SKA_ERR_TIMEOUT
-    # bits 0-1: the statistics kernel, bits 2-3: the tensor-core readout kernel
-    assert bad == 0 and (code & 3) in (1, 2) and (code >> 2) in (0, 1, 2)
+    # bits 0-1: the statistics kernel, bits 2-3: the tensor-core readout kernel,
+    # bits 4-5: the tensor-core chunk-operator kernel (a product wait: 2)
+    assert bad == 0 and (code & 3) in (1, 2) and ((code >> 2) & 3) in (0, 1, 2)
+    assert (code >> 4) == (2 if p.path() & _lib.SKA_PATH_TC_CHUNK_FWD else 0)
     assert torch.isnan(p.y.float()).any()
 
     p.L.ska_set_wait_limit(_lib.SKA_WAIT_LIMIT_DEFAULT)
@@ -129,6 +131,8 @@ def test_backward_wait_expiry_is_reported_and_recoverable():
     rc, bad, code = p.status()
     assert rc == _lib.SKA_ERR_TIMEOUT
     assert bad == 0 and code > _lib.SKA_STATUS_BWD_BASE
+    # bits 4-5: the tensor-core chunk-operator kernel (a product wait: 2)
+    assert ((code - _lib.SKA_STATUS_BWD_BASE) >> 4) == (2 if p.path() & _lib.SKA_PATH_TC_CHUNK_BWD else 0)
     for t in (p.dz, p.dzq, p.dv):
         assert torch.isnan(t.float()).any()
 
