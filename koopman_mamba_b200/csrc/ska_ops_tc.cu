@@ -605,7 +605,7 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
                                                                float* __restrict__ dmpart,
                                                                float* __restrict__ dgpart, int* __restrict__ status) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar, bar2;   // products into R0 (thread 0) and into R1 (thread 32)
   __shared__ uint32_t tmem_slot;
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const long long nq = (long long)d.B * d.H * d.C;
@@ -622,6 +622,7 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
   if (w == 0) tc::tmem_alloc(&tmem_slot, kBwdCols);
   if (tid == 0) {
     tc::mbar_init(&bar, 1);
+    tc::mbar_init(&bar2, 1);
     tc::mbar_fence_init();
   }
   tc::fence_before_sync();
@@ -633,7 +634,7 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
   const float gs = fminf(fmaxf(gam, 1.f), 1.5f);
   const bool gpass = gam >= 1.f && gam <= 1.5f;       // the clamp passes gradients inclusively
   const int npb = (P + 31) >> 5;
-  uint32_t phase = 0;
+  uint32_t phase = 0, phase2 = 0;
 
 #pragma unroll 1
   for (long long gi = blockIdx.x; gi < ngroups; gi += gridDim.x) {
@@ -647,9 +648,12 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     RowLd cl, dl;                                       // block 0's C and dW' rows
     row_issue(cl, crec, lane, P, r);
     row_issue(dl, dwq, lane, P, r);
-    if (gi + gridDim.x < ngroups) {
-      const long long qn = (gi + gridDim.x) * 4 + w;
-      bwd_prefetch(d, stats, ops, dwraw, qn < nq ? qn : nq - 1, lane);
+    if (gi + gridDim.x < ngroups) {   // what the next group's first step reads: V, the C rows, dW'
+      long long qn = (gi + gridDim.x) * 4 + w;
+      qn = qn < nq ? qn : nq - 1;
+      prefetch_l2(ops + qn * (long long)(kNumOps * kOpFloats) + kOpV * kOpFloats, kOpFloats * 4, lane);
+      prefetch_l2(stats + qn * d.SW + 2 * r * r, P * r * 4, lane);
+      prefetch_l2(dwraw + qn * (long long)P * r, P * r * 4, lane);
     }
     bool ok = true;
     const ChunkId id = wpc::chunk_id(d, q);
@@ -673,8 +677,11 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
       if (tid == 0) {
         tc::fence_after_sync();
         mma3(R0, aX, true, aY, true, 128, pb > 0);
-        mma3(R1, aZ, false, aW, false, 128, false);
         tc::mma_commit(&bar);
+      } else if (tid == 32) {
+        tc::fence_after_sync();
+        mma3(R1, aZ, false, aW, false, 128, false);
+        tc::mma_commit(&bar2);
       }
       if (pb + 1 < npb) {
         row_issue(cl, crec + (pb + 1) * 32 * r, lane, P - 32 * (pb + 1), r);
@@ -684,6 +691,7 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
         ld_op_row(u, opq + kOpU * kOpFloats, lane);     //   and U
       }
       ok &= product_wait(&bar, phase, d.wlim);
+      ok &= product_wait(&bar2, phase2, d.wlim);
       tc::tmem_ld32(R1 + mine, t);                      // TY rows p = 32 pb + lane
       if (valid) st_rec_row(drec + 2 * r * r + pb * 32 * r, t, lane, P - 32 * pb, r, im2);   // dCn / m
       dmc += dot32(t, a1);                              // <TY, C> = m^2 <dCn, Cn>
@@ -702,12 +710,16 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     if (tid == 0) {
       tc::fence_after_sync();
       mma3(R0, aW, true, aY, true, 128, false);
-      mma3(R1, aX, false, aZ, false, 128, false);
       tc::mma_commit(&bar);
+    } else if (tid == 32) {
+      tc::fence_after_sync();
+      mma3(R1, aX, false, aZ, false, 128, false);
+      tc::mma_commit(&bar2);
     }
     ld_op_row(a1, opq + kOpAK * kOpFloats, lane);       // for the next step: A^K
     ld_op_row(a2, opq + kOpA * kOpFloats, lane);        //   and A
     ok &= product_wait(&bar, phase, d.wlim);
+    ok &= product_wait(&bar2, phase2, d.wlim);
     tc::tmem_ld32(R0 + mine, t);                        // dU
     tc::tmem_ld32(R1 + mine, dli);
     // ---- dAK = dU Li^T (R0), dLi += AK^T dU (R1) ----
@@ -718,13 +730,17 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     if (tid == 0) {
       tc::fence_after_sync();
       mma3(R0, aY, false, aW, true, 128, false);
-      mma3(R1, aX, true, aZ, true, 128, false);
       tc::mma_commit(&bar);
+    } else if (tid == 32) {
+      tc::fence_after_sync();
+      mma3(R1, aX, true, aZ, true, 128, false);
+      tc::mma_commit(&bar2);
     }
     ld_op_row(a1, opq + kOpS * kOpFloats, lane);        // for the step after: S
     RowLd ml;
     row_issue(ml, rec + r * r, lane, r, r);             //   and M
     ok &= product_wait(&bar, phase, d.wlim);
+    ok &= product_wait(&bar2, phase2, d.wlim);
     tc::tmem_ld32(R0 + mine, t);                        // dAK
     tc::tmem_ld32(R1 + mine, u);
 #pragma unroll
@@ -758,12 +774,16 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     if (tid == 0) {
       tc::fence_after_sync();
       mma3(R0, aZ, false, aX, true, 128, false);
+      tc::mma_commit(&bar);
+    } else if (tid == 32) {
+      tc::fence_after_sync();
       mma3(R1, aY, true, aW, true, 128, false);
       mma3(R1, aW, true, aY, true, 128, true);
-      tc::mma_commit(&bar);
+      tc::mma_commit(&bar2);
     }
     ld_op_row(a1, opq + kOpLi * kOpFloats, lane);       // for the next steps: Li^T
     ok &= product_wait(&bar, phase, d.wlim);
+    ok &= product_wait(&bar2, phase2, d.wlim);
     tc::tmem_ld32(R0 + mine, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) t[j] *= kk;            // dMn
