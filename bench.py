@@ -58,6 +58,9 @@ if REPO not in sys.path:
 
 METRIC = "SKA fwd+bwd tokens/sec/GPU (L=2048,r=32) and % of HBM roofline at 1/2/4/8 B200"
 METRIC_C3 = "SKA fwd tokens/s, long context (L=32768, r=64), heads split over the GPUs"
+METRICS = {"c2": METRIC, "c3": METRIC_C3,
+           "c4": "SKA fwd+bwd tokens/sec/GPU, the 50M hybrid LM's SKA layer (H=7, r=48)",
+           "c5": "SKA fwd tokens/sec/GPU, the 2-layer recall model's SKA layer (H=4, r=16, P=32)"}
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20   # > 126 MB L2
 
@@ -67,6 +70,13 @@ WORKLOADS = {
     "c3": dict(B=1, H=16, L=32768, P=64, r=64, CS=128, K=2, ridge=1e-3, seed=2, bwd=False, scaling="strong",
                name="ska_core fwd B=1 H=16 (heads split over the GPUs) L=32768 P=64 r=64 chunk=128 K=2 "
                     "ridge=1e-3 bf16 I/O"),
+    # the SKA layers of the two model configurations, as core workloads of their own
+    "c4": dict(B=32, H=7, L=2048, P=64, r=48, CS=64, K=2, ridge=1e-3, seed=3, bwd=True, scaling="weak",
+               name="ska_core fwd+bwd, the SKA layer of the 50M hybrid LM: B=32/GPU H=7 L=2048 P=64 r=48 "
+                    "chunk=64 K=2 ridge=1e-3 bf16 I/O"),
+    "c5": dict(B=256, H=4, L=1024, P=32, r=16, CS=64, K=2, ridge=1e-3, seed=4, bwd=False, scaling="weak",
+               name="ska_core fwd, the SKA layer of the 2-layer recall model: B=256/GPU H=4 L=1024 P=32 r=16 "
+                    "chunk=64 K=2 ridge=1e-3 bf16 I/O"),
 }
 
 
@@ -81,7 +91,7 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("c2", "c3", "lm"), default="c2",
+    ap.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "lm"), default="c2",
                     help="c2 (default, with a c3 block), c3, or lm (the full-model training step of config 4)")
     ap.add_argument("--no-c3", action="store_true", help="skip the c3 block of the default c2 run")
     ap.add_argument("--no-e2e", action="store_true")
@@ -171,12 +181,12 @@ def _make_pool(workers):
 
 
 def cpu_tasks(key):
-    """The whole workload as independent series slices: c2 one batch element per
-    task, c3 one head per task."""
+    """The whole workload as independent series slices: fwd+bwd workloads one batch
+    element per task, forward-only ones one (batch element, head) per task."""
     wl = WORKLOADS[key]
     if wl["bwd"]:
         return [(key, b, 0, wl["H"]) for b in range(wl["B"])]
-    return [(key, 0, h, h + 1) for h in range(wl["H"])]
+    return [(key, b, h, h + 1) for b in range(wl["B"]) for h in range(wl["H"])]
 
 
 def cpu_step(pool, key):
@@ -222,7 +232,7 @@ def run_reference_arm(args):
     total = sum(times)
     value = wl["B"] * wl["L"] * args.steps / total
     line = {
-        "impl": "reference", "metric": METRIC if key == "c2" else METRIC_C3, "value": value, "unit": UNIT,
+        "impl": "reference", "metric": METRICS[key], "value": value, "unit": UNIT,
         "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
@@ -632,7 +642,7 @@ def measure(key, args, rank, world, local, dev, barrier, max_over_ranks):
     run.check_status()
     launches = len(names)
     line = {
-        "metric": METRIC if key == "c2" else METRIC_C3, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": METRICS[key], "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": wl["scaling"],
         "vs_baseline": None, "dtype": "bf16",

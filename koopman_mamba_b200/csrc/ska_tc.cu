@@ -825,10 +825,11 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
     mbar_wait(&bar_load, 0, kWaitLimit);
   }
 
-  // warp 0 issues the dZ and dV products, warp 1 (at the same time) the dZQ product
-  // into its own TMEM columns; each commits to its own barrier
+  // warp 0 issues the dZ product, warp 1 (at the same time) the dV and dZQ products
+  // into their own TMEM columns (one thread issues a tcgen05.mma about every 70
+  // cycles whatever its shape); each commits to its own barrier
   if (warp < 2) {   // one lane issues; the rest of the warp waits converged
-    if (st == 0 && lane == 0 && (warp == 0 || dzq_on)) {
+    if (st == 0 && lane == 0) {
       fence_after_sync();
       const uint32_t a0 = smem_u32(tile), ay = smem_u32(tile + dyg);
       // A operand (tokens x features, K-major) for K step ks: 8-feature groups grp apart
@@ -843,12 +844,12 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
         if (warp == 0) {
           for (int ks = 0; ks < kz; ++ks)
             mma_bf16(tbase, tok_adesc(a0, ks), sdesc(bz0 + 2u * lbo_z * ks, lbo_z, 128u), idz, part > 0 || ks > 0);
+        } else {
           for (int ks = 0; ks < kv; ++ks)
             mma_bf16(tbase + (uint32_t)r, tok_adesc(a0, ks), sdesc(bv0 + 2u * lbo_v * ks, lbo_v, 128u), idv,
                      part > 0 || ks > 0);
-        } else {
           // W / m MN-major: k-groups (8 p) 128 B apart, n-groups (8 j) P * 16 B apart
-          for (int ks = 0; ks < kq; ++ks)
+          for (int ks = 0; dzq_on && ks < kq; ++ks)
             mma_bf16(tbase + (uint32_t)(r + P), tok_adesc(ay, ks), sdesc(bw0 + 256u * ks, 128u, (uint32_t)P * 16u),
                      idq, part > 0 || ks > 0);
         }
@@ -888,10 +889,10 @@ __global__ void __launch_bounds__(kTokThreads, 2) k_tok_bwd_tc(const __grid_cons
       if (lane == 0) corr[i] = a;
     }
   }
-  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim) && (!dzq_on || mbar_wait(&bar_mmq, 0, d.wlim)))) {
+  if (st == 0 && !__syncthreads_and(mbar_wait(&bar_mma, 0, d.wlim) && mbar_wait(&bar_mmq, 0, d.wlim))) {
     st = 2;
     mbar_wait(&bar_mma, 0, kWaitLimit);
-    if (dzq_on) mbar_wait(&bar_mmq, 0, kWaitLimit);
+    mbar_wait(&bar_mmq, 0, kWaitLimit);
   }
   __syncthreads();
   fence_after_sync();
