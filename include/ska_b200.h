@@ -113,10 +113,21 @@ const char* ska_status_string(int code);
  * backward's scratch buffer.  Either output pointer may be NULL. */
 int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scratch_bytes);
 
+/* Bytes of the saved buffer for a forward that no ska_bwd will follow
+ * (inference, prefill; no counterpart in the reference, whose autograd keeps
+ * what it keeps).  It is the leading part of ska_workspace_size's saved_bytes:
+ * statistics, norms and the readout operands, without the chunk operators
+ * (Li, A, A^K, U, V, S) that the bf16 backward reads.  ska_fwd given at least
+ * this but fewer than saved_bytes does not write those operators; ska_bwd
+ * checks saved_bytes >= ska_workspace_size's and must be given the buffer of a
+ * forward that was given that many. */
+int ska_forward_workspace_size(const SkaShape* shape, size_t* saved_bytes);
+
 /* Forward.  Replaces ska.py:436-457 between the projections and eta:
  *   y = SKA_core(z, zq, v; ssn_gamma)   (y in io_dtype, [B,T,H,P]).
- * `saved` must hold ska_workspace_size(...).saved_bytes; its contents are
- * consumed by ska_bwd for the same inputs. */
+ * `saved` must hold ska_workspace_size(...).saved_bytes when ska_bwd will
+ * follow (its contents are consumed by ska_bwd for the same inputs), else at
+ * least ska_forward_workspace_size(...) bytes. */
 int ska_fwd(const SkaShape* shape, int io_dtype,
             const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
             const float* gamma, const SkaTensor* y,
@@ -182,7 +193,12 @@ int ska_set_profile_events(void* const* events, int count);
  *                        TC_READOUT_FWD); otherwise on the warp-per-chunk kernel
  *   SKA_PATH_TC_CHUNK_BWD  the backward's chunk operators the same way (bf16,
  *                        TC_READOUT_BWD, r % 16 == 0, power_K <= 2); otherwise
- *                        warp per chunk */
+ *                        warp per chunk
+ *   SKA_PATH_QUAD_CHUNK_BWD  the backward's chunk operators for 32 < r <= 64 on
+ *                        four warps per chunk from the operators the forward
+ *                        kept (QUAD_CHUNK shapes with TC_READOUT_BWD and
+ *                        power_K <= 2); otherwise one CTA per chunk that
+ *                        recomputes the forward */
 #define SKA_PATH_TC_STATS 1
 #define SKA_PATH_WARP_CHUNK 2
 #define SKA_PATH_TC_TOKEN_BWD 4
@@ -192,6 +208,7 @@ int ska_set_profile_events(void* const* events, int count);
 #define SKA_PATH_QUAD_CHUNK 64
 #define SKA_PATH_TC_CHUNK_FWD 128
 #define SKA_PATH_TC_CHUNK_BWD 256
+#define SKA_PATH_QUAD_CHUNK_BWD 512
 int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v);
 
 /* Bounded waits of the tensor-core kernels (no counterpart in the reference,
@@ -251,7 +268,8 @@ int ska_state_init(const SkaShape* shape, void* state, size_t state_bytes, void*
  * `saved` buffer that ska_fwd wrote for the same shape, z and v: the exclusive
  * prefix statistics of the last chunk plus that chunk's own tokens (the rest of
  * the prompt is not read again), scaled by the forward's max key norm, which
- * becomes the state's max_norm; z_last = z[T-1] / max_norm. */
+ * becomes the state's max_norm; z_last = z[T-1] / max_norm.  saved_bytes >=
+ * ska_forward_workspace_size(...). */
 int ska_prefill_state(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* v,
                       const void* saved, size_t saved_bytes, void* state, size_t state_bytes, void* stream);
 
@@ -273,7 +291,7 @@ int ska_step(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaT
  * the process exits.  It serves callers that cannot call cudaMalloc: FFI hosts
  * with no CUDA allocator of their own, and inference loops that must not
  * allocate between launches (cudaMalloc can synchronise the device).
- *   - Problems whose ska_workspace_size saved_bytes exceed
+ *   - Problems whose ska_forward_workspace_size exceeds
  *     SKA_NOALLOC_SCRATCH_BYTES return SKA_ERR_WORKSPACE and launch nothing.
  *     The checks run in this order: the shape (as ska_workspace_size), then
  *     the size against the array, then everything ska_fwd checks (dtype,

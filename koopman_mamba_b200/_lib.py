@@ -24,6 +24,7 @@ EXPORTED = (
     "ska_abi_version",
     "ska_status_string",
     "ska_workspace_size",
+    "ska_forward_workspace_size",
     "ska_fwd",
     "ska_bwd",
     "ska_set_profile_events",
@@ -56,6 +57,7 @@ SKA_PATH_TC_READOUT_FWD = 32
 SKA_PATH_QUAD_CHUNK = 64
 SKA_PATH_TC_CHUNK_FWD = 128
 SKA_PATH_TC_CHUNK_BWD = 256
+SKA_PATH_QUAD_CHUNK_BWD = 512
 SKA_NOALLOC_SCRATCH_BYTES = 16 << 20
 SKA_PROFILE_EVENTS = 10
 
@@ -104,6 +106,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.ska_status_string.restype = ctypes.c_char_p
     L.ska_workspace_size.argtypes = [P(SkaShape), P(ctypes.c_size_t), P(ctypes.c_size_t)]
     L.ska_workspace_size.restype = ctypes.c_int
+    L.ska_forward_workspace_size.argtypes = [P(SkaShape), P(ctypes.c_size_t)]
+    L.ska_forward_workspace_size.restype = ctypes.c_int
     L.ska_fwd.argtypes = [P(SkaShape), ctypes.c_int, P(SkaTensor), P(SkaTensor), P(SkaTensor),
                           ctypes.c_void_p, P(SkaTensor), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
     L.ska_fwd.restype = ctypes.c_int
@@ -174,6 +178,13 @@ def make_shape(B, T, H, r, P, chunk_size, power_K, ridge_eps, strategy=SKA_STRAT
 def state_size(shape: SkaShape) -> int:
     n = ctypes.c_size_t(0)
     check("ska_state_size", lib().ska_state_size(ctypes.byref(shape), ctypes.byref(n)))
+    return int(n.value)
+
+
+def forward_workspace_size(shape: SkaShape) -> int:
+    """Saved-buffer bytes for a forward that no backward follows."""
+    n = ctypes.c_size_t(0)
+    check("ska_forward_workspace_size", lib().ska_forward_workspace_size(ctypes.byref(shape), ctypes.byref(n)))
     return int(n.value)
 
 

@@ -11,7 +11,7 @@
 namespace ska {
 template <typename T>
 cudaError_t launch_fwd(const Dims&, const In&, const In&, const In&, const float*, const Out&,
-                       const SavedLayout&, char*, cudaStream_t, bool);
+                       const SavedLayout&, char*, cudaStream_t, bool, bool);
 template <typename T>
 cudaError_t launch_bwd(const Dims&, const In&, const In&, const In&, const float*, const In&,
                        const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&, const Out&,
@@ -180,7 +180,8 @@ int ska_kernel_path(const SkaShape* shape, int io_dtype, const SkaTensor* z, con
     ska::bwd_tc_paths<__nv_bfloat16>(d, iz, iz, iv, iv, gz, gz, gv, &full, &tok);
     if (tok) mask |= SKA_PATH_TC_TOKEN_BWD;
     if (full) mask |= SKA_PATH_TC_READOUT_BWD;
-    if (full && ska::bwd_ops_tc_ok(d)) mask |= SKA_PATH_TC_CHUNK_BWD;
+    if (full && ska::warp_path_ok(d) && ska::bwd_ops_tc_ok(d)) mask |= SKA_PATH_TC_CHUNK_BWD;
+    if (full && !ska::warp_path_ok(d)) mask |= SKA_PATH_QUAD_CHUNK_BWD;
   }
   return mask;
 }
@@ -249,6 +250,14 @@ int ska_workspace_size(const SkaShape* shape, size_t* saved_bytes, size_t* scrat
   return SKA_OK;
 }
 
+int ska_forward_workspace_size(const SkaShape* shape, size_t* saved_bytes) {
+  Dims d{};
+  const int rc = make_dims(shape, &d);
+  if (rc) return rc;
+  if (saved_bytes) *saved_bytes = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P).fwd;
+  return SKA_OK;
+}
+
 int ska_fwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq, const SkaTensor* v,
             const float* gamma, const SkaTensor* y, void* saved, size_t saved_bytes, void* stream) {
   Dims d{};
@@ -268,14 +277,17 @@ int ska_fwd(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTe
   if (!gamma || !saved) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
   const ska::SavedLayout L = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
-  if (saved_bytes < L.total) return SKA_ERR_WORKSPACE;
+  if (saved_bytes < L.fwd) return SKA_ERR_WORKSPACE;
+  // the chunk operators for the backward are kept only in a buffer of the whole size
+  const bool keep_ops = saved_bytes >= L.total;
   if (y32 && !ska::fwd_tc_readout<__nv_bfloat16>(d, izq, oy)) return SKA_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (io_dtype == SKA_DTYPE_F32)
-    e = ska::launch_fwd<float>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, false);
+    e = ska::launch_fwd<float>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, false, false);
   else
-    e = ska::launch_fwd<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, y32);
+    e = ska::launch_fwd<__nv_bfloat16>(d, iz, izq, iv, gamma, oy, L, static_cast<char*>(saved), st, y32,
+                                       keep_ops);
   return e == cudaSuccess ? SKA_OK : SKA_ERR_LAUNCH;
 }
 
@@ -362,7 +374,7 @@ int ska_prefill_state(const SkaShape* shape, int io_dtype, const SkaTensor* z, c
   if (!saved) return SKA_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(saved) % 256) return SKA_ERR_ALIGN;
   const ska::SavedLayout S = ska::saved_layout(d.B, d.H, d.C, d.SW, d.r, d.P);
-  if (saved_bytes < S.total) return SKA_ERR_WORKSPACE;
+  if (saved_bytes < S.fwd) return SKA_ERR_WORKSPACE;
   const char* sv = static_cast<const char*>(saved);
   const float* stats = reinterpret_cast<const float*>(sv + S.stats);
   const auto* cmax = reinterpret_cast<const unsigned long long*>(sv + S.cmax);

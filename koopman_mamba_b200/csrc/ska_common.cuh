@@ -97,12 +97,22 @@ __device__ __forceinline__ void st_tok(const Out& x, int b, int t, int h, int j,
 
 __host__ __device__ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Chunk operators kept by the warp-path forward (r <= 32) for the backward, one
-// 32 x 32 fp32 row-major tile each (rows and columns past r hold the padding the
-// warp kernels use: identity for Li and S, zero elsewhere, identity for A^K when
-// K = 0):
+// Chunk operators kept by the bf16 forward for the backward.  r <= 32: one 32 x 32
+// fp32 row-major tile each (rows and columns past r hold the padding the warp
+// kernels use: identity for Li and S, zero elsewhere, identity for A^K when K = 0):
 constexpr int kOpLi = 0, kOpA = 1, kOpAK = 2, kOpU = 3, kOpV = 4, kOpS = 5, kNumOps = 6;
 constexpr int kOpFloats = 32 * 32;
+// 32 < r <= 64: one 64 x 64 matrix each, as the four-warp kernels hold it in shared
+// memory (four swizzled 32 x 32 tiles, column-block major), in the order Li, S,
+// A0 = Mn S (unscaled), A0^K (unscaled), U, V
+constexpr int kQOpLi = 0, kQOpS = 1, kQOpA0 = 2, kQOpA0K = 3, kQOpU = 4, kQOpV = 5;
+constexpr int kQOpFloats = 64 * 64;
+
+// (the four-warp kernels take r % 8 == 0 and P <= 64)
+__host__ __device__ constexpr size_t ops_floats_per_chunk(long long r, long long P) {
+  return r <= 32 ? (size_t)kNumOps * kOpFloats
+                 : (r <= 64 && r % 8 == 0 && P <= 64) ? (size_t)kNumOps * kQOpFloats : 0;
+}
 
 struct SavedLayout {
   size_t stats;     // float [B][H][C][SW]  exclusive-scanned raw statistics
@@ -111,11 +121,12 @@ struct SavedLayout {
   size_t flags;     // int   [B][H][C]      bit0: jittered, bit1: jitter failed too
   size_t status;    // int   [B][H][C]      tensor-core statistics kernel: 0 ok,
                     //                      1 TMA wait expired, 2 MMA wait expired
-  size_t ops;       // float [B][H][C][kNumOps][32][32]  (r <= 32 only)
-                    //   Li = L^{-1}, A = gamma' A0 / max(sigma, 1), A^K, U = A^K Li,
-                    //   V = Li^T U, S = Li^T Li (bf16 I/O forwards write them)
   size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the
                     //   tensor-core operand of the readout products
+  size_t fwd;       // bytes a forward needs when no backward reads its buffer
+  size_t ops;       // float [B][H][C][ops_floats_per_chunk(r, P)]: Li = L^{-1}, A, A^K,
+                    //   U = A^K Li, V = Li^T U, S = Li^T Li, written by bf16 forwards
+                    //   given the whole buffer (total bytes) and read by the backward
   size_t total;
 };
 
@@ -136,15 +147,15 @@ __host__ __device__ inline SavedLayout saved_layout(long long B, long long H, lo
                                                    long long r, long long P) {
   SavedLayout L{};
   const size_t n = (size_t)B * H * C;
-  const bool warp_ops = r <= 32;
   size_t off = 0;
   L.stats = off; off = align256(off + n * SW * sizeof(float));
   L.cmax = off;  off = align256(off + n * sizeof(unsigned long long));
   L.invs = off;  off = align256(off + n * sizeof(float));
   L.flags = off; off = align256(off + n * sizeof(int));
   L.status = off; off = align256(off + n * sizeof(int));
-  L.ops = off;   off = align256(off + (warp_ops ? n * kNumOps * kOpFloats * sizeof(float) : 0));
   L.wm = off;    off = align256(off + (r <= 64 ? n * (size_t)P * r * 4 : 0));
+  L.fwd = off;
+  L.ops = off;   off = align256(off + n * ops_floats_per_chunk(r, P) * sizeof(float));
   L.total = off;
   return L;
 }

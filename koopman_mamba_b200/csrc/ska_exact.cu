@@ -1087,6 +1087,7 @@ cudaError_t launch_tok_bwd_tc(const Dims& d, const In& z, const In& v, const In&
 bool dw_tc_ok(const Dims& d, const In& zq, const In& dy);
 cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, int* status, cudaStream_t st);
 bool readout_tc_ok(const Dims& d, const In& zq, const Out& y);
+bool readout_tc_zq_ok(const Dims& d, const In& zq);
 cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, bool y32,
                               int* status, cudaStream_t st);
 }  // namespace tc
@@ -1094,19 +1095,39 @@ cudaError_t launch_bwd_chunk_s(const Dims& d, const float* gamma, const float* s
                                const float* invs, const float* ops, const float* dwraw, float* dstats,
                                float* dmpart, float* dgpart, cudaStream_t st);
 bool bwd_ops_tc_ok(const Dims& d);
+bool quad_bwd_ok(const Dims& d);
+cudaError_t launch_bwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               const float* invs, const float* ops, const float* dwraw, float* dstats, float* dmpart,
+                               float* dgpart, cudaStream_t st);
 cudaError_t launch_bwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                               const float* invs, const float* ops, const float* dwraw, float* dstats, float* dmpart,
                               float* dgpart, int* status, cudaStream_t st);
 
+bool quad_path_ok(const Dims& d);
+
+// bf16 forwards for 32 < r <= 64 that run the four-warp operator kernel (and keep its
+// operators and W / m): the sizes it takes, with a zq the tensor-core readout reads
+template <typename IO>
+bool quad_fwd(const Dims& d, const In& zq) {
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
+    return quad_path_ok(d) && tc::readout_tc_zq_ok(d, zq);
+  } else {
+    return false;
+  }
+}
+
 // Which backward kernels run (bf16 token tensors with TMA-compatible layouts):
-//   full: dW' and dzq on tcgen05, chunk operators without a token pass (r <= 32)
+//   full: dW' and dzq on tcgen05, chunk operators without a token pass, from the
+//         operators the forward kept (r <= 32, or the four-warp shapes with
+//         power_K <= 2)
 //   tok : dz, dv on tcgen05; the chunk kernel does the readout's token pass
 template <typename IO>
 void bwd_tc_paths(const Dims& d, const In& z, const In& zq, const In& v, const In& dy, const Out& dz,
                   const Out& dzq, const Out& dv, bool* full, bool* tok) {
   *full = *tok = false;
   if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
-    *full = warp_path_ok(d) && tc::dw_tc_ok(d, zq, dy) && tc::tok_bwd_tc_ok(d, z, v, dy, dz, dv, dzq, true);
+    const bool ops_kept = warp_path_ok(d) || (quad_fwd<IO>(d, zq) && quad_bwd_ok(d));
+    *full = ops_kept && tc::dw_tc_ok(d, zq, dy) && tc::tok_bwd_tc_ok(d, z, v, dy, dz, dv, dzq, true);
     *tok = *full || tc::tok_bwd_tc_ok(d, z, v, dy, dz, dv, dzq, false);
   }
 }
@@ -1135,9 +1156,8 @@ template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 bool ops_tc_ok(const Dims& d);
 cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                               float* invs, int* flags, float* ops, unsigned char* wm, int* status, cudaStream_t st);
-bool quad_path_ok(const Dims& d);
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               float* invs, int* flags, unsigned char* wm, cudaStream_t st);
+                               float* invs, int* flags, float* ops, unsigned char* wm, cudaStream_t st);
 
 // bf16 tensors on the warp or four-warp path whose zq and y the tensor-core readout
 // can take
@@ -1153,10 +1173,11 @@ template bool fwd_tc_readout<float>(const Dims&, const In&, const Out&);
 template bool fwd_tc_readout<__nv_bfloat16>(const Dims&, const In&, const Out&);
 
 // y32: bf16 inputs with an fp32 y (the tensor-core readout path only; the caller checks
-// fwd_tc_readout first)
+// fwd_tc_readout first).  keep_ops: write the chunk operators the backward reads
+// (the saved buffer has room for them).
 template <typename IO>
 cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, const float* gamma, const Out& y,
-                       const SavedLayout& L, char* saved, cudaStream_t st, bool y32) {
+                       const SavedLayout& L, char* saved, cudaStream_t st, bool y32, bool keep_ops) {
   float* stats = reinterpret_cast<float*>(saved + L.stats);
   unsigned long long* cmax = reinterpret_cast<unsigned long long*>(saved + L.cmax);
   float* invs = reinterpret_cast<float*>(saved + L.invs);
@@ -1190,10 +1211,10 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
   prof_record(2, st);
   bool tc_read = false;   // readout as its own tensor-core kernel
   if (warp_path_ok(d)) {
-    // bf16 forwards keep the chunk operators and W / m for the tensor-core backward
-    // and readout
+    // bf16 forwards write W / m for the tensor-core readout and backward, and keep
+    // the chunk operators for the backward when the buffer has room for them
     const bool keep = std::is_same<IO, __nv_bfloat16>::value;
-    float* ops = keep ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
+    float* ops = keep && keep_ops ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
     unsigned char* wm = keep ? reinterpret_cast<unsigned char*>(saved + L.wm) : nullptr;
     tc_read = fwd_tc_readout<IO>(d, zq, y);
     if (keep && tc_read && ops_tc_ok(d)) {   // four chunks per CTA on tcgen05
@@ -1204,11 +1225,15 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
       e = launch_fwd_chunk_w<IO>(d, zq, gamma, ychunk, stats, cmax, invs, flags, ops, wm, st);
     }
     if (e != cudaSuccess) return e;
-  } else if (fwd_tc_readout<IO>(d, zq, y)) {   // 32 < r <= 64: four-warp operators, tensor-core readout
-    tc_read = true;
-    if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, reinterpret_cast<unsigned char*>(saved + L.wm),
+  } else if (quad_fwd<IO>(d, zq)) {   // 32 < r <= 64: four-warp operators, tensor-core readout
+    float* ops = keep_ops ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
+    if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, ops, reinterpret_cast<unsigned char*>(saved + L.wm),
                                 st)) != cudaSuccess)
       return e;
+    tc_read = fwd_tc_readout<IO>(d, zq, y);
+    // a y the tensor-core readout cannot store: the one-CTA kernel writes it (and
+    // the same invs and flags)
+    if (!tc_read) k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
   } else {
     k_fwd_chunk<IO><<<grid, kThreads, s3, st>>>(d, zq, gamma, y, stats, cmax, invs, flags);
   }
@@ -1255,9 +1280,14 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
   if (full && (e = tc::launch_dw_tc(d, zq, dy, dw, status, st)) != cudaSuccess) return e;
   prof_record(5, st);
   if (full) {
-    // four chunks per CTA on tcgen05 (r % 16 == 0, power_K <= 2), else warp per chunk
-    e = bwd_ops_tc_ok(d) ? launch_bwd_ops_tc(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, status, st)
-                         : launch_bwd_chunk_s(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st);
+    // r <= 32: four chunks per CTA on tcgen05 (r % 16 == 0, power_K <= 2), else warp
+    // per chunk; 32 < r <= 64: four warps per chunk
+    if (!warp_path_ok(d))
+      e = launch_bwd_chunk_q(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st);
+    else if (bwd_ops_tc_ok(d))
+      e = launch_bwd_ops_tc(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, status, st);
+    else
+      e = launch_bwd_chunk_s(d, gamma, stats, cmax, invs, ops, dw, dstats, dmpart, dgpart, st);
     if (e != cudaSuccess) return e;
   } else if (warp_path_ok(d)) {
     if ((e = launch_bwd_chunk_w<IO>(d, zq, dy, gamma, dzq, stats, cmax, invs, flags, dstats, dmpart, dgpart,
@@ -1286,9 +1316,9 @@ cudaError_t launch_bwd(const Dims& d, const In& z, const In& zq, const In& v, co
 }
 
 template cudaError_t launch_fwd<float>(const Dims&, const In&, const In&, const In&, const float*, const Out&,
-                                       const SavedLayout&, char*, cudaStream_t, bool);
+                                       const SavedLayout&, char*, cudaStream_t, bool, bool);
 template cudaError_t launch_fwd<__nv_bfloat16>(const Dims&, const In&, const In&, const In&, const float*,
-                                               const Out&, const SavedLayout&, char*, cudaStream_t, bool);
+                                               const Out&, const SavedLayout&, char*, cudaStream_t, bool, bool);
 template cudaError_t launch_bwd<float>(const Dims&, const In&, const In&, const In&, const float*, const In&,
                                        const SavedLayout&, const char*, const ScratchLayout&, char*, const Out&,
                                        const Out&, const Out&, float*, cudaStream_t);

@@ -37,12 +37,14 @@ void* scratch_on_current_device() {
 
 extern "C" int ska_fwd_noalloc(const SkaShape* shape, int io_dtype, const SkaTensor* z, const SkaTensor* zq,
                                const SkaTensor* v, const float* gamma, const SkaTensor* y, void* stream) {
+  // the forward-only size: no backward reads this array, so the chunk operators
+  // that a backward would need are not written
   size_t need = 0;
-  int rc = ska_workspace_size(shape, &need, nullptr);
+  int rc = ska_forward_workspace_size(shape, &need);
   if (rc != SKA_OK) return rc;
   if (need > SKA_NOALLOC_SCRATCH_BYTES) return SKA_ERR_WORKSPACE;
   if (shape->B == 0) return ska_fwd(shape, io_dtype, z, zq, v, gamma, y, nullptr, 0, stream);
   void* ws = scratch_on_current_device();
   if (!ws) return SKA_ERR_LAUNCH;
-  return ska_fwd(shape, io_dtype, z, zq, v, gamma, y, ws, SKA_NOALLOC_SCRATCH_BYTES, stream);
+  return ska_fwd(shape, io_dtype, z, zq, v, gamma, y, ws, need, stream);
 }

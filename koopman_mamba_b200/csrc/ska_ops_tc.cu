@@ -402,7 +402,9 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     bool ok = true;
     const ChunkId id = wpc::chunk_id(d, q);
     const float* rec = stats + q * d.SW;
-    float* opq = ops_out + q * (long long)(kNumOps * kOpFloats);
+    // operators are kept only when the caller gave the whole saved buffer
+    float* opq = ops_out ? ops_out + q * (long long)(kNumOps * kOpFloats) : nullptr;
+    const bool keep = valid && opq;
     const float m = wpc::series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
     float t[32];
 
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
       // S2's part of this warp (free until C(S) is written) holds the column broadcasts
       const int flag = factor_invert_rows(d, rec, lane, im2, x, reinterpret_cast<float*>(S2 + 2048 * w));
       if (valid && lane == 0) flags_out[q] = flag;
-      if (valid) store_op(opq + kOpLi * kOpFloats, x, lane);
+      if (keep) store_op(opq + kOpLi * kOpFloats, x, lane);
       put_row<false>(S0, w, lane, x);
     }
     operands_ready();
@@ -430,7 +432,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
       put_row<false>(S1, w, lane, mn);                  // R(Mn)
     }
     tc::tmem_ld32(tmine, t);
-    if (valid) store_op(opq + kOpS * kOpFloats, t, lane);
+    if (keep) store_op(opq + kOpS * kOpFloats, t, lane);
     put_row<true>(S2, w, lane, t);                      // C(S): the right operand S
     operands_ready();
     if (tid == 0) {
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     const float kk = gs * invs;                         // ska.py:167-169
 #pragma unroll
     for (int j = 0; j < 32; ++j) t[j] *= kk;
-    if (valid) store_op(opq + kOpA * kOpFloats, t, lane);
+    if (keep) store_op(opq + kOpA * kOpFloats, t, lane);
     put_row_rc(S1, S2, w, lane, t);                     // R(A): left operand; C(A): right operand
     if (d.K == 0) {
 #pragma unroll
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
       tc::tmem_ld32(tmine, t);
       put_row<false>(S1, w, lane, t);
     }
-    if (valid) store_op(opq + kOpAK * kOpFloats, t, lane);
+    if (keep) store_op(opq + kOpAK * kOpFloats, t, lane);
     operands_ready();
     if (tid == 0) {
       tc::fence_after_sync();
@@ -480,7 +482,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     }
     ok &= product_wait(&bar, phase, d.wlim);
     tc::tmem_ld32(tmine, t);
-    if (valid) store_op(opq + kOpU * kOpFloats, t, lane);
+    if (keep) store_op(opq + kOpU * kOpFloats, t, lane);
     put_row<true>(S2, w, lane, t);                      // C(U)
     operands_ready();
     if (tid == 0) {
@@ -498,7 +500,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
       for (int pb = 0; pb < kEarly; ++pb) row_issue(cl[pb], crec + pb * 32 * r, lane, P - 32 * pb, r);
       ok &= product_wait(&bar, phase, d.wlim);
       tc::tmem_ld32(tmine, t);
-      if (valid) store_op(opq + kOpV * kOpFloats, t, lane);
+      if (keep) store_op(opq + kOpV * kOpFloats, t, lane);
       put_row<true>(S0, w, lane, t);                    // C(V): S0 is free once V has landed
       unsigned char* cs = smem + (size_t)(1 + w / kCpg) * kSlot;
 #pragma unroll

@@ -23,7 +23,8 @@
 //   A = clamp(gamma, 1, 1.5) / max(sigma, 1) A0,  A^K,  U = A^K Li,  V = Li^T U
 //   W / m = C V / m^2                            one output block per warp
 // and writes W / m as the bf16 hi / lo planes that k_readout_tc multiplies into
-// the tokens (the readout is not done here).
+// the tokens (the readout is not done here).  Given a kept-operator array, it
+// also copies Li, S, A0, A0^K, U and V out for the backward (k_bwd_chunk_q, below).
 #include "ska_warp.cuh"
 
 namespace ska {
@@ -113,6 +114,15 @@ __device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, fl
   return true;
 }
 
+// tile t of a 64 x 64 region -> the same tile of a kept operator in global memory
+// (verbatim: the backward copies it back as it is), 16 bytes per lane and step
+__device__ __forceinline__ void keep_tile(float* dst, const float* M, int t, int lane) {
+  const float4* s = reinterpret_cast<const float4*>(M + t * kTile);
+  float4* g = reinterpret_cast<float4*>(dst + t * kTile);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) g[32 * k + lane] = s[32 * k + lane];
+}
+
 // A0 = Mn S etc.: out block (bi, bj) = alpha X(bi, :) Y(:, bj) for 64 x 64 X, Y
 __device__ __forceinline__ void mul_block(float* out, float* X, float* Y, int bi, int bj, float alpha) {
   wmmp<false, 32, 64, false, false, false>(blk(out, bi, bj), blk(X, bi, 0), 2 * kTile, Y + bj * 2 * kTile, alpha);
@@ -182,6 +192,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
                                                               const unsigned long long* __restrict__ cmax,
                                                               float* __restrict__ invs_out,
                                                               int* __restrict__ flags_out,
+                                                              float* __restrict__ ops_out,
                                                               unsigned char* __restrict__ wm_out) {
   extern __shared__ float4 sm4[];
   float* R0 = reinterpret_cast<float*>(sm4);   // G, then S, then A^K / U / V / spare
@@ -196,6 +207,8 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   const ChunkId id = chunk_id(d, q);
   const int r = d.r, P = d.P;
   const float* rec = stats + q * d.SW;
+  // kept operators (when the caller keeps them): each warp writes tile w of each
+  float* opq = ops_out ? ops_out + q * (long long)(kNumOps * kQOpFloats) : nullptr;
 
   if (w == 0) fetch_square(R0, rec, r, lane);              // G
   if (w == 1) fetch_square(RK, rec + r * r, r, lane);      // M
@@ -217,6 +230,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     if (lane == 0) s_flag = flag;
   }
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpLi * kQOpFloats, RLi, w, lane);
 
   // ---- S = Li^T Li (block (0, 1) of Li is zero) ----
   {
@@ -233,9 +247,11 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   }
   cp_async_wait<0>();                                      // M (warp 1's copies)
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpS * kQOpFloats, R0, w, lane);
   // ---- A0 = Mn S ----
   mul_block(RA, RK, R0, w & 1, w >> 1, im2);
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpA0 * kQOpFloats, RA, w, lane);
   // ---- spectral norm (warps 0, 1) while warps 2, 3 form A0^K ----
   // A = kk A0 with kk = clamp(gamma, 1, 1.5) / max(sigma, 1), so A^K = kk^K A0^K:
   // the power of the unscaled A0 does not wait for sigma, and kk^K goes into the
@@ -274,6 +290,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     for (int s = 1; s < d.K; ++s) AK = (AK == RK) ? R0 : RK;
   }
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpA0K * kQOpFloats, AK, w, lane);
   const float kk = gs * (1.f / fmaxf(s_sigma, 1.f));     // as the backward forms it from invs
   float kkK = 1.f;
   for (int s = 0; s < d.K; ++s) kkK *= kk;
@@ -305,6 +322,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
       wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), kkK);
   }
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpU * kQOpFloats, RU, w, lane);
   // ---- V = Li^T U (into the A^K region, dead now) ----
   float* RV = AK;
   {
@@ -316,6 +334,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   }
   if (w == 2) cp_async_wait<0>();                          // C
   __syncthreads();
+  if (opq) keep_tile(opq + kQOpV * kQOpFloats, RV, w, lane);
   // ---- W / m = C V / m^2 (into the Li region, dead now), then its bf16 planes ----
   float* RW = RLi;
   for (int t = w; t < 2 * NPB; t += 4) {
@@ -344,6 +363,283 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   }
 }
 
+// ---------------------------------------------------------------------------
+// backward for 32 < r <= 64 without the token pass (bf16 token tensors on the
+// tensor-core path), from the operators the forward kept: one CTA of four warps
+// per chunk, warp w owning output block (w & 1, w >> 1) = tile w of every product.
+//
+// dW' = sum_t dy_t zq_t^T comes from k_dw_tc and dzq from k_tok_bwd_tc (W / m
+// planes), as for r <= 32.  The chain rule through W / m = C V / m^2, V = Li^T U,
+// U = A^K Li, A = kk A0, A0 = Mn S, S = Li^T Li (KLF/koopman_lm/ska.py:136-186
+// differentiated; the same steps as the warp kernel k_bwd_chunk_s):
+//   dV = C^T dW' / m^2, m dCn = dW' V^T
+//   dU = Li dV,          dLi  = U dV^T
+//   dA^K = dU Li^T,      dLi += (A^K)^T dU
+//   dA = dA^K A^T + A^T dA^K (K = 2), dA^K (K = 1), 0 (K = 0)
+//   dMn = kk dA S,  dS = kk Mn^T dA,  dLi += Li (dS + dS^T)
+//   Pm = tril(-tril(dLi) Li^T),  P' = (Pm + tril(Pm, -1)^T) / 2
+//   dGn = sym(Li^T P' Li)
+// with the d(max norm) share -(2 <dGn, Gn> + 2 <dMn, Mn> + <dCn, Cn> + <dQn, Qn>) / m
+// and the d(gamma) share <dA, A> / gamma' (zero outside the clamp).  Seven 64 x 64
+// regions (112 KB, two CTAs per SM); the kept operators arrive by cp.async into
+// regions as they free up.
+// ---------------------------------------------------------------------------
+constexpr int kBwdRegions = 7;
+
+// tile t of a kept operator -> tile t of region M (this lane's next commit group)
+__device__ __forceinline__ void fetch_kept_tile(float* M, const float* src, int t, int lane) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(M + t * kTile + (32 * k + lane) * 4));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + t * kTile + (32 * k + lane) * 4)
+                 : "memory");
+  }
+}
+
+// rows [0, nrows) x columns [0, ncols) of tile T, times scale -> global matrix with
+// row stride ld (16-byte pieces when the layout allows).  Synchronise the warp before.
+__device__ __forceinline__ void store_block(float* dst, int ld, const float* T, int nrows, int ncols, float scale,
+                                            int lane) {
+  if (nrows <= 0 || ncols <= 0) return;
+  if ((ld & 3) == 0 && (ncols & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int f = 32 * k + lane, row = f >> 3, q = f & 7;
+      if (row < nrows && 4 * q < ncols) {
+        const float4 x = reinterpret_cast<const float4*>(T + row * 32)[q ^ (row & 7)];
+        *reinterpret_cast<float4*>(dst + (size_t)row * ld + 4 * q) =
+            make_float4(x.x * scale, x.y * scale, x.z * scale, x.w * scale);
+      }
+    }
+  } else {
+    float v[32];
+    ld_row(v, T, lane);
+    if (lane < nrows) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) dst[(size_t)lane * ld + j] = v[j] * scale;
+    }
+  }
+}
+
+// out block (bi, bj) of 64 x 64 products (alpha folded in; ACC accumulates)
+template <bool ACC>
+__device__ __forceinline__ void mm_nn(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+  wmmp<false, 32, 64, false, false, ACC>(blk(out, bi, bj), blk(const_cast<float*>(X), bi, 0), 2 * kTile,
+                                         Y + bj * 2 * kTile, alpha);   // X Y
+}
+template <bool ACC>
+__device__ __forceinline__ void mm_tn(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+  wmmp<false, 32, 64, true, false, ACC>(blk(out, bi, bj), X + bi * 2 * kTile, kTile, Y + bj * 2 * kTile,
+                                        alpha);                        // X^T Y
+}
+template <bool ACC>
+__device__ __forceinline__ void mm_nt(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+  float* Xm = const_cast<float*>(X);
+  float* Ym = const_cast<float*>(Y);
+  wmmp<false, 32, 32, false, true, ACC>(blk(out, bi, bj), blk(Xm, bi, 0), kTile, blk(Ym, bj, 0), alpha);   // X Y^T
+  wmmp<false, 32, 32, false, true, true>(blk(out, bi, bj), blk(Xm, bi, 1), kTile, blk(Ym, bj, 1), alpha);
+}
+
+// tril of block (bi, bj) of a 64 x 64 matrix, in place, by the warp that owns it
+__device__ __forceinline__ void tril_block(float* M, int bi, int bj, int lane) {
+  float t[32];
+  float* T = blk(M, bi, bj);
+  ld_row(t, T, lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (bi < bj || (bi == bj && j > lane)) t[j] = 0.f;
+  __syncwarp();
+  st_row(T, lane, t);
+}
+
+__device__ __forceinline__ float dot_block(const float* X, const float* Y, int bi, int bj, int lane) {
+  float a[32], b[32];
+  ld_row(a, blk(const_cast<float*>(X), bi, bj), lane);
+  ld_row(b, blk(const_cast<float*>(Y), bi, bj), lane);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s = fmaf(a[j], b[j], s);
+  return s;
+}
+
+__global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const float* __restrict__ gamma_p,
+                                                              const float* __restrict__ stats,
+                                                              const unsigned long long* __restrict__ cmax,
+                                                              const float* __restrict__ invs_in,
+                                                              const float* __restrict__ ops,
+                                                              const float* __restrict__ dwraw,
+                                                              float* __restrict__ dstats,
+                                                              float* __restrict__ dmpart,
+                                                              float* __restrict__ dgpart) {
+  extern __shared__ float4 sm4[];
+  float* R[kBwdRegions];
+#pragma unroll
+  for (int i = 0; i < kBwdRegions; ++i) R[i] = reinterpret_cast<float*>(sm4) + i * kRegion;
+  float* red = reinterpret_cast<float*>(sm4) + kBwdRegions * kRegion;   // 8 floats
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int bi = w & 1, bj = w >> 1;   // this warp's block; its tile index is w
+  const long long q = blockIdx.x;
+  const ChunkId id = chunk_id(d, q);
+  const int r = d.r, P = d.P;
+  const float* rec = stats + q * d.SW;
+  const float* opq = ops + q * (long long)(kNumOps * kQOpFloats);
+  const float* dwq = dwraw + q * (long long)P * r;
+  float* drec = dstats + q * d.SW;
+  const int rows_r = r - 32 * bi, cols_r = r - 32 * bj, rows_p = P - 32 * bi;
+
+  // C -> R0, dW' -> R1, V -> R2 (group 0); Li -> R3, U -> R4 (group 1)
+  fetch_block(blk(R[0], bi, bj), rec + 2 * r * r + (size_t)(32 * bi) * r + 32 * bj, r, rows_p, cols_r, lane);
+  fetch_block(blk(R[1], bi, bj), dwq + (size_t)(32 * bi) * r + 32 * bj, r, rows_p, cols_r, lane);
+  fetch_kept_tile(R[2], opq + kQOpV * kQOpFloats, w, lane);
+  cp_async_commit();
+  fetch_kept_tile(R[3], opq + kQOpLi * kQOpFloats, w, lane);
+  fetch_kept_tile(R[4], opq + kQOpU * kQOpFloats, w, lane);
+  cp_async_commit();
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const float gam = *gamma_p;
+  const float gs = fminf(fmaxf(gam, 1.f), 1.5f);
+  const bool gpass = gam >= 1.f && gam <= 1.5f;       // clamp passes gradients inclusively
+  const float kk = gs * invs_in[q];
+  float kkK = 1.f;
+  for (int s = 0; s < d.K; ++s) kkK *= kk;
+  cp_async_wait<1>();
+  __syncthreads();
+
+  // ---- dV = C^T dW' / m^2 -> R5,  TY = dW' V^T = m dCn -> R6 ----
+  mm_tn<false>(R[5], R[0], R[1], bi, bj, im2);
+  mm_nt<false>(R[6], R[1], R[2], bi, bj, 1.f);
+  __syncwarp();
+  store_block(drec + 2 * r * r + (size_t)(32 * bi) * r + 32 * bj, r, blk(R[6], bi, bj), min(rows_p, 32),
+              min(cols_r, 32), im2, lane);
+  const float dmc = dot_block(R[6], R[0], bi, bj, lane);   // <TY, C> = m^2 <dCn, Cn>
+  const float dmq = dot_block(R[2], R[5], bi, bj, lane);   // <V, dV> = <W, dW> = <dQn, Qn>
+  cp_async_wait<0>();
+  __syncthreads();
+  // free: R0, R1, R2, R6.  A0^K -> R0, A0 -> R1 (group 2)
+  fetch_kept_tile(R[0], opq + kQOpA0K * kQOpFloats, w, lane);
+  fetch_kept_tile(R[1], opq + kQOpA0 * kQOpFloats, w, lane);
+  cp_async_commit();
+
+  // ---- dU = Li dV -> R2,  dLi = U dV^T -> R6 ----
+  mm_nn<false>(R[2], R[3], R[5], bi, bj, 1.f);
+  mm_nt<false>(R[6], R[4], R[5], bi, bj, 1.f);
+  cp_async_wait<0>();
+  __syncthreads();
+  // free: R4 (U), R5 (dV).  S -> R4 (group 3)
+  fetch_kept_tile(R[4], opq + kQOpS * kQOpFloats, w, lane);
+  cp_async_commit();
+
+  // ---- dLi += (A^K)^T dU,  dA^K = dU Li^T -> R5  (A^K = kk^K A0^K) ----
+  mm_tn<true>(R[6], R[0], R[2], bi, bj, kkK);
+  mm_nt<false>(R[5], R[2], R[3], bi, bj, 1.f);
+  cp_async_wait<0>();
+  __syncthreads();
+  // free: R0 (A0^K), R2 (dU).  M -> R0 (group 4)
+  fetch_block(blk(R[0], bi, bj), rec + r * r + (size_t)(32 * bi) * r + 32 * bj, r, rows_r, cols_r, lane);
+  cp_async_commit();
+
+  // ---- dA (A = kk A0) ----
+  float* RdA = R[2];
+  if (d.K >= 2) {
+    // K = 2: dA^K A^T + A^T dA^K
+    mm_nt<false>(R[2], R[5], R[1], bi, bj, kk);
+    mm_tn<true>(R[2], R[1], R[5], bi, bj, kk);
+  } else if (d.K == 1) {
+    RdA = R[5];
+  } else {
+    float t[32];
+    zero(t);
+    st_row(blk(R[2], bi, bj), lane, t);
+  }
+  __syncwarp();
+  const float dg = kk * dot_block(RdA, R[1], bi, bj, lane);   // <dA, A>
+  cp_async_wait<0>();
+  __syncthreads();
+  float* RdS = (RdA == R[5]) ? R[2] : R[5];
+  float* RdMn = R[1];                                          // A0 is dead
+
+  // ---- dMn = kk dA S -> R1,  dS = kk Mn^T dA -> RdS ----
+  mm_nn<false>(RdMn, RdA, R[4], bi, bj, kk);
+  mm_tn<false>(RdS, R[0], RdA, bi, bj, kk * im2);
+  __syncwarp();
+  store_block(drec + r * r + (size_t)(32 * bi) * r + 32 * bj, r, blk(RdMn, bi, bj), min(rows_r, 32), min(cols_r, 32),
+              im2, lane);
+  const float dmm = im2 * dot_block(RdMn, R[0], bi, bj, lane);   // <dMn, Mn>
+  __syncthreads();
+  // free: R0 (M), R1 (dMn), R4 (S), RdA.  G -> R4 (group 5)
+  fetch_block(blk(R[4], bi, bj), rec + (size_t)(32 * bi) * r + 32 * bj, r, rows_r, cols_r, lane);
+  cp_async_commit();
+
+  // ---- dS + dS^T -> R0 ----
+  {
+    float t[32], u[32];
+    ld_row(t, blk(RdS, bi, bj), lane);
+    ld_col<32>(u, blk(RdS, bj, bi), lane);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] += u[j];
+    st_row(blk(R[0], bi, bj), lane, t);
+  }
+  __syncthreads();
+  // ---- dLi += Li (dS + dS^T); only tril(dLi) reaches L ----
+  mm_nn<true>(R[6], R[3], R[0], bi, bj, 1.f);
+  __syncwarp();
+  tril_block(R[6], bi, bj, lane);
+  __syncthreads();
+  // ---- Pm = tril(-dLi Li^T) -> R1 ----
+  mm_nt<false>(R[1], R[6], R[3], bi, bj, -1.f);
+  __syncwarp();
+  tril_block(R[1], bi, bj, lane);
+  __syncthreads();
+  // ---- P' = (Pm + tril(Pm, -1)^T) / 2 -> RdS (dS is dead) ----
+  {
+    float t[32], u[32];
+    ld_row(t, blk(R[1], bi, bj), lane);
+    ld_col<32>(u, blk(R[1], bj, bi), lane);
+    const int I = 32 * bi + lane;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] = 0.5f * ((32 * bj + j <= I) ? t[j] : u[j]);
+    st_row(blk(RdS, bi, bj), lane, t);
+  }
+  __syncthreads();
+  // ---- T1 = P' Li -> R0,  dGn = Li^T T1 -> R1 ----
+  mm_nn<false>(R[0], RdS, R[3], bi, bj, 1.f);
+  cp_async_wait<0>();                                          // G
+  __syncthreads();
+  mm_tn<false>(R[1], R[3], R[0], bi, bj, 1.f);
+  __syncthreads();
+  // ---- sym(dGn) / m^2 -> dstats; <dGn, Gn> ----
+  float dmg = 0.f;
+  {
+    float t[32], u[32], gr[32], gc[32];
+    ld_row(t, blk(R[1], bi, bj), lane);
+    ld_col<32>(u, blk(R[1], bj, bi), lane);
+    ld_row(gr, blk(R[4], bi, bj), lane);
+    ld_col<32>(gc, blk(R[4], bj, bi), lane);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float gsym = 0.5f * (t[j] + u[j]);
+      dmg = fmaf(gsym, 0.5f * (gr[j] + gc[j]) * im2, dmg);
+      t[j] = gsym;
+    }
+    st_row(blk(R[6], bi, bj), lane, t);                        // dLi is dead
+    __syncwarp();
+    store_block(drec + (size_t)(32 * bi) * r + 32 * bj, r, blk(R[6], bi, bj), min(rows_r, 32), min(cols_r, 32), im2,
+                lane);
+  }
+  const float tot = warp_sum32(2.f * dmg + 2.f * dmm + dmc * im2 + dmq);
+  const float dgs = warp_sum32(dg);
+  if (lane == 0) {
+    red[w] = tot;
+    red[4 + w] = dgs;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    dmpart[q] = -((red[0] + red[1]) + (red[2] + red[3])) / m;
+    dgpart[q] = gpass ? ((red[4] + red[5]) + (red[6] + red[7])) / gs : 0.f;
+  }
+}
+
 }  // namespace quad
 
 // 32 < r <= 64, r % 8 == 0, P <= 64: the four-warp chunk operators (readout elsewhere)
@@ -351,8 +647,23 @@ bool quad_path_ok(const Dims& d) { return d.r > 32 && d.r <= 64 && (d.r & 7) == 
 
 size_t smem_fwd_chunk_q(const Dims&) { return (size_t)4 * quad::kRegion * sizeof(float); }
 
+// the four-warp backward from kept operators: power_K <= 2
+bool quad_bwd_ok(const Dims& d) { return quad_path_ok(d) && d.K <= 2; }
+
+cudaError_t launch_bwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
+                               const float* invs, const float* ops, const float* dwraw, float* dstats, float* dmpart,
+                               float* dgpart, cudaStream_t st) {
+  const size_t smem = (size_t)quad::kBwdRegions * quad::kRegion * sizeof(float) + 8 * sizeof(float);
+  const long long n = (long long)d.B * d.H * d.C;
+  cudaError_t e = cudaFuncSetAttribute(quad::k_bwd_chunk_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  quad::k_bwd_chunk_q<<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, ops, dwraw, dstats,
+                                                                  dmpart, dgpart);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               float* invs, int* flags, unsigned char* wm, cudaStream_t st) {
+                               float* invs, int* flags, float* ops, unsigned char* wm, cudaStream_t st) {
   const size_t smem = smem_fwd_chunk_q(d);
   const long long n = (long long)d.B * d.H * d.C;
   cudaError_t e;
@@ -360,12 +671,12 @@ cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* s
     if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
         cudaSuccess)
       return e;
-    quad::k_fwd_chunk_q<1><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, wm);
+    quad::k_fwd_chunk_q<1><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, ops, wm);
   } else {
     if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
         cudaSuccess)
       return e;
-    quad::k_fwd_chunk_q<2><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, wm);
+    quad::k_fwd_chunk_q<2><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, ops, wm);
   }
   return cudaGetLastError();
 }

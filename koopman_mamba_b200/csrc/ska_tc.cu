@@ -1548,13 +1548,18 @@ __global__ void __launch_bounds__(kReadPsThreads, 1) k_readout_ps(const __grid_c
   }
 }
 
-bool readout_tc_ok(const Dims& d, const In& zq, const Out& y) {
+// the readout's conditions on the sizes and on zq (TMA-readable), without y
+bool readout_tc_zq_ok(const Dims& d, const In& zq) {
   if (d.r % 16 != 0 || d.r > 64 || d.P % 16 != 0 || d.P > 128 || d.CS % 16 != 0 || d.CS > 128) return false;
-  const auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (!al(zq.p) || !al(y.p)) return false;
+  if ((reinterpret_cast<uintptr_t>(zq.p) & 15u) != 0) return false;
   if (!stride_ok(zq.st, d.T) || !stride_ok(zq.sh, d.H) || !stride_ok(zq.sb, d.B)) return false;
+  return read_geom(d.r, d.P, d.CS).smem <= 227u * 1024u - 64u;
+}
+
+bool readout_tc_ok(const Dims& d, const In& zq, const Out& y) {
+  if (!readout_tc_zq_ok(d, zq) || (reinterpret_cast<uintptr_t>(y.p) & 15u) != 0) return false;
   const auto s8 = [](long long s, long long extent) { return extent == 1 || s % 8 == 0; };
-  return s8(y.st, d.T) && s8(y.sh, d.H) && s8(y.sb, d.B) && read_geom(d.r, d.P, d.CS).smem <= 227u * 1024u - 64u;
+  return s8(y.st, d.T) && s8(y.sh, d.H) && s8(y.sb, d.B);
 }
 
 cudaError_t launch_readout_tc(const Dims& d, const In& zq, const unsigned char* wm, const Out& y, bool y32,

@@ -276,8 +276,8 @@ __device__ __forceinline__ void store_wm_block(unsigned char* wq, const float* T
   }
 }
 
-// ops_out / wm_out (both or neither): keep the chunk's operators (kOp* tiles) and
-// W / m for the backward (and the tensor-core readout); nullptr = do not keep them.
+// ops_out: keep the chunk's operators (kOp* tiles) for the backward; wm_out: write
+// W / m as the tensor-core readout's operand; nullptr = do not write them.
 template <typename IO, int NPB>
 __global__ void __launch_bounds__(kMaxWarps * 32) k_fwd_chunk_w(Dims d, In zq, const float* __restrict__ gamma_p,
                                                                 Out y, const float* __restrict__ stats,

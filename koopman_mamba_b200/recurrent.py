@@ -110,7 +110,7 @@ def ska_prefill(ska, x):
     z, zq, v = _projections(ska, x)
     dev = z.device
     shape = _shape(ska, B, T)
-    saved_bytes, _ = _lib.workspace_size(shape)
+    saved_bytes = _lib.forward_workspace_size(shape)   # no backward reads this buffer
     saved = torch.empty(max(saved_bytes, 256), dtype=torch.uint8, device=dev)
     y = torch.empty(B, T, ska.H, ska.P, dtype=z.dtype, device=dev)
     g32 = ska.ssn_gamma.detach().reshape(()).float().contiguous()

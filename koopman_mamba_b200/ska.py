@@ -87,12 +87,15 @@ def _y32_ok(z, v, params: _Params) -> bool:
     return mask >= 0 and bool(mask & _lib.SKA_PATH_TC_READOUT_FWD)
 
 
-def _core_fwd(z, zq, v, g32, params: _Params, y32: bool = False):
+def _core_fwd(z, zq, v, g32, params: _Params, y32: bool = False, for_backward: bool = True):
     """ska_fwd on caller-owned tensors; returns (y, saved, saved_bytes, scratch_bytes).
-    y32: bf16 inputs with an fp32 y (the caller checked _y32_ok)."""
+    y32: bf16 inputs with an fp32 y (the caller checked _y32_ok).  for_backward=False:
+    the smaller forward-only saved buffer (no chunk operators kept for ska_bwd)."""
     dev = z.device
     shape = _shape(z, v, params)
     saved_bytes, scratch_bytes = _lib.workspace_size(shape)
+    if not for_backward:
+        saved_bytes = _lib.forward_workspace_size(shape)
     B, T, H, _ = z.shape
     y = torch.empty((B, T, H, v.shape[-1]), dtype=torch.float32 if y32 else z.dtype, device=dev)
     saved = torch.empty(max(saved_bytes, 1), dtype=torch.uint8, device=dev)
@@ -139,7 +142,8 @@ class SkaCoreFunction(torch.autograd.Function):
         _check_inputs(z, zq, v, gamma)
         z, zq, v = (_feature_contiguous(t) for t in (z, zq, v))
         g32 = _gamma32(gamma, z.device)
-        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params)
+        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params,
+                                                                 for_backward=any(ctx.needs_input_grad[:4]))
         ctx.params = params
         ctx.gamma_dtype = gamma.dtype
         ctx.gamma_shape = gamma.shape
@@ -189,7 +193,8 @@ class ProjectedSkaFunction(torch.autograd.Function):
         # core's output in fp32 (ska.py:436-458), so y is written in fp32 where the
         # tensor-core readout allows it
         y32 = x.dtype == torch.float32 and proj.dtype == torch.bfloat16 and _y32_ok(z, v, params)
-        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params, y32)
+        y, saved, ctx.saved_bytes, ctx.scratch_bytes = _core_fwd(z, zq, v, g32, params, y32,
+                                                                 for_backward=any(ctx.needs_input_grad[:3]))
         ctx.params, ctx.hrp = params, (H, r, P)
         ctx.gamma_dtype, ctx.gamma_shape = gamma.dtype, gamma.shape
         ctx.save_for_backward(x, w, proj, g32, saved)

@@ -55,6 +55,20 @@ def test_workspace_size_config2(built_lib):
     assert saved % 256 == 0 and scratch % 256 == 0
 
 
+@pytest.mark.parametrize("r,P,op_floats", [(32, 64, 6 * 32 * 32), (16, 32, 6 * 32 * 32), (48, 64, 6 * 64 * 64),
+                                            (64, 64, 6 * 64 * 64), (48, 96, 0), (36, 64, 0),
+                                            (40, 64, 6 * 64 * 64)])
+def test_forward_workspace_is_the_leading_part(built_lib, r, P, op_floats):
+    # the chunk operators the backward reads sit at the end of the saved buffer: a
+    # forward with no backward after it needs only what comes before them
+    s = _shape(r=r, P=P)
+    saved, _ = _lib.workspace_size(s)
+    fwd = _lib.forward_workspace_size(s)
+    n = 8 * 12 * 32
+    assert fwd % 256 == 0 and fwd >= n * (2 * r * r + P * r) * 4
+    assert saved - fwd == -(-(n * op_floats * 4) // 256) * 256
+
+
 @pytest.mark.parametrize("kw,code", [
     (dict(T=0), -2), (dict(H=0), -2), (dict(r=0), -2), (dict(B=-1), -2), (dict(power_K=-1), -2),
     (dict(chunk_size=0), -2), (dict(r=65), -3), (dict(P=129), -3), (dict(chunk_size=257), -3),
@@ -112,12 +126,15 @@ def _contig(base, B, T, H, D):
     (dict(B=2, H=4), 1, None, TC | _lib.SKA_PATH_WARP_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | RD | OPS),
     # fp32 tensors: CUDA-core token kernels
     (dict(), 0, None, _lib.SKA_PATH_WARP_CHUNK),
-    # r = 64 (config 3): tensor-core token kernels and readout, four-warp forward
-    # chunk operators (the backward keeps the one-CTA operator kernel)
-    (dict(r=64, chunk_size=128), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
-    # r = 48 (the module default): tensor-core statistics, readout and token backward,
-    # four-warp forward operators (the backward keeps the one-CTA operator kernel)
-    (dict(r=48), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
+    # r = 64 (config 3): tensor-core token kernels, readout and readout gradient,
+    # four-warp chunk operators forward and backward
+    (dict(r=64, chunk_size=128), 1, None,
+     TC | RD | _lib.SKA_PATH_QUAD_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_QUAD_CHUNK_BWD),
+    # r = 48 (the module default): the same
+    (dict(r=48), 1, None,
+     TC | RD | _lib.SKA_PATH_QUAD_CHUNK | _lib.SKA_PATH_TC_READOUT_BWD | _lib.SKA_PATH_QUAD_CHUNK_BWD),
+    # power_K = 3 at r = 48: the backward's one-CTA operator kernel recomputes the forward
+    (dict(r=48, power_K=3), 1, None, TC | RD | _lib.SKA_PATH_QUAD_CHUNK),
     # chunk 256: tensor-core statistics only
     (dict(r=64, chunk_size=256), 1, None, _lib.SKA_PATH_TC_STATS),
     # P % 16 != 0: tensor-core statistics only

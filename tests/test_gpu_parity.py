@@ -128,7 +128,11 @@ def test_config3_bf16_forward_all_heads():
 def test_config3_bf16_backward_full_size():
     """Config 3 shape forward + backward through the C ABI (all 16 heads, L=32768,
     r=64, chunk 128), checked against the oracle on 3 heads at full length (the
-    series are independent; the backward runs the one-CTA chunk operators)."""
+    series are independent; the backward runs the four-warp chunk operators from
+    the operators the forward kept)."""
+    from koopman_mamba_b200 import _lib
+    zt = torch.empty(1, 32768, 16, 64, dtype=torch.bfloat16, device=DEV)
+    assert _path(zt, zt, 64, 64, chunk=128) & _lib.SKA_PATH_QUAD_CHUNK_BWD
     z, zq, v, dy = _inputs(1, 32768, 16, 64, 64, 2)
     got = run_cuda(z, zq, v, 1.0, dy, torch.bfloat16, chunk_size=128)
     heads = [0, 9, 15]
@@ -153,11 +157,11 @@ def test_fused_projection_strides_bitwise():
     assert torch.equal(y1, y2)
 
 
-def _path(z, v, r, P, chunk=64):
+def _path(z, v, r, P, chunk=64, power_K=2):
     from koopman_mamba_b200 import _lib
     import ctypes
     B, T, H = z.shape[0], z.shape[1], z.shape[2]
-    s = _lib.make_shape(B, T, H, r, P, chunk, 2, 1e-3)
+    s = _lib.make_shape(B, T, H, r, P, chunk, power_K, 1e-3)
     tz = _lib.SkaTensor(z.data_ptr(), z.stride(0), z.stride(1), z.stride(2))
     tv = _lib.SkaTensor(v.data_ptr(), v.stride(0), v.stride(1), v.stride(2))
     return _lib.lib().ska_kernel_path(ctypes.byref(s), _lib.SKA_DTYPE_BF16, ctypes.byref(tz), ctypes.byref(tv))
@@ -232,6 +236,65 @@ def test_bf16_r32_short_chunks_each_power(K):
     ref = ska_core_fwd_bwd(zb, zqb, vb, 1.2, dyb, SkaParams(chunk_size=32, power_K=K))
     assert_close(got[:4], ref[:4], BF16_TOL)
     assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
+@pytest.mark.parametrize("r,P,K,chunk,alpha", [
+    (48, 64, 0, 64, None), (48, 64, 1, 64, None), (48, 64, 2, 32, None),   # each A^K branch
+    (48, 32, 2, 64, None),          # P = 32: zero rows past P in the value operands
+    (64, 48, 2, 128, None),         # r = 64 (no padding), P = 48, 128-token chunks
+    (48, 64, 2, 64, 0.9),           # the decayed scan
+])
+def test_bf16_four_warp_backward(r, P, K, chunk, alpha):
+    """bf16, 32 < r <= 64: the four-warp backward from the operators the forward
+    kept (SKA_PATH_QUAD_CHUNK_BWD), a ragged tail, forward and backward against the
+    oracle."""
+    from koopman_mamba_b200 import _lib
+    zt = torch.empty(2, 300, 3, r, dtype=torch.bfloat16, device=DEV)
+    vt = torch.empty(2, 300, 3, P, dtype=torch.bfloat16, device=DEV)
+    assert _path(zt, vt, r, P, chunk, power_K=K) & _lib.SKA_PATH_QUAD_CHUNK_BWD
+    z, zq, v, dy = _inputs(2, 300, 3, r, P, 50 + r + K)
+    kw = {} if alpha is None else dict(chunk_strategy="decay", decay_alpha=alpha)
+    got = run_cuda(z, zq, v, 1.2, dy, torch.bfloat16, chunk_size=chunk, power_K=K, **kw)
+    zb, zqb, vb, dyb = (bf16_round(a) for a in (z, zq, v, dy))
+    ref = ska_core_fwd_bwd(zb, zqb, vb, 1.2, dyb, SkaParams(chunk_size=chunk, power_K=K, decay_alpha=alpha))
+    assert_close(got[:4], ref[:4], BF16_TOL)
+    assert abs(got[4] - ref[4]) <= BF16_TOL * max(1.0, abs(ref[4]))
+
+
+def _fwd_raw(shape, z, zq, v, g, y, saved, nbytes):
+    import ctypes
+    from koopman_mamba_b200 import _lib
+    from koopman_mamba_b200.ska import _tensor_desc
+    return _lib.lib().ska_fwd(ctypes.byref(shape), _lib.SKA_DTYPE_BF16, ctypes.byref(_tensor_desc(z)),
+                              ctypes.byref(_tensor_desc(zq)), ctypes.byref(_tensor_desc(v)),
+                              ctypes.c_void_p(g.data_ptr()), ctypes.byref(_tensor_desc(y)),
+                              ctypes.c_void_p(saved.data_ptr()), nbytes,
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+@pytest.mark.parametrize("r,P", [(32, 64), (48, 64), (64, 64), (16, 32)])
+def test_forward_only_buffer_gives_the_same_y(r, P):
+    """A forward given only ska_forward_workspace_size bytes (no chunk operators
+    kept) writes the same y, bitwise, as one given the whole saved buffer; fewer
+    bytes than that are refused."""
+    from koopman_mamba_b200 import _lib
+    z, zq, v = (torch.as_tensor(a).to(DEV, torch.bfloat16) for a in _inputs(2, 500, 3, r, P, 80 + r, dy=False))
+    g = torch.tensor(1.2, device=DEV)
+    shape = _lib.make_shape(2, 500, 3, r, P, 64, 2, 1e-3)
+    full, _ = _lib.workspace_size(shape)
+    fwd = _lib.forward_workspace_size(shape)
+    assert fwd < full
+    ys = []
+    for nbytes in (full, fwd):
+        saved = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+        y = torch.full((2, 500, 3, P), float("nan"), dtype=torch.bfloat16, device=DEV)
+        assert _fwd_raw(shape, z, zq, v, g, y, saved, nbytes) == 0
+        torch.cuda.synchronize()
+        ys.append(y.float().cpu())
+    assert torch.isfinite(ys[0]).all()
+    assert torch.equal(ys[0], ys[1])
+    saved = torch.empty(fwd - 256, dtype=torch.uint8, device=DEV)
+    assert _fwd_raw(shape, z, zq, v, g, y, saved, fwd - 256) == _lib.SKA_ERR_WORKSPACE
 
 
 @pytest.mark.parametrize("P", [32, 128])
@@ -314,13 +377,16 @@ def test_empty_batch_and_errors():
 def test_bf16_model_config_heads(B, T, H, r, P, chunk):
     """The SKA shapes of the two full-model configurations, bf16, forward and backward
     against the oracle: r = 16 takes every tensor-core kernel but the fused
-    statistics + scan; r = 48 the tensor-core statistics, readout and token backward
-    around the four-warp forward operators."""
+    statistics + scan; r = 48 the tensor-core statistics, readout, readout gradient
+    and token backward around the four-warp chunk operators, forward and backward."""
     from koopman_mamba_b200 import _lib
     zt = torch.empty(B, T, H, r, dtype=torch.bfloat16, device=DEV)
     vt = torch.empty(B, T, H, P, dtype=torch.bfloat16, device=DEV)
     path = _path(zt, vt, r, P, chunk)
     assert path & _lib.SKA_PATH_TC_STATS and path & _lib.SKA_PATH_TC_TOKEN_BWD
+    assert path & _lib.SKA_PATH_TC_READOUT_BWD
+    if r > 32:
+        assert path & _lib.SKA_PATH_QUAD_CHUNK_BWD
     z, zq, v, dy = _inputs(B, T, H, r, P, 70 + r)
     got = run_cuda(z, zq, v, 1.15, dy, torch.bfloat16, chunk_size=chunk)
     ref = ska_core_fwd_bwd(z, zq, v, 1.15, dy, SkaParams(chunk_size=chunk), np.float32)

@@ -78,7 +78,7 @@ def test_noalloc_matches_ska_fwd_two_calls_in_a_row():
 def test_noalloc_refuses_problems_larger_than_its_array():
     L = _lib.lib()
     shape = _lib.make_shape(8, 2048, 12, 32, 64, 64, 2, 1e-3)   # needs ~50 MB of workspace
-    saved_bytes, _ = _lib.workspace_size(shape)
+    saved_bytes = _lib.forward_workspace_size(shape)
     assert saved_bytes > _lib.SKA_NOALLOC_SCRATCH_BYTES
     t = _lib.SkaTensor(0, 0, 0, 0)
     rc = L.ska_fwd_noalloc(ctypes.byref(shape), _lib.SKA_DTYPE_BF16, ctypes.byref(t), ctypes.byref(t),
