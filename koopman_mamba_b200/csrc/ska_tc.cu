@@ -1238,7 +1238,9 @@ cudaError_t launch_dw_tc(const Dims& d, const In& zq, const In& dy, float* dw, i
     }
   }
   g.nb = 1;
-  g.ncols = d.r < 32 ? 32u : (uint32_t)d.r;
+  // tcgen05.alloc takes a power of two >= 32 columns (r = 48 takes 64)
+  g.ncols = 32u;
+  while (g.ncols < (uint32_t)d.r) g.ncols <<= 1;
   // ZQ groups + the groups of 128 A rows (P real)
   g.smem = g.sw ? (size_t)(d.r / 32 + 4) * g.grp + 1024 : (size_t)(d.r / 8 + 16) * g.grp + 1024;
   const size_t smem = tmem_safe_smem(g.ncols, kStatsThreads, g.smem);
