@@ -366,6 +366,8 @@ class Runner:
         self.dgamma = torch.empty((), dtype=torch.float32, device=dev)
         self.shape = _lib.make_shape(B, Lq, H, wl["r"], P, wl["CS"], wl["K"], wl["ridge"])
         self.saved_bytes, self.scratch_bytes = _lib.workspace_size(self.shape)
+        if not wl["bwd"]:   # no backward reads the buffer: the forward keeps no chunk operators
+            self.saved_bytes = _lib.forward_workspace_size(self.shape)
         self.saved = torch.empty(self.saved_bytes, dtype=torch.uint8, device=dev)
         self.scratch = torch.empty(self.scratch_bytes if wl["bwd"] else 256, dtype=torch.uint8, device=dev)
         self.stream = torch.cuda.current_stream(dev)
