@@ -124,8 +124,10 @@ __device__ __forceinline__ void keep_tile(float* dst, const float* M, int t, int
 }
 
 // A0 = Mn S etc.: out block (bi, bj) = alpha X(bi, :) Y(:, bj) for 64 x 64 X, Y
-__device__ __forceinline__ void mul_block(float* out, float* X, float* Y, int bi, int bj, float alpha) {
-  wmmp<false, 32, 64, false, false, false>(blk(out, bi, bj), blk(X, bi, 0), 2 * kTile, Y + bj * 2 * kTile, alpha);
+// (kn: the first kn of the 64 K terms; past r they are zero)
+__device__ __forceinline__ void mul_block(float* out, float* X, float* Y, int bi, int bj, float alpha, int kn) {
+  wmmp<false, 32, 64, false, false, false>(blk(out, bi, bj), blk(X, bi, 0), 2 * kTile, Y + bj * 2 * kTile, alpha,
+                                           kn);
 }
 
 // sigma_max estimate of ska.py:41-58 for the 64 x 64 matrix A (region), by warps
@@ -237,19 +239,19 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     const int bi = w & 1, bj = w >> 1;
     float* out = blk(R0, bi, bj);
     if (bi == 0 && bj == 0)
-      wmmp<false, 32, 64, true, false, false>(out, RLi, kTile, RLi, 1.f);
+      wmmp<false, 32, 64, true, false, false>(out, RLi, kTile, RLi, 1.f, r);
     else if (bi == 1 && bj == 0)
-      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 0), 1.f);
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 0), 1.f, r - 32);
     else if (bi == 0)
-      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 0), kTile, blk(RLi, 1, 1), 1.f);
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 0), kTile, blk(RLi, 1, 1), 1.f, r - 32);
     else
-      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 1), 1.f);
+      wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 1), 1.f, r - 32);
   }
   cp_async_wait<0>();                                      // M (warp 1's copies)
   __syncthreads();
   if (opq) keep_tile(opq + kQOpS * kQOpFloats, R0, w, lane);
   // ---- A0 = Mn S ----
-  mul_block(RA, RK, R0, w & 1, w >> 1, im2);
+  mul_block(RA, RK, R0, w & 1, w >> 1, im2, r);
   __syncthreads();
   if (opq) keep_tile(opq + kQOpA0 * kQOpFloats, RA, w, lane);
   // ---- spectral norm (warps 0, 1) while warps 2, 3 form A0^K ----
@@ -279,8 +281,8 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     for (int s = 1; s < d.K; ++s) {
       float* out = (prev == RK) ? R0 : RK;
       const int bj = w - 2;   // warps 2, 3: column block 0, 1 (both row blocks)
-      mul_block(out, const_cast<float*>(prev), RA, 0, bj, 1.f);
-      mul_block(out, const_cast<float*>(prev), RA, 1, bj, 1.f);
+      mul_block(out, const_cast<float*>(prev), RA, 0, bj, 1.f, r);
+      mul_block(out, const_cast<float*>(prev), RA, 1, bj, 1.f, r);
       asm volatile("bar.sync 2, 64;" ::: "memory");   // warps 2, 3: the power is complete
       prev = out;
     }
@@ -317,9 +319,9 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   {
     const int bi = w & 1, bj = w >> 1;
     if (bj == 0)
-      wmmp<false, 32, 64, false, false, false>(blk(RU, bi, 0), blk(AK, bi, 0), 2 * kTile, RLi, kkK);
+      wmmp<false, 32, 64, false, false, false>(blk(RU, bi, 0), blk(AK, bi, 0), 2 * kTile, RLi, kkK, r);
     else
-      wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), kkK);
+      wmmp<false, 32, 32, false, false, false>(blk(RU, bi, 1), blk(AK, bi, 1), kTile, blk(RLi, 1, 1), kkK, r - 32);
   }
   __syncthreads();
   if (opq) keep_tile(opq + kQOpU * kQOpFloats, RU, w, lane);
@@ -328,9 +330,9 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   {
     const int bi = w & 1, bj = w >> 1;
     if (bi == 0)
-      wmmp<false, 32, 64, true, false, false>(blk(RV, 0, bj), RLi, kTile, RU + bj * 2 * kTile, 1.f);
+      wmmp<false, 32, 64, true, false, false>(blk(RV, 0, bj), RLi, kTile, RU + bj * 2 * kTile, 1.f, r);
     else
-      wmmp<false, 32, 32, true, false, false>(blk(RV, 1, bj), blk(RLi, 1, 1), kTile, blk(RU, 1, bj), 1.f);
+      wmmp<false, 32, 32, true, false, false>(blk(RV, 1, bj), blk(RLi, 1, 1), kTile, blk(RU, 1, bj), 1.f, r - 32);
   }
   if (w == 2) cp_async_wait<0>();                          // C
   __syncthreads();
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   for (int t = w; t < 2 * NPB; t += 4) {
     const int pb = t % NPB, bj = t / NPB;
     float* out = RW + (bj * NPB + pb) * kTile;
-    wmmp<false, 32, 64, false, false, false>(out, RC + pb * kTile, NPB * kTile, RV + bj * 2 * kTile, im2);
+    wmmp<false, 32, 64, false, false, false>(out, RC + pb * kTile, NPB * kTile, RV + bj * 2 * kTile, im2, r);
     __syncwarp();
     float u[32];
     ld_row(u, out, lane);
@@ -422,23 +424,31 @@ __device__ __forceinline__ void store_block(float* dst, int ld, const float* T, 
   }
 }
 
-// out block (bi, bj) of 64 x 64 products (alpha folded in; ACC accumulates)
+// out block (bi, bj) of 64 x 64 products (alpha folded in; ACC accumulates).  kn:
+// the first kn (a multiple of 8) of the 64 K terms; past r (or P) they are
+// zero, and every matrix here is zero between its valid and padding parts, so the
+// valid part of the product does not change
 template <bool ACC>
-__device__ __forceinline__ void mm_nn(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+__device__ __forceinline__ void mm_nn(float* out, const float* X, const float* Y, int bi, int bj, float alpha,
+                                      int kn) {
   wmmp<false, 32, 64, false, false, ACC>(blk(out, bi, bj), blk(const_cast<float*>(X), bi, 0), 2 * kTile,
-                                         Y + bj * 2 * kTile, alpha);   // X Y
+                                         Y + bj * 2 * kTile, alpha, kn);   // X Y
 }
 template <bool ACC>
-__device__ __forceinline__ void mm_tn(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+__device__ __forceinline__ void mm_tn(float* out, const float* X, const float* Y, int bi, int bj, float alpha,
+                                      int kn) {
   wmmp<false, 32, 64, true, false, ACC>(blk(out, bi, bj), X + bi * 2 * kTile, kTile, Y + bj * 2 * kTile,
-                                        alpha);                        // X^T Y
+                                        alpha, kn);                        // X^T Y
 }
 template <bool ACC>
-__device__ __forceinline__ void mm_nt(float* out, const float* X, const float* Y, int bi, int bj, float alpha) {
+__device__ __forceinline__ void mm_nt(float* out, const float* X, const float* Y, int bi, int bj, float alpha,
+                                      int kn) {
   float* Xm = const_cast<float*>(X);
   float* Ym = const_cast<float*>(Y);
-  wmmp<false, 32, 32, false, true, ACC>(blk(out, bi, bj), blk(Xm, bi, 0), kTile, blk(Ym, bj, 0), alpha);   // X Y^T
-  wmmp<false, 32, 32, false, true, true>(blk(out, bi, bj), blk(Xm, bi, 1), kTile, blk(Ym, bj, 1), alpha);
+  wmmp<false, 32, 32, false, true, ACC>(blk(out, bi, bj), blk(Xm, bi, 0), kTile, blk(Ym, bj, 0), alpha,
+                                        min(kn, 32));   // X Y^T
+  if (kn > 32)
+    wmmp<false, 32, 32, false, true, true>(blk(out, bi, bj), blk(Xm, bi, 1), kTile, blk(Ym, bj, 1), alpha, kn - 32);
 }
 
 // tril of block (bi, bj) of a 64 x 64 matrix, in place, by the warp that owns it
@@ -487,6 +497,7 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   const float* dwq = dwraw + q * (long long)P * r;
   float* drec = dstats + q * d.SW;
   const int rows_r = r - 32 * bi, cols_r = r - 32 * bj, rows_p = P - 32 * bi;
+  const int kp = (P + 7) & ~7;                       // K of the products over the P value rows
 
   // C -> R0, dW' -> R1, V -> R2 (group 0); Li -> R3, U -> R4 (group 1)
   fetch_block(blk(R[0], bi, bj), rec + 2 * r * r + (size_t)(32 * bi) * r + 32 * bj, r, rows_p, cols_r, lane);
@@ -507,8 +518,8 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   __syncthreads();
 
   // ---- dV = C^T dW' / m^2 -> R5,  TY = dW' V^T = m dCn -> R6 ----
-  mm_tn<false>(R[5], R[0], R[1], bi, bj, im2);
-  mm_nt<false>(R[6], R[1], R[2], bi, bj, 1.f);
+  mm_tn<false>(R[5], R[0], R[1], bi, bj, im2, kp);
+  mm_nt<false>(R[6], R[1], R[2], bi, bj, 1.f, r);
   __syncwarp();
   store_block(drec + 2 * r * r + (size_t)(32 * bi) * r + 32 * bj, r, blk(R[6], bi, bj), min(rows_p, 32),
               min(cols_r, 32), im2, lane);
@@ -522,8 +533,8 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   cp_async_commit();
 
   // ---- dU = Li dV -> R2,  dLi = U dV^T -> R6 ----
-  mm_nn<false>(R[2], R[3], R[5], bi, bj, 1.f);
-  mm_nt<false>(R[6], R[4], R[5], bi, bj, 1.f);
+  mm_nn<false>(R[2], R[3], R[5], bi, bj, 1.f, r);
+  mm_nt<false>(R[6], R[4], R[5], bi, bj, 1.f, r);
   cp_async_wait<0>();
   __syncthreads();
   // free: R4 (U), R5 (dV).  S -> R4 (group 3)
@@ -531,8 +542,8 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   cp_async_commit();
 
   // ---- dLi += (A^K)^T dU,  dA^K = dU Li^T -> R5  (A^K = kk^K A0^K) ----
-  mm_tn<true>(R[6], R[0], R[2], bi, bj, kkK);
-  mm_nt<false>(R[5], R[2], R[3], bi, bj, 1.f);
+  mm_tn<true>(R[6], R[0], R[2], bi, bj, kkK, r);
+  mm_nt<false>(R[5], R[2], R[3], bi, bj, 1.f, r);
   cp_async_wait<0>();
   __syncthreads();
   // free: R0 (A0^K), R2 (dU).  M -> R0 (group 4)
@@ -543,8 +554,8 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   float* RdA = R[2];
   if (d.K >= 2) {
     // K = 2: dA^K A^T + A^T dA^K
-    mm_nt<false>(R[2], R[5], R[1], bi, bj, kk);
-    mm_tn<true>(R[2], R[1], R[5], bi, bj, kk);
+    mm_nt<false>(R[2], R[5], R[1], bi, bj, kk, r);
+    mm_tn<true>(R[2], R[1], R[5], bi, bj, kk, r);
   } else if (d.K == 1) {
     RdA = R[5];
   } else {
@@ -560,8 +571,8 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   float* RdMn = R[1];                                          // A0 is dead
 
   // ---- dMn = kk dA S -> R1,  dS = kk Mn^T dA -> RdS ----
-  mm_nn<false>(RdMn, RdA, R[4], bi, bj, kk);
-  mm_tn<false>(RdS, R[0], RdA, bi, bj, kk * im2);
+  mm_nn<false>(RdMn, RdA, R[4], bi, bj, kk, r);
+  mm_tn<false>(RdS, R[0], RdA, bi, bj, kk * im2, r);
   __syncwarp();
   store_block(drec + r * r + (size_t)(32 * bi) * r + 32 * bj, r, blk(RdMn, bi, bj), min(rows_r, 32), min(cols_r, 32),
               im2, lane);
@@ -582,12 +593,12 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   }
   __syncthreads();
   // ---- dLi += Li (dS + dS^T); only tril(dLi) reaches L ----
-  mm_nn<true>(R[6], R[3], R[0], bi, bj, 1.f);
+  mm_nn<true>(R[6], R[3], R[0], bi, bj, 1.f, r);
   __syncwarp();
   tril_block(R[6], bi, bj, lane);
   __syncthreads();
   // ---- Pm = tril(-dLi Li^T) -> R1 ----
-  mm_nt<false>(R[1], R[6], R[3], bi, bj, -1.f);
+  mm_nt<false>(R[1], R[6], R[3], bi, bj, -1.f, r);
   __syncwarp();
   tril_block(R[1], bi, bj, lane);
   __syncthreads();
@@ -603,10 +614,10 @@ __global__ void __launch_bounds__(kThreads4, 2) k_bwd_chunk_q(Dims d, const floa
   }
   __syncthreads();
   // ---- T1 = P' Li -> R0,  dGn = Li^T T1 -> R1 ----
-  mm_nn<false>(R[0], RdS, R[3], bi, bj, 1.f);
+  mm_nn<false>(R[0], RdS, R[3], bi, bj, 1.f, r);
   cp_async_wait<0>();                                          // G
   __syncthreads();
-  mm_tn<false>(R[1], R[3], R[0], bi, bj, 1.f);
+  mm_tn<false>(R[1], R[3], R[0], bi, bj, 1.f, r);
   __syncthreads();
   // ---- sym(dGn) / m^2 -> dstats; <dGn, Gn> ----
   float dmg = 0.f;

@@ -479,10 +479,11 @@ __device__ __forceinline__ void split_trunc(float x, uint32_t& hi, uint32_t& lo)
 // is passed unsplit).  RN_: round unsplit operands to the nearest tf32 value
 // (bits + 0x1000, low 13 bits cleared; exact values stay exact) instead of
 // letting the MMA truncate them.  Two 16-row blocks are processed together so that they share
-// the B fragments; M is a multiple of 32.
+// the B fragments; M is a multiple of 32.  kn (a multiple of 8, <= K): only the first
+// kn of the K terms are summed (the rest are known zero: padding past r).
 template <int M, int K, bool TA, bool TB, bool ACC, bool SA_, bool SB_, bool RN_ = false>
 __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict__ A, int SA,
-                                  const float* __restrict__ B, float alpha) {
+                                  const float* __restrict__ B, float alpha, int kn = K) {
   static_assert(M % 32 == 0 && K % 8 == 0, "tile shape");
   static_assert(!TB || K <= 32, "transposed B holds 32 x K");
   const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
@@ -499,7 +500,7 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
     // B=8, H=12, L=2048, P=64, r=32: full unroll 0.2105 ms, by 2 0.2035 ms, none
     // 0.2012 ms)
 #pragma unroll 1
-    for (int k0 = 0; k0 < K; k0 += 8) {
+    for (int k0 = 0; k0 < kn; k0 += 8) {
       if ((k0 & 15) == 0) sched_fence();
       const int kc = (k0 & 31) >> 2;         // 16-byte chunk of column ka; kb is kc + 1
       uint32_t ah[2][4], al[2][4];
@@ -608,11 +609,11 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
 //     numerics, but with power_K = 3 and 32-token chunks the backward reached the
 //     2e-2 bf16 bar, so it is not used.
 template <bool FAST, int M, int K, bool TA, bool TB, bool ACC>
-__device__ __forceinline__ void wmmp(float* C, const float* A, int SA, const float* B, float alpha) {
+__device__ __forceinline__ void wmmp(float* C, const float* A, int SA, const float* B, float alpha, int kn = K) {
   if constexpr (FAST) {
-    wmm2<M, K, TA, TB, ACC, false, false, true>(C, A, SA, B, alpha);
+    wmm2<M, K, TA, TB, ACC, false, false, true>(C, A, SA, B, alpha, kn);
   } else {
-    wmm2<M, K, TA, TB, ACC, true, true>(C, A, SA, B, alpha);
+    wmm2<M, K, TA, TB, ACC, true, true>(C, A, SA, B, alpha, kn);
   }
 }
 
