@@ -73,16 +73,17 @@ __device__ __forceinline__ void fetch_square(float* M, const float* src, int r, 
 
 // Gn row blocks for the blocked Cholesky (warp 0).  attempt: jitter or not.
 // Returns false (uniformly) when a pivot is not positive.  On success Li holds the
-// inverse factor (block (0, 1) zero).  T0..T3 are scratch tiles.
+// inverse factor (block (0, 1) zero).  T0..T3 are scratch tiles; cb: 32 floats
+// (16-byte aligned) for the factorisations' column broadcasts (chol_inv32_bc).
 __device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, float* T1, float* T2, float* T3,
-                               float im2, float jit, int lane) {
+                               float im2, float jit, float* cb, int lane) {
   const int r = d.r;
   float g[32], x[32], a[32], b[32];
   // block 11
   ld_row(a, blk(G, 0, 0), lane);
   ld_col<32>(b, blk(G, 0, 0), lane);
   build_gram_row(g, a, b, lane, 32, im2, d.ridge, jit);
-  if (!chol_inv32(g, x, lane)) return false;
+  if (!chol_inv32_bc(g, x, cb, lane)) return false;
   st_col<32>(blk(Li, 0, 0), lane, x);                            // Li11 rows
   // Gn21 (row 32 + lane, column j): (G21 + G12^T) / 2 / m^2
   ld_row(a, blk(G, 1, 0), lane);
@@ -102,7 +103,7 @@ __device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, fl
   wmmp<false, 32, 32, false, true, true>(T2, T1, kTile, T1, -1.f);              // Gn22 - L21 L21^T
   __syncwarp();
   ld_row(g, T2, lane);
-  if (!chol_inv32(g, x, lane)) return false;
+  if (!chol_inv32_bc(g, x, cb, lane)) return false;
   st_col<32>(blk(Li, 1, 1), lane, x);                            // Li22 rows
   __syncwarp();
   wmmp<false, 32, 32, false, false, false>(T3, T1, kTile, blk(Li, 0, 0), 1.f);  // L21 Li11
@@ -201,7 +202,8 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   float* RLi = R0 + kRegion;                   // Li, then W / m
   float* RA = RLi + kRegion;                   // Cholesky scratch, then A0 / A
   float* RK = RA + kRegion;                    // Mn, then A^K
-  __shared__ float vsh[64], part[128], red[2];
+  __shared__ __align__(16) float part[128];   // power-iteration partials; the Cholesky's broadcasts before
+  __shared__ float vsh[64], red[2];
   __shared__ float s_sigma;
   __shared__ int s_flag;
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
@@ -223,9 +225,10 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     cp_async_wait<0>();
     __syncwarp();
     int flag = 0;
-    if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, 0.f, lane)) {
+    if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, 0.f, part,
+                        lane)) {
       flag = 1;
-      if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, kJitter,
+      if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, kJitter, part,
                           lane))
         flag |= 2;
     }
