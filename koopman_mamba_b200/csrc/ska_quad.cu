@@ -103,7 +103,7 @@ __device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, fl
   wmmp<false, 32, 32, false, true, true>(T2, T1, kTile, T1, -1.f);              // Gn22 - L21 L21^T
   __syncwarp();
   ld_row(g, T2, lane);
-  if (!chol_inv32_bc(g, x, cb, lane)) return false;
+  if (!chol_inv32_bc<true>(g, x, cb, lane, r - 32)) return false;
   st_col<32>(blk(Li, 1, 1), lane, x);                            // Li22 rows
   __syncwarp();
   wmmp<false, 32, 32, false, false, false>(T3, T1, kTile, blk(Li, 0, 0), 1.f);  // L21 Li11

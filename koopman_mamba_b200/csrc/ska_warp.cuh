@@ -173,13 +173,19 @@ __device__ __forceinline__ bool chol_inv32(float (&g)[32], float (&x)[32], int l
 // loads, so that a step costs one store, eight loads and the FMAs (the shuffle
 // version issues 31 - j shuffles per step, and twelve or more warps per SM doing
 // that saturate the shuffle unit).  Same results and return value as chol_inv32,
-// up to the rounding of the fused scale.
-__device__ __forceinline__ bool chol_inv32_bc(float (&g)[32], float (&x)[32], float* cb, int lane) {
+// up to the rounding of the fused scale.  TRIM: the steps past n (warp-uniform) are
+// skipped; rows and columns past n must hold the identity padding, which those
+// steps would leave unchanged (a template switch, so that the full-size factor
+// keeps its straight-line code: a run-time test in it, or a second trimmed copy
+// beside it, slowed the r = 32 operator kernel by 2-11 us at config 2).
+template <bool TRIM = false>
+__device__ __forceinline__ bool chol_inv32_bc(float (&g)[32], float (&x)[32], float* cb, int lane, int n = 32) {
 #pragma unroll
   for (int k = 0; k < 32; ++k) x[k] = (k == lane) ? 1.f : 0.f;
   const float4* cb4 = reinterpret_cast<const float4*>(cb);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
+    if (TRIM && j >= n) break;
     cb[lane] = g[j];
     __syncwarp();
     float c[32];
