@@ -333,7 +333,7 @@ def _measured_peak():
 def _ncu_traffic(key, names):
     """DRAM bytes per step (read + write of every kernel of the step) from the
     committed ncu capture of the same kernels, or None when the capture does not
-    cover the kernels this build launches."""
+    cover the kernels this library launches."""
     try:
         with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
             per = json.load(f)[key]["bytes_per_launch"]
