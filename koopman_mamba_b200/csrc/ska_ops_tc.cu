@@ -183,7 +183,9 @@ __device__ __forceinline__ void ld_gmem_col(float (&v)[32], const float* src, in
 
 // Gn = sym(G) / m^2 + ridge I (+ jitter), factored with its inverse (ska.py:136-145):
 // x = row `lane` of Li^T (column `lane` of L^{-1}); cb: 32 floats of the warp's shared
-// memory for the column broadcasts.  Returns the jitter flags.
+// memory for the column broadcasts.  Returns the jitter flags.  R16: r <= 16, the
+// factorisation stops after 16 steps (the rest is identity padding).
+template <bool R16 = false>
 __device__ __forceinline__ int factor_invert_rows(const Dims& d, const float* rec, int lane, float im2,
                                                   float (&x)[32], float* cb) {
   const int r = d.r;
@@ -199,7 +201,7 @@ __device__ __forceinline__ int factor_invert_rows(const Dims& d, const float* re
       wpc::build_gram_row(g, grow, gcol, lane, r, im2, d.ridge, jit ? kJitter : 0.f);
     }
     if (jit) flag |= 1;
-    if (wpc::chol_inv32_bc(g, x, cb, lane)) break;
+    if (wpc::chol_inv32_bc<R16>(g, x, cb, lane, 16)) break;
     if (jit) {
       flag |= 2;
       break;
@@ -370,9 +372,11 @@ static cudaError_t persistent_grid(const void* fn, size_t smem, int per_sm, long
 
 // ---------------------------------------------------------------------------
 // forward.  Persistent: CTA b takes the chunk groups b, b + gridDim.x, ... and
-// starts the next group's record on its way to L2 when it begins a group.
+// starts the next group's record on its way to L2 when it begins a group.  R16:
+// the r <= 16 instance (a shorter factorisation; its own code, so that the r = 32
+// instance keeps its straight-line Cholesky).
 // ---------------------------------------------------------------------------
-template <int NPB>
+template <int NPB, bool R16 = false>
 __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const float* __restrict__ gamma_p,
                                                                const float* __restrict__ stats,
                                                                const unsigned long long* __restrict__ cmax,
@@ -434,7 +438,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     {
       float x[32];
       // S2's part of this warp (free until C(S) is written) holds the column broadcasts
-      const int flag = factor_invert_rows(d, rec, lane, im2, x, reinterpret_cast<float*>(S2 + 2048 * w));
+      const int flag = factor_invert_rows<R16>(d, rec, lane, im2, x, reinterpret_cast<float*>(S2 + 2048 * w));
       if (valid && lane == 0) flags_out[q] = flag;
       if (keep) store_op(opq + kOpLi * kOpFloats, x, lane);
       put_row<false>(S0, w, lane, x);
@@ -921,8 +925,11 @@ cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* st
   Dims dd = d;
   void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags, (void*)&ops,
                   (void*)&wm, (void*)&status};
-  const void* fn = npb == 1 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<1>)
-                   : npb == 2 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<2>)
+  const bool r16 = d.r <= 16;
+  const void* fn = npb == 1 ? (r16 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<1, true>)
+                                   : reinterpret_cast<const void*>(otc::k_fwd_ops_tc<1>))
+                   : npb == 2 ? (r16 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<2, true>)
+                                     : reinterpret_cast<const void*>(otc::k_fwd_ops_tc<2>))
                               : reinterpret_cast<const void*>(otc::k_fwd_ops_tc<4>);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
