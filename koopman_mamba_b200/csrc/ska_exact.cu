@@ -1157,7 +1157,7 @@ bool ops_tc_ok(const Dims& d);
 cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                               float* invs, int* flags, float* ops, unsigned char* wm, int* status, cudaStream_t st);
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               float* invs, int* flags, float* ops, unsigned char* wm, cudaStream_t st);
+                               float* invs, int* flags, float* lis, float* ops, unsigned char* wm, cudaStream_t st);
 
 // bf16 tensors on the warp or four-warp path whose zq and y the tensor-core readout
 // can take
@@ -1227,8 +1227,8 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
     if (e != cudaSuccess) return e;
   } else if (quad_fwd<IO>(d, zq)) {   // 32 < r <= 64: four-warp operators, tensor-core readout
     float* ops = keep_ops ? reinterpret_cast<float*>(saved + L.ops) : nullptr;
-    if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, ops, reinterpret_cast<unsigned char*>(saved + L.wm),
-                                st)) != cudaSuccess)
+    if ((e = launch_fwd_chunk_q(d, gamma, stats, cmax, invs, flags, reinterpret_cast<float*>(saved + L.lis), ops,
+                                reinterpret_cast<unsigned char*>(saved + L.wm), st)) != cudaSuccess)
       return e;
     tc_read = fwd_tc_readout<IO>(d, zq, y);
     // a y the tensor-core readout cannot store: the one-CTA kernel writes it (and

@@ -71,48 +71,128 @@ __device__ __forceinline__ void fetch_square(float* M, const float* src, int r, 
       fetch_block(blk(M, bi, bj), src + (size_t)(32 * bi) * r + 32 * bj, r, r - 32 * bi, r - 32 * bj, lane);
 }
 
-// Gn row blocks for the blocked Cholesky (warp 0).  attempt: jitter or not.
-// Returns false (uniformly) when a pivot is not positive.  On success Li holds the
-// inverse factor (block (0, 1) zero).  T0..T3 are scratch tiles; cb: 32 floats
-// (16-byte aligned) for the factorisations' column broadcasts (chol_inv32_bc).
-__device__ bool blocked_factor(const Dims& d, float* G, float* Li, float* T0, float* T1, float* T2, float* T3,
-                               float im2, float jit, float* cb, int lane) {
+// G (r x r, row stride r, raw) read straight from the chunk record, as 32 x 32
+// blocks: row(v, bi, bj) = row `lane` of block (bi, bj), col(v, bi, bj) = its
+// column `lane`; zero past r.  (rec is 16-byte aligned and r % 8 == 0.)
+struct GlobalGram {
+  const float* G;
+  int r;
+  __device__ __forceinline__ void row(float (&v)[32], int bi, int bj, int lane) const {
+    const int i = 32 * bi + lane, c0 = 32 * bj;
+    const bool rv = i < r;
+    const float4* p4 = reinterpret_cast<const float4*>(G + (size_t)(rv ? i : 0) * r + c0);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const bool ok = rv && c0 + 4 * k < r;
+      const float4 x = ok ? __ldg(p4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * k] = x.x;
+      v[4 * k + 1] = x.y;
+      v[4 * k + 2] = x.z;
+      v[4 * k + 3] = x.w;
+    }
+  }
+  __device__ __forceinline__ void col(float (&v)[32], int bi, int bj, int lane) const {
+    const int j = 32 * bj + lane, r0 = 32 * bi;
+    const bool cv = j < r;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (cv && r0 + i < r) ? __ldg(G + (size_t)(r0 + i) * r + j) : 0.f;
+  }
+};
+
+// The blocked Cholesky + inverse of one chunk's Gram matrix by one warp:
+//   L11 = chol(Gn11), Li11 = L11^{-1}             (chol_inv32_bc)
+//   L21 = Gn21 Li11^T,  Gn22' = Gn22 - L21 L21^T
+//   L22 = chol(Gn22'), Li22 = L22^{-1}            (chol_inv32_bc, r - 32 steps)
+//   Li21 = -Li22 L21 Li11
+// with Gn = sym(G) / m^2 + (ridge + jit) I and identity padding past r.  Returns
+// false (uniformly) when a pivot is not positive (the blocked pivots are those of
+// the unblocked factorisation).  Li11, Li21, Li22: output tiles (Li12 is zero);
+// T0, T1, T2: scratch tiles; cb: 32 floats (16-byte aligned) for the broadcasts.
+__device__ bool blocked_factor(const Dims& d, const GlobalGram& G, float* Li11, float* Li21, float* Li22, float* T0,
+                               float* T1, float* T2, float im2, float jit, float* cb, int lane) {
   const int r = d.r;
   float g[32], x[32], a[32], b[32];
   // block 11
-  ld_row(a, blk(G, 0, 0), lane);
-  ld_col<32>(b, blk(G, 0, 0), lane);
+  G.row(a, 0, 0, lane);
+  G.col(b, 0, 0, lane);
   build_gram_row(g, a, b, lane, 32, im2, d.ridge, jit);
   if (!chol_inv32_bc(g, x, cb, lane)) return false;
-  st_col<32>(blk(Li, 0, 0), lane, x);                            // Li11 rows
+  st_col<32>(Li11, lane, x);                                      // Li11 rows
   // Gn21 (row 32 + lane, column j): (G21 + G12^T) / 2 / m^2
-  ld_row(a, blk(G, 1, 0), lane);
-  ld_col<32>(b, blk(G, 0, 1), lane);
+  G.row(a, 1, 0, lane);
+  G.col(b, 0, 1, lane);
   const bool row_ok = 32 + lane < r;
 #pragma unroll
   for (int j = 0; j < 32; ++j) a[j] = row_ok ? 0.5f * (a[j] * im2 + b[j] * im2) : 0.f;
   st_row(T0, lane, a);
   // Gn22 (with identity padding past r)
-  ld_row(a, blk(G, 1, 1), lane);
-  ld_col<32>(b, blk(G, 1, 1), lane);
+  G.row(a, 1, 1, lane);
+  G.col(b, 1, 1, lane);
   build_gram_row(g, a, b, lane, r - 32, im2, d.ridge, jit);
   st_row(T2, lane, g);
   __syncwarp();
-  wmmp<false, 32, 32, false, true, false>(T1, T0, kTile, blk(Li, 0, 0), 1.f);   // L21 = Gn21 Li11^T
+  wmmp<false, 32, 32, false, true, false>(T1, T0, kTile, Li11, 1.f);     // L21 = Gn21 Li11^T
   __syncwarp();
-  wmmp<false, 32, 32, false, true, true>(T2, T1, kTile, T1, -1.f);              // Gn22 - L21 L21^T
+  wmmp<false, 32, 32, false, true, true>(T2, T1, kTile, T1, -1.f);       // Gn22 - L21 L21^T
   __syncwarp();
   ld_row(g, T2, lane);
   if (!chol_inv32_bc<true>(g, x, cb, lane, r - 32)) return false;
-  st_col<32>(blk(Li, 1, 1), lane, x);                            // Li22 rows
+  st_col<32>(Li22, lane, x);                                      // Li22 rows
   __syncwarp();
-  wmmp<false, 32, 32, false, false, false>(T3, T1, kTile, blk(Li, 0, 0), 1.f);  // L21 Li11
+  wmmp<false, 32, 32, false, false, false>(T0, T1, kTile, Li11, 1.f);    // L21 Li11 (Gn21 is dead)
   __syncwarp();
-  wmmp<false, 32, 32, false, false, false>(blk(Li, 1, 0), blk(Li, 1, 1), kTile, T3, -1.f);   // Li21
-  zero(a);
-  st_row(blk(Li, 0, 1), lane, a);
+  wmmp<false, 32, 32, false, false, false>(Li21, Li22, kTile, T0, -1.f); // Li21
   __syncwarp();
   return true;
+}
+
+// ---------------------------------------------------------------------------
+// k_factor_q: the blocked Cholesky + inverse of every chunk, one warp per chunk,
+// eight warps per SM (six 4 KB tiles of shared memory each), ahead of the
+// four-warp operator kernel: there the factorisation ran on one warp while the
+// other three waited at the next block barrier (~38K of the ~92K cycles of a
+// chunk at r = 64).  Writes Li's three non-zero 32 x 32 tiles (Li11, Li21, Li22,
+// as the operator kernel holds them in shared memory) and the jitter flags
+// (ska.py:140-145: a non-positive pivot refactors with 1e-4 added to the
+// diagonal; bit 1 when that fails too).
+// ---------------------------------------------------------------------------
+constexpr int kFacWarps = 4;
+constexpr int kFacFloats = 6 * kTile + 32;   // per warp: Li11, Li21, Li22, T0..T2, the broadcast row
+
+__global__ void __launch_bounds__(kFacWarps * 32, 2) k_factor_q(Dims d, const float* __restrict__ stats,
+                                                                const unsigned long long* __restrict__ cmax,
+                                                                float* __restrict__ lis, int* __restrict__ flags_out) {
+  extern __shared__ float4 sm4[];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long q = (long long)blockIdx.x * kFacWarps + w;
+  if (q >= (long long)d.B * d.H * d.C) return;   // warp-uniform; no block barriers below
+  float* base = reinterpret_cast<float*>(sm4) + (size_t)w * kFacFloats;
+  float* L11 = base;
+  float* L21 = base + kTile;
+  float* L22 = base + 2 * kTile;
+  float* T0 = base + 3 * kTile;
+  float* T1 = base + 4 * kTile;
+  float* T2 = base + 5 * kTile;
+  float* cb = base + 6 * kTile;
+  const ChunkId id = chunk_id(d, q);
+  const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
+  const GlobalGram G{stats + q * d.SW, d.r};
+  int flag = 0;
+  if (!blocked_factor(d, G, L11, L21, L22, T0, T1, T2, im2, 0.f, cb, lane)) {
+    flag = 1;
+    if (!blocked_factor(d, G, L11, L21, L22, T0, T1, T2, im2, kJitter, cb, lane)) flag |= 2;
+  }
+  if (lane == 0) flags_out[q] = flag;
+  __syncwarp();
+  float* dst = lis + q * (long long)(3 * kTile);
+  const float4* src4[3] = {reinterpret_cast<const float4*>(L11), reinterpret_cast<const float4*>(L21),
+                           reinterpret_cast<const float4*>(L22)};
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    float4* g4 = reinterpret_cast<float4*>(dst + t * kTile);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g4[32 * k + lane] = src4[t][32 * k + lane];
+  }
 }
 
 // tile t of a 64 x 64 region -> the same tile of a kept operator in global memory
@@ -194,18 +274,16 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
                                                               const float* __restrict__ stats,
                                                               const unsigned long long* __restrict__ cmax,
                                                               float* __restrict__ invs_out,
-                                                              int* __restrict__ flags_out,
+                                                              const float* __restrict__ lis,
                                                               float* __restrict__ ops_out,
                                                               unsigned char* __restrict__ wm_out) {
   extern __shared__ float4 sm4[];
-  float* R0 = reinterpret_cast<float*>(sm4);   // G, then S, then A^K / U / V / spare
+  float* R0 = reinterpret_cast<float*>(sm4);   // S, then A^K / U / V / spare
   float* RLi = R0 + kRegion;                   // Li, then W / m
-  float* RA = RLi + kRegion;                   // Cholesky scratch, then A0 / A
+  float* RA = RLi + kRegion;                   // A0 / A
   float* RK = RA + kRegion;                    // Mn, then A^K
-  __shared__ __align__(16) float part[128];   // power-iteration partials; the Cholesky's broadcasts before
-  __shared__ float vsh[64], red[2];
+  __shared__ float vsh[64], part[128], red[2];
   __shared__ float s_sigma;
-  __shared__ int s_flag;
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const long long q = blockIdx.x;
   const ChunkId id = chunk_id(d, q);
@@ -214,26 +292,29 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
   // kept operators (when the caller keeps them): each warp writes tile w of each
   float* opq = ops_out ? ops_out + q * (long long)(kNumOps * kQOpFloats) : nullptr;
 
-  if (w == 0) fetch_square(R0, rec, r, lane);              // G
+  // Li (k_factor_q): warps 0-2 copy its three non-zero tiles in, warp 3 zeroes
+  // block (0, 1); M from the record (warp 1)
+  {
+    const float* src = lis + q * (long long)(3 * kTile);
+    if (w < 3) {
+      float* dst = RLi + (w == 2 ? 3 : w) * kTile;           // tiles (0, 0), (1, 0), (1, 1)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t da = static_cast<uint32_t>(__cvta_generic_to_shared(dst + (32 * k + lane) * 4));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(da), "l"(src + w * kTile + (32 * k + lane) * 4)
+                     : "memory");
+      }
+    } else {
+      float z[32];
+      zero(z);
+      st_row(blk(RLi, 0, 1), lane, z);
+    }
+  }
   if (w == 1) fetch_square(RK, rec + r * r, r, lane);      // M
   cp_async_commit();
   const float m = series_norm(cmax, id, d.C, lane), im = 1.f / m, im2 = im * im;
   const float gs = fminf(fmaxf(*gamma_p, 1.f), 1.5f);
-
-  // ---- blocked Cholesky + inverse (warp 0), jitter retry ----
-  if (w == 0) {
-    cp_async_wait<0>();
-    __syncwarp();
-    int flag = 0;
-    if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, 0.f, part,
-                        lane)) {
-      flag = 1;
-      if (!blocked_factor(d, R0, RLi, blk(RA, 0, 0), blk(RA, 1, 0), blk(RA, 0, 1), blk(RA, 1, 1), im2, kJitter, part,
-                          lane))
-        flag |= 2;
-    }
-    if (lane == 0) s_flag = flag;
-  }
+  cp_async_wait<0>();                                      // Li (and M on warp 1)
   __syncthreads();
   if (opq) keep_tile(opq + kQOpLi * kQOpFloats, RLi, w, lane);
 
@@ -250,7 +331,6 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     else
       wmmp<false, 32, 32, true, false, false>(out, blk(RLi, 1, 1), kTile, blk(RLi, 1, 1), 1.f, r - 32);
   }
-  cp_async_wait<0>();                                      // M (warp 1's copies)
   __syncthreads();
   if (opq) keep_tile(opq + kQOpS * kQOpFloats, R0, w, lane);
   // ---- A0 = Mn S ----
@@ -267,8 +347,7 @@ __global__ void __launch_bounds__(kThreads4, 3) k_fwd_chunk_q(Dims d, const floa
     const float sg = power_sigma64(RA, vsh, part, red, r, w, lane);
     if (tid == 0) {
       s_sigma = sg;
-      invs_out[q] = 1.f / fmaxf(sg, 1.f);
-      flags_out[q] = s_flag;
+      invs_out[q] = 1.f / fmaxf(sg, 1.f);   // (k_factor_q wrote the flags)
     }
   } else if (d.K == 0) {
     float t[32];
@@ -676,21 +755,31 @@ cudaError_t launch_bwd_chunk_q(const Dims& d, const float* gamma, const float* s
   return cudaGetLastError();
 }
 
+// lis: room for Li's three tiles per chunk (the factor kernel's output)
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                               float* invs, int* flags, float* ops, unsigned char* wm, cudaStream_t st) {
+                               float* invs, int* flags, float* lis, float* ops, unsigned char* wm, cudaStream_t st) {
   const size_t smem = smem_fwd_chunk_q(d);
   const long long n = (long long)d.B * d.H * d.C;
   cudaError_t e;
+  {
+    const size_t fsmem = (size_t)quad::kFacWarps * quad::kFacFloats * sizeof(float);
+    if ((e = cudaFuncSetAttribute(quad::k_factor_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem)) !=
+        cudaSuccess)
+      return e;
+    const unsigned fgrid = (unsigned)((n + quad::kFacWarps - 1) / quad::kFacWarps);
+    quad::k_factor_q<<<fgrid, quad::kFacWarps * 32, fsmem, st>>>(d, stats, cmax, lis, flags);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   if (d.P <= 32) {
     if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
         cudaSuccess)
       return e;
-    quad::k_fwd_chunk_q<1><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, ops, wm);
+    quad::k_fwd_chunk_q<1><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, lis, ops, wm);
   } else {
     if ((e = cudaFuncSetAttribute(quad::k_fwd_chunk_q<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
         cudaSuccess)
       return e;
-    quad::k_fwd_chunk_q<2><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, flags, ops, wm);
+    quad::k_fwd_chunk_q<2><<<(unsigned)n, quad::kThreads4, smem, st>>>(d, gamma, stats, cmax, invs, lis, ops, wm);
   }
   return cudaGetLastError();
 }
