@@ -123,8 +123,9 @@ struct SavedLayout {
                     //                      1 TMA wait expired, 2 MMA wait expired
   size_t wm;        // bf16 hi, lo planes [B][H][C][2][r/8][P][8]: W / m as the
                     //   tensor-core operand of the readout products
-  size_t lis;       // float [B][H][C][3][32][32] (32 < r <= 64): Li's non-zero 32 x 32
-                    //   tiles from the factor kernel, for the four-warp operator kernel
+  size_t lis;       // the factor kernels' Li, for the operator kernels: r <= 32,
+                    //   float [B][H][C][32][32] (Li^T, kept-operator layout); 32 < r <= 64,
+                    //   float [B][H][C][3][32][32] (Li's non-zero 32 x 32 tiles)
   size_t fwd;       // bytes a forward needs when no backward reads its buffer
   size_t ops;       // float [B][H][C][ops_floats_per_chunk(r, P)]: Li = L^{-1}, A, A^K,
                     //   U = A^K Li, V = Li^T U, S = Li^T Li, written by bf16 forwards
@@ -156,7 +157,8 @@ __host__ __device__ inline SavedLayout saved_layout(long long B, long long H, lo
   L.flags = off; off = align256(off + n * sizeof(int));
   L.status = off; off = align256(off + n * sizeof(int));
   L.wm = off;    off = align256(off + (r <= 64 ? n * (size_t)P * r * 4 : 0));
-  L.lis = off;   off = align256(off + (r > 32 && ops_floats_per_chunk(r, P) ? n * (size_t)3 * 1024 * 4 : 0));
+  L.lis = off;
+  off = align256(off + (r <= 32 ? n * (size_t)1024 * 4 : ops_floats_per_chunk(r, P) ? n * (size_t)3 * 1024 * 4 : 0));
   L.fwd = off;
   L.ops = off;   off = align256(off + n * ops_floats_per_chunk(r, P) * sizeof(float));
   L.total = off;

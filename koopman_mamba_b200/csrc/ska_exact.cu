@@ -1155,7 +1155,8 @@ template bool tc_stats_path<__nv_bfloat16>(const Dims&, const In&, const In&);
 
 bool ops_tc_ok(const Dims& d);
 cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                              float* invs, int* flags, float* ops, unsigned char* wm, int* status, cudaStream_t st);
+                              float* invs, int* flags, float* lit, float* ops, unsigned char* wm, int* status,
+                              cudaStream_t st);
 cudaError_t launch_fwd_chunk_q(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
                                float* invs, int* flags, float* lis, float* ops, unsigned char* wm, cudaStream_t st);
 
@@ -1218,7 +1219,8 @@ cudaError_t launch_fwd(const Dims& d, const In& z, const In& zq, const In& v, co
     unsigned char* wm = keep ? reinterpret_cast<unsigned char*>(saved + L.wm) : nullptr;
     tc_read = fwd_tc_readout<IO>(d, zq, y);
     if (keep && tc_read && ops_tc_ok(d)) {   // four chunks per CTA on tcgen05
-      e = launch_fwd_ops_tc(d, gamma, stats, cmax, invs, flags, ops, wm, reinterpret_cast<int*>(saved + L.status),
+      e = launch_fwd_ops_tc(d, gamma, stats, cmax, invs, flags, reinterpret_cast<float*>(saved + L.lis), ops, wm,
+                            reinterpret_cast<int*>(saved + L.status),
                             st);
     } else {
       const Out ychunk = tc_read ? Out{nullptr, 0, 0, 0} : y;

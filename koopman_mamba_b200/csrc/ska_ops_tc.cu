@@ -281,6 +281,23 @@ __device__ __forceinline__ void ld_op_row(float (&v)[32], const float* src, int 
   }
 }
 
+// the same, issued now and finished later
+__device__ __forceinline__ void row_issue_op(RowLd& L, const float* src, int lane) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) L.x[k] = __ldg(s4 + k * 32 + lane);
+}
+__device__ __forceinline__ void row_finish_op(float (&v)[32], RowLd& L) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    touch(L.x[k]);
+    v[4 * k] = L.x[k].x;
+    v[4 * k + 1] = L.x[k].y;
+    v[4 * k + 2] = L.x[k].z;
+    v[4 * k + 3] = L.x[k].w;
+  }
+}
+
 // Columns of a 32 x 32 matrix whose row `lane` the lanes hold, through a warp's
 // own fp32 tile in shared memory: rows 0-15 at lo16, rows 16-31 at hi16 (two
 // 2 KB pieces), 16-byte chunks XOR-swizzled by row so that the row writes and
@@ -371,10 +388,38 @@ static cudaError_t persistent_grid(const void* fn, size_t smem, int per_sm, long
 }
 
 // ---------------------------------------------------------------------------
+// k_factor32: the Cholesky + inverse of every chunk's Gram matrix (r <= 32), one
+// warp per chunk, ahead of the operator kernel: there each warp factored its own
+// chunk in registers (~11K cycles of a group) before the group's first product.
+// Here the factorisations of many chunks run at once with next to no shared
+// memory.  Writes Li^T in the kept-operator layout (store_op) and the jitter
+// flags (ska.py:140-145).  R16: r <= 16, 16 steps.
+// ---------------------------------------------------------------------------
+constexpr int kFac32Warps = 4;
+
+template <bool R16>
+__global__ void __launch_bounds__(kFac32Warps * 32, 3) k_factor32(Dims d, const float* __restrict__ stats,
+                                                              const unsigned long long* __restrict__ cmax,
+                                                              float* __restrict__ lit, int* __restrict__ flags_out) {
+  __shared__ __align__(16) float cb[kFac32Warps][32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long q = (long long)blockIdx.x * kFac32Warps + w;
+  if (q >= (long long)d.B * d.H * d.C) return;   // warp-uniform; no block barriers
+  const ChunkId id = wpc::chunk_id(d, q);
+  const float m = wpc::series_norm(cmax, id, d.C, lane), im = 1.f / m;
+  float x[32];
+  const int flag = factor_invert_rows<R16>(d, stats + q * d.SW, lane, im * im, x, cb[w]);
+  if (lane == 0) flags_out[q] = flag;
+  store_op(lit + q * (long long)kOpFloats, x, lane);
+}
+
+// ---------------------------------------------------------------------------
 // forward.  Persistent: CTA b takes the chunk groups b, b + gridDim.x, ... and
-// starts the next group's record on its way to L2 when it begins a group.  R16:
-// the r <= 16 instance (a shorter factorisation; its own code, so that the r = 32
-// instance keeps its straight-line Cholesky).
+// starts the next group's record on its way to L2 when it begins a group.  The
+// chunks' Li^T rows come from k_factor32, except in the r <= 16 instance (R16),
+// which factors its chunks itself (16 steps; a separate kernel cost more there
+// than it saved: config 5's layer 0.332 -> 0.342 ms, against config 2 0.337 ->
+// 0.328 ms).
 // ---------------------------------------------------------------------------
 template <int NPB, bool R16 = false>
 __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const float* __restrict__ gamma_p,
@@ -382,6 +427,7 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
                                                                const unsigned long long* __restrict__ cmax,
                                                                float* __restrict__ invs_out,
                                                                int* __restrict__ flags_out,
+                                                               const float* __restrict__ lit,
                                                                float* __restrict__ ops_out,
                                                                unsigned char* __restrict__ wm_out,
                                                                int* __restrict__ status) {
@@ -421,9 +467,13 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     const long long q0 = gi * 4;
     const bool valid = q0 + w < nq;
     const long long q = valid ? q0 + w : nq - 1;   // a spare warp redoes the last chunk and stores nothing
+    RowLd ll;                                          // Li^T rows (k_factor32)
+    if (!R16) row_issue_op(ll, lit + q * (long long)kOpFloats, lane);
     if (gi + gridDim.x < ngroups) {
-      const long long qn = (gi + gridDim.x) * 4 + w;
-      prefetch_l2(stats + (qn < nq ? qn : nq - 1) * d.SW, d.SW * 4, lane);
+      long long qn = (gi + gridDim.x) * 4 + w;
+      qn = qn < nq ? qn : nq - 1;
+      prefetch_l2(stats + qn * d.SW, d.SW * 4, lane);
+      if (!R16) prefetch_l2(lit + qn * (long long)kOpFloats, kOpFloats * 4, lane);
     }
     bool ok = true;
     const ChunkId id = wpc::chunk_id(d, q);
@@ -437,9 +487,13 @@ __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const flo
     // Li^T rows -> R(Li^T) in S0: the left operand Li^T and the right operand Li
     {
       float x[32];
-      // S2's part of this warp (free until C(S) is written) holds the column broadcasts
-      const int flag = factor_invert_rows<R16>(d, rec, lane, im2, x, reinterpret_cast<float*>(S2 + 2048 * w));
-      if (valid && lane == 0) flags_out[q] = flag;
+      if (R16) {
+        // S2's part of this warp (free until C(S) is written) holds the column broadcasts
+        const int flag = factor_invert_rows<true>(d, rec, lane, im2, x, reinterpret_cast<float*>(S2 + 2048 * w));
+        if (valid && lane == 0) flags_out[q] = flag;
+      } else {
+        row_finish_op(x, ll);
+      }
       if (keep) store_op(opq + kOpLi * kOpFloats, x, lane);
       put_row<false>(S0, w, lane, x);
     }
@@ -916,16 +970,24 @@ bool ops_tc_ok(const Dims& d) { return d.r <= 32 && d.r % 16 == 0 && d.P <= 128;
 // and power_K <= 2 for the backward (its Horner step is one batched pair of products)
 bool bwd_ops_tc_ok(const Dims& d) { return ops_tc_ok(d) && d.K <= 2; }
 
+// lit: room for every chunk's Li^T (32 x 32 fp32)
 cudaError_t launch_fwd_ops_tc(const Dims& d, const float* gamma, const float* stats, const unsigned long long* cmax,
-                              float* invs, int* flags, float* ops, unsigned char* wm, int* status, cudaStream_t st) {
+                              float* invs, int* flags, float* lit, float* ops, unsigned char* wm, int* status,
+                              cudaStream_t st) {
   const long long nq = (long long)d.B * d.H * d.C;
   if (nq == 0) return cudaSuccess;
+  const bool r16 = d.r <= 16;   // factored inside the operator kernel
+  if (!r16) {
+    const unsigned fgrid = (unsigned)((nq + otc::kFac32Warps - 1) / otc::kFac32Warps);
+    otc::k_factor32<false><<<fgrid, otc::kFac32Warps * 32, 0, st>>>(d, stats, cmax, lit, flags);
+    const cudaError_t e0 = cudaGetLastError();
+    if (e0 != cudaSuccess) return e0;
+  }
   const int npb = otc::ops_npb(d.P);
   const size_t smem = (size_t)otc::ops_slots(npb) * otc::kSlot;
   Dims dd = d;
-  void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags, (void*)&ops,
+  void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&flags, (void*)&lit, (void*)&ops,
                   (void*)&wm, (void*)&status};
-  const bool r16 = d.r <= 16;
   const void* fn = npb == 1 ? (r16 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<1, true>)
                                    : reinterpret_cast<const void*>(otc::k_fwd_ops_tc<1>))
                    : npb == 2 ? (r16 ? reinterpret_cast<const void*>(otc::k_fwd_ops_tc<2, true>)
