@@ -197,6 +197,16 @@ __global__ void __launch_bounds__(kFacWarps * 32, 2) k_factor_q(Dims d, const fl
 
 // tile t of a 64 x 64 region -> the same tile of a kept operator in global memory
 // (verbatim: the backward copies it back as it is), 16 bytes per lane and step
+// The backward operator kernel's products: bf16 hi / lo operand halves on the
+// m16n8k16 MMA (wmm2b, ~2^-16 relative, as the tcgen05 chunk products; half the
+// MMAs of the TF32 split: k_bwd_chunk_q 0.925 -> 0.874 ms at the r = 48 layer).
+// The forward keeps the TF32 split (wmmp): there the MMAs are not what limits it
+// (no change with wmm2b).
+template <int M, int K, bool TA, bool TB, bool ACC>
+__device__ __forceinline__ void qmm(float* C, const float* A, int SA, const float* B, float alpha, int kn = K) {
+  wmm2b<M, K, TA, TB, ACC>(C, A, SA, B, alpha, kn);
+}
+
 __device__ __forceinline__ void keep_tile(float* dst, const float* M, int t, int lane) {
   const float4* s = reinterpret_cast<const float4*>(M + t * kTile);
   float4* g = reinterpret_cast<float4*>(dst + t * kTile);
@@ -513,13 +523,13 @@ __device__ __forceinline__ void store_block(float* dst, int ld, const float* T, 
 template <bool ACC>
 __device__ __forceinline__ void mm_nn(float* out, const float* X, const float* Y, int bi, int bj, float alpha,
                                       int kn) {
-  wmmp<false, 32, 64, false, false, ACC>(blk(out, bi, bj), blk(const_cast<float*>(X), bi, 0), 2 * kTile,
+  qmm<32, 64, false, false, ACC>(blk(out, bi, bj), blk(const_cast<float*>(X), bi, 0), 2 * kTile,
                                          Y + bj * 2 * kTile, alpha, kn);   // X Y
 }
 template <bool ACC>
 __device__ __forceinline__ void mm_tn(float* out, const float* X, const float* Y, int bi, int bj, float alpha,
                                       int kn) {
-  wmmp<false, 32, 64, true, false, ACC>(blk(out, bi, bj), X + bi * 2 * kTile, kTile, Y + bj * 2 * kTile,
+  qmm<32, 64, true, false, ACC>(blk(out, bi, bj), X + bi * 2 * kTile, kTile, Y + bj * 2 * kTile,
                                         alpha, kn);                        // X^T Y
 }
 template <bool ACC>
@@ -527,10 +537,10 @@ __device__ __forceinline__ void mm_nt(float* out, const float* X, const float* Y
                                       int kn) {
   float* Xm = const_cast<float*>(X);
   float* Ym = const_cast<float*>(Y);
-  wmmp<false, 32, 32, false, true, ACC>(blk(out, bi, bj), blk(Xm, bi, 0), kTile, blk(Ym, bj, 0), alpha,
+  qmm<32, 32, false, true, ACC>(blk(out, bi, bj), blk(Xm, bi, 0), kTile, blk(Ym, bj, 0), alpha,
                                         min(kn, 32));   // X Y^T
   if (kn > 32)
-    wmmp<false, 32, 32, false, true, true>(blk(out, bi, bj), blk(Xm, bi, 1), kTile, blk(Ym, bj, 1), alpha, kn - 32);
+    qmm<32, 32, false, true, true>(blk(out, bi, bj), blk(Xm, bi, 1), kTile, blk(Ym, bj, 1), alpha, kn - 32);
 }
 
 // tril of block (bi, bj) of a 64 x 64 matrix, in place, by the warp that owns it

@@ -608,6 +608,104 @@ __device__ __noinline__ void wmm2(float* __restrict__ C, const float* __restrict
   }
 }
 
+// wmm2 with bf16 operand halves on the m16n8k16 MMA: x = hi + lo with hi = bf16(x)
+// and lo = bf16(x - hi) (~2^-16 relative, the precision of the tcgen05 chunk
+// products), a*b ~= hi_a hi_b + hi_a lo_b + lo_a hi_b.  Half the MMAs of the TF32
+// split for the same K (16 per instruction instead of 8); for the bf16-only chunk
+// kernels.  Same operand forms, tile layout and alpha / ACC semantics as wmm2; kn
+// is rounded up to a multiple of 16 (the extra terms are the zero padding).
+__device__ __forceinline__ void mma_bf16_acc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x0, x1) -> bf16 pairs hi (x0 in the low half) and lo = the remainders
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int M, int K, bool TA, bool TB, bool ACC>
+__device__ __noinline__ void wmm2b(float* __restrict__ C, const float* __restrict__ A, int SA,
+                                   const float* __restrict__ B, float alpha, int kn = K) {
+  static_assert(M % 32 == 0 && K % 16 == 0, "tile shape");
+  static_assert(!TB || K <= 32, "transposed B holds 32 x K");
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int kr = (kn + 15) & ~15;
+  // op(A)(i, k) and op(B)(k, j) as in wmm2
+  const auto opA = [&](int i, int k) -> float {
+    return TA ? A[(i >> 5) * SA + swz(k, i & 31)] : A[(k >> 5) * SA + swz(i, k & 31)];
+  };
+  const auto opB = [&](int k, int j) -> float { return TB ? B[swz(j, k)] : B[swz(k, j)]; };
+#pragma unroll 1
+  for (int i0 = 0; i0 < M; i0 += 32) {
+    float d[2][4][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int n = 0; n < 4; ++n) d[h][n][0] = d[h][n][1] = d[h][n][2] = d[h][n][3] = 0.f;
+#pragma unroll 1
+    for (int k0 = 0; k0 < kr; k0 += 16) {
+      sched_fence();
+      const int c0 = k0 + 2 * t4;
+      uint32_t ah[2][4], al[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ra = i0 + 16 * h + g, rb = ra + 8;
+        split_bf16x2(opA(ra, c0), opA(ra, c0 + 1), ah[h][0], al[h][0]);
+        split_bf16x2(opA(rb, c0), opA(rb, c0 + 1), ah[h][1], al[h][1]);
+        split_bf16x2(opA(ra, c0 + 8), opA(ra, c0 + 9), ah[h][2], al[h][2]);
+        split_bf16x2(opA(rb, c0 + 8), opA(rb, c0 + 9), ah[h][3], al[h][3]);
+      }
+      uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int j = n * 8 + g;
+        split_bf16x2(opB(c0, j), opB(c0 + 1, j), bh[n][0], bl[n][0]);
+        split_bf16x2(opB(c0 + 8, j), opB(c0 + 9, j), bh[n][1], bl[n][1]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) mma_bf16_acc(d[h][n], al[h], bh[n][0], bh[n][1]);
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) mma_bf16_acc(d[h][n], ah[h], bl[n][0], bl[n][1]);
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) mma_bf16_acc(d[h][n], ah[h], bh[n][0], bh[n][1]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int ra = i0 + 16 * h + g, rb = ra + 8;
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int cw = ((((2 * n + (t4 >> 1)) ^ g) << 2) | ((2 * t4) & 3));
+        float* c0p = C + ra * 32 + cw;
+        float* c1p = C + rb * 32 + cw;
+        if (ACC) {
+          c0p[0] += alpha * d[h][n][0];
+          c0p[1] += alpha * d[h][n][1];
+          c1p[0] += alpha * d[h][n][2];
+          c1p[1] += alpha * d[h][n][3];
+        } else {
+          c0p[0] = alpha * d[h][n][0];
+          c0p[1] = alpha * d[h][n][1];
+          c1p[0] = alpha * d[h][n][2];
+          c1p[1] = alpha * d[h][n][3];
+        }
+      }
+    }
+  }
+}
+
 // Product of two fp32 tiles:
 //   FAST = false: 3-term split, fp32-level products (what the kernels use);
 //   FAST = true:  one TF32 product of round-to-nearest operands, ~2^-11 relative
