@@ -709,6 +709,11 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
   unsigned char* Wt = smem + 3 * kSlot;
   const uint32_t aX = tc::smem_u32(X), aY = aX + kSlot, aZ = aX + 2 * kSlot, aW = aX + 3 * kSlot;
   float* stg = reinterpret_cast<float*>(smem + (size_t)kBwdSlots * kSlot + (size_t)w * kStageBytes);
+  // this warp's two fp32 tiles for record blocks (C and dW' blocks, then M, then G):
+  // cp.async copies of whole 32 x 32 blocks (coalesced; row `lane` loads would touch
+  // 32 lines per instruction), read back a row per lane without bank conflicts
+  float* TC = reinterpret_cast<float*>(smem + (size_t)kBwdSlots * kSlot + 4 * kStageBytes + (size_t)w * 8192);
+  float* TW = TC + 1024;
 
   if (w == 0) tc::tmem_alloc(&tmem_slot, kBwdCols);
   if (tid == 0) {
@@ -736,9 +741,11 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     const float* dwq = dwraw + q * (long long)P * r;
     const float* crec = rec + 2 * r * r;
     float* drec = dstats + q * d.SW;
-    RowLd cl, dl;                                       // block 0's C and dW' rows
-    row_issue(cl, crec, lane, P, r);
-    row_issue(dl, dwq, lane, P, r);
+    // block 0's C and dW' rows (the tiles' last reader was this warp: sync first)
+    __syncwarp();
+    wpc::cp_tile_async(TC, crec, P < 32 ? P : 32, r, lane);
+    wpc::cp_tile_async(TW, dwq, P < 32 ? P : 32, r, lane);
+    wpc::cp_async_commit();
     if (gi + gridDim.x < ngroups) {   // what the next group's first step reads: V, the C rows, dW'
       long long qn = (gi + gridDim.x) * 4 + w;
       qn = qn < nq ? qn : nq - 1;
@@ -758,8 +765,10 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     put_row<false>(Wt, w, lane, t);                     // R(V): the right operand V^T
 #pragma unroll 1
     for (int pb = 0; pb < npb; ++pb) {
-      row_finish(a1, cl, 32 * pb + lane < P, 1.f);      // C rows (raw)
-      row_finish(a2, dl, 32 * pb + lane < P, 1.f);      // dW' rows
+      wpc::cp_async_wait<0>();
+      __syncwarp();
+      wpc::ld_row(a1, TC, lane);                         // C rows (raw; zero past P)
+      wpc::ld_row(a2, TW, lane);                         // dW' rows
 #pragma unroll
       for (int j = 0; j < 32; ++j) t[j] = a1[j] * im2;
       put_row<true>(X, w, lane, t);                     // C(C_pb / m^2): the left operand C_pb^T / m^2
@@ -775,8 +784,10 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
         tc::mma_commit(&bar2);
       }
       if (pb + 1 < npb) {
-        row_issue(cl, crec + (pb + 1) * 32 * r, lane, P - 32 * (pb + 1), r);
-        row_issue(dl, dwq + (pb + 1) * 32 * r, lane, P - 32 * (pb + 1), r);
+        const int nr = P - 32 * (pb + 1) < 32 ? P - 32 * (pb + 1) : 32;
+        wpc::cp_tile_async(TC, crec + (pb + 1) * 32 * r, nr, r, lane);   // read before the block barrier
+        wpc::cp_tile_async(TW, dwq + (pb + 1) * 32 * r, nr, r, lane);
+        wpc::cp_async_commit();
       } else {
         ld_op_row(a2, opq + kOpLi * kOpFloats, lane);   // for the next step: Li^T
         ld_op_row(u, opq + kOpU * kOpFloats, lane);     //   and U
@@ -828,8 +839,8 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
       tc::mma_commit(&bar2);
     }
     ld_op_row(a1, opq + kOpS * kOpFloats, lane);        // for the step after: S
-    RowLd ml;
-    row_issue(ml, rec + r * r, lane, r, r);             //   and M
+    wpc::cp_tile_async(TC, rec + r * r, r, r, lane);    //   and M (TC was last read before a block barrier)
+    wpc::cp_async_commit();
     ok &= product_wait(&bar, phase, d.wlim);
     ok &= product_wait(&bar2, phase2, d.wlim);
     tc::tmem_ld32(R0 + mine, t);                        // dAK
@@ -858,7 +869,11 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     // ---- dMn = kk dA S (R0), dS + dS^T = kk (Mn^T dA + dA^T Mn) (R1) ----
     touch32(a1);
     put_row<true>(X, w, lane, a1);                      // C(S)
-    row_finish(a2, ml, lane < r, im2);                  // Mn rows
+    wpc::cp_async_wait<0>();
+    __syncwarp();
+    wpc::ld_row(a2, TC, lane);                          // Mn rows
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a2[j] *= im2;
     put_row<true>(Y, w, lane, a2);                      // C(Mn): the left operand Mn^T, the right operand Mn
     put_row_rc(Z, Wt, w, lane, t);                      // R(dA); C(dA): the left operand dA^T, the right operand dA
     operands_ready();
@@ -893,8 +908,8 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
       mma3(R0, aY, true, aX, true, 128, false);
       tc::mma_commit(&bar);
     }
-    RowLd gl;
-    row_issue(gl, rec, lane, r, r);                     // for the end: G rows
+    wpc::cp_tile_async(TW, rec, r, r, lane);            // for the end: G
+    wpc::cp_async_commit();
     ok &= product_wait(&bar, phase, d.wlim);
     tc::tmem_ld32(R0 + mine, t);
 #pragma unroll
@@ -907,7 +922,6 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
       mma3(R0, aX, false, aY, true, 128, false);
       tc::mma_commit(&bar);
     }
-    ld_gmem_col(a1, rec, lane, r);                      // for the end: G columns
     ok &= product_wait(&bar, phase, d.wlim);
     tc::tmem_ld32(R0 + mine, t);
     // P' = (L'' + L''^T) / 2 with L'' = tril(Pm), its diagonal halved
@@ -937,7 +951,10 @@ __global__ void __launch_bounds__(kOpsThreads, 2) k_bwd_ops_tc(Dims d, const flo
     }
     ok &= product_wait(&bar, phase, d.wlim);
     tc::tmem_ld32(R0 + mine, t);
-    row_finish(a2, gl, lane < r, 1.f);
+    wpc::cp_async_wait<0>();
+    __syncwarp();
+    wpc::ld_row(a2, TW, lane);                          // G rows and columns (zero past r)
+    wpc::ld_col<32>(a1, TW, lane);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       t[j] *= 0.5f;
@@ -1007,7 +1024,7 @@ cudaError_t launch_bwd_ops_tc(const Dims& d, const float* gamma, const float* st
                               float* dgpart, int* status, cudaStream_t st) {
   const long long nq = (long long)d.B * d.H * d.C;
   if (nq == 0) return cudaSuccess;
-  const size_t smem = (size_t)otc::kBwdSlots * otc::kSlot + 4 * otc::kStageBytes;
+  const size_t smem = (size_t)otc::kBwdSlots * otc::kSlot + 4 * otc::kStageBytes + 4 * 8192;
   Dims dd = d;
   void* args[] = {&dd, (void*)&gamma, (void*)&stats, (void*)&cmax, (void*)&invs, (void*)&ops, (void*)&dwraw,
                   (void*)&dstats, (void*)&dmpart, (void*)&dgpart, (void*)&status};
