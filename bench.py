@@ -92,7 +92,7 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "lm"), default="c2",
-                    help="c2 (default, with a c3 block), c3, or lm (the full-model training step of config 4)")
+                    help="c2 (default, with a c3 block), c3, c4, c5, or lm (the 50M hybrid model's training step)")
     ap.add_argument("--no-c3", action="store_true", help="skip the c3 block of the default c2 run")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -667,7 +667,7 @@ def measure(key, args, rank, world, local, dev, barrier, max_over_ranks):
 
 
 def measure_lm(args, rank, world, local, dev, barrier, max_over_ranks):
-    """Config 4: the whole language model's training step (forward, backward with the
+    """The 50M hybrid Mamba-2 + SKA model's training step (forward, backward with the
     DDP all-reduce over NCCL, AdamW) on synthetic token ids (uniform over the
     vocabulary, seed 3 + 1000 * rank).  The Mamba-2 layers are the package's
     PyTorch stand-in unless mamba_ssm is importable."""
@@ -730,7 +730,7 @@ def measure_lm(args, rank, world, local, dev, barrier, max_over_ranks):
     torch.cuda.synchronize()
     e_ms = max_over_ranks(ea.elapsed_time(eb), dev)
     return {
-        "metric": "hybrid Mamba-2 + SKA LM training tokens/s (config 4)", "value": tokens * args.steps / (dev_ms / 1e3),
+        "metric": "hybrid Mamba-2 + SKA LM training tokens/s (50M model, batch 32 x 2048)", "value": tokens * args.steps / (dev_ms / 1e3),
         "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform token ids, seed 3 + 1000*rank)",

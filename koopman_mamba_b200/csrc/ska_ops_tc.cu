@@ -151,8 +151,9 @@ __device__ __forceinline__ void store_op(float* dst, const float (&v)[32], int l
 // The backward's record rows (lane = row, 128-byte rows: each warp store
 // instruction would touch 32 lines) go out as one bulk copy per block from a 4 KB
 // staging buffer per warp, off the load/store path the operand loads use (the
-// backward kernel 115.4 -> 112.7 us at config 2; the forward's kept operators are
-// already stored 512 contiguous bytes per instruction and stay plain stores).
+// backward kernel 115.4 -> 112.7 us at B=8, H=12, L=2048, r=32, P=64; the
+// forward's kept operators are already stored 512 contiguous bytes per
+// instruction and stay plain stores).
 // Lane 0 issues every bulk copy of its warp and, before the buffer is rewritten,
 // waits until the previous one has read it.  Call with the whole warp.
 constexpr uint32_t kStageBytes = 4096;
@@ -418,8 +419,8 @@ __global__ void __launch_bounds__(kFac32Warps * 32, 3) k_factor32(Dims d, const 
 // starts the next group's record on its way to L2 when it begins a group.  The
 // chunks' Li^T rows come from k_factor32, except in the r <= 16 instance (R16),
 // which factors its chunks itself (16 steps; a separate kernel cost more there
-// than it saved: config 5's layer 0.332 -> 0.342 ms, against config 2 0.337 ->
-// 0.328 ms).
+// than it saved: at B=256, H=4, L=1024, r=16, P=32 the forward went 0.332 -> 0.342
+// ms, against 0.337 -> 0.328 ms fwd+bwd at B=8, H=12, L=2048, r=32, P=64).
 // ---------------------------------------------------------------------------
 template <int NPB, bool R16 = false>
 __global__ void __launch_bounds__(kOpsThreads, 3) k_fwd_ops_tc(Dims d, const float* __restrict__ gamma_p,

@@ -177,7 +177,7 @@ __device__ __forceinline__ bool chol_inv32(float (&g)[32], float (&x)[32], int l
 // skipped; rows and columns past n must hold the identity padding, which those
 // steps would leave unchanged (a template switch, so that the full-size factor
 // keeps its straight-line code: a run-time test in it, or a second trimmed copy
-// beside it, slowed the r = 32 operator kernel by 2-11 us at config 2).
+// beside it, slowed the r = 32 operator kernel by 2-11 us at B=8, H=12, L=2048).
 template <bool TRIM = false>
 __device__ __forceinline__ bool chol_inv32_bc(float (&g)[32], float (&x)[32], float* cb, int lane, int n = 32) {
 #pragma unroll
@@ -709,8 +709,8 @@ __device__ __noinline__ void wmm2b(float* __restrict__ C, const float* __restric
 // Product of two fp32 tiles:
 //   FAST = false: 3-term split, fp32-level products (what the kernels use);
 //   FAST = true:  one TF32 product of round-to-nearest operands, ~2^-11 relative
-//     per product.  Through the chunk algebra that is ~1.5e-3 at config-2
-//     numerics, but with power_K = 3 and 32-token chunks the backward reached the
+//     per product.  Through the chunk algebra that is ~1.5e-3 at B=8, H=12,
+//     L=2048, r=32 numerics, but with power_K = 3 and 32-token chunks the backward reached the
 //     2e-2 bf16 bar, so it is not used.
 template <bool FAST, int M, int K, bool TA, bool TB, bool ACC>
 __device__ __forceinline__ void wmmp(float* C, const float* A, int SA, const float* B, float alpha, int kn = K) {
