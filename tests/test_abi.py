@@ -67,6 +67,10 @@ def test_forward_workspace_is_the_leading_part(built_lib, r, P, op_floats):
     n = 8 * 12 * 32
     assert fwd % 256 == 0 and fwd >= n * (2 * r * r + P * r) * 4
     assert saved - fwd == -(-(n * op_floats * 4) // 256) * 256
+    # the factor kernels' Li (r <= 32: Li^T, 4 KB per chunk; the four-warp shapes:
+    # three 4 KB tiles) is part of the forward's share, with the W/m planes
+    lis = 1024 if r <= 32 else (3 * 1024 if op_floats else 0)
+    assert fwd >= n * (2 * r * r + P * r + P * r + lis) * 4
 
 
 @pytest.mark.parametrize("kw,code", [
